@@ -1,0 +1,466 @@
+// fo_api.cu -- the extern "C" boundary of libb200fo.so (declared in include/b200fo.h):
+// argument validation, TMA tensor-map encoding, config legality, kernel selection and
+// the device status word.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/b200fo.h"
+#include "fo_launch.cuh"
+
+namespace {
+
+thread_local std::string g_err;
+thread_local int g_err_code = 0;
+std::atomic<uint64_t> g_launches{0};
+std::atomic<uint64_t> g_timeout_ns{2000000000ull};
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  g_err_code = code;
+  return code;
+}
+
+int ok() {
+  g_err.clear();
+  g_err_code = 0;
+  return FO_OK;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+constexpr int kMaxDevices = 64;
+std::mutex g_dev_mu;
+int* g_status[kMaxDevices] = {nullptr};
+int g_sms[kMaxDevices] = {0};
+
+struct DevInfo {
+  int dev;
+  int sms;
+  int* status;
+};
+
+int device_info(DevInfo* out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return fail(FO_ENODEVICE, "no current CUDA device");
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (g_status[dev] == nullptr) {
+    int major = 0, sms = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (major != 10)
+      return fail(FO_ENODEVICE, "device %d has compute capability %d.x; this library is built for sm_100a",
+                  dev, major);
+    int* st = nullptr;
+    if (cudaMalloc(&st, 4 * sizeof(int)) != cudaSuccess)
+      return fail(FO_ECUDA, "cudaMalloc of the device status word failed");
+    cudaMemset(st, 0, 4 * sizeof(int));
+    cudaDeviceSynchronize();
+    g_status[dev] = st;
+    g_sms[dev] = sms;
+  }
+  out->dev = dev;
+  out->sms = g_sms[dev];
+  out->status = g_status[dev];
+  return FO_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+int esize(int dt) { return dt == FO_DT_F32 ? 4 : 2; }
+bool valid_dt(int dt) { return dt == FO_DT_F16 || dt == FO_DT_BF16 || dt == FO_DT_F32; }
+
+CUtensorMapDataType tma_dt(int dt) {
+  switch (dt) {
+    case FO_DT_F16: return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    case FO_DT_BF16: return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    default: return CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  }
+}
+
+// 2-D row-major tensor [outer, inner] with row stride `row_bytes`, 128-byte swizzled
+// boxes of box_inner x box_outer elements.  Out-of-range elements load as zero and are
+// skipped by stores.
+int make_tmap(CUtensorMap* m, int dt, const void* base, uint64_t inner, uint64_t outer,
+              uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, const char* what) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return fail(FO_ECUDA, "cuTensorMapEncodeTiled is unavailable in the driver");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, tma_dt(dt), 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(FO_EINVAL, "tensor map for %s rejected by the driver (CUresult %d; dims %llu x %llu, row %llu B)",
+                what, static_cast<int>(r), static_cast<unsigned long long>(outer),
+                static_cast<unsigned long long>(inner), static_cast<unsigned long long>(row_bytes));
+  return FO_OK;
+}
+
+int check_cfg(int op, int out_dtype, const FoTileCfg* cfg, char* why, size_t why_len) {
+  auto say = [&](const char* fmt, int v) {
+    if (why != nullptr && why_len > 0) snprintf(why, why_len, fmt, v);
+    return FO_EINVAL;
+  };
+  if (cfg == nullptr) return say("null config%d", 0);
+  if (cfg->block_m != 128) return say("block_m must be 128 (tcgen05 M with cta_group::1), got %d", cfg->block_m);
+  if (cfg->block_n != 64 && cfg->block_n != 128 && cfg->block_n != 256)
+    return say("block_n must be 64, 128 or 256, got %d", cfg->block_n);
+  if (cfg->block_k != 64) return say("block_k must be 64 (one 128-byte swizzle row), got %d", cfg->block_k);
+  const int min_stages = op == 1 ? 3 : 2;
+  if (cfg->stages < min_stages || cfg->stages > fo::kMaxStages)
+    return say("stages out of range: %d", cfg->stages);
+  if (cfg->group_m < 0) return say("group_m must be >= 0, got %d", cfg->group_m);
+  if (cfg->max_ctas < 0) return say("max_ctas must be >= 0, got %d", cfg->max_ctas);
+  const int smem = fo::smem_bytes_for(cfg->block_n, cfg->stages);
+  if (smem > 232448) return say("shared memory %d B exceeds the 227 KB per-block limit", smem);
+  // TMEM: two fp32 accumulators of block_n columns each, <= 512 columns.
+  if (2 * cfg->block_n > 512) return say("TMEM columns %d exceed 512", 2 * cfg->block_n);
+  if (out_dtype < 0 || out_dtype > 2) return say("bad output dtype %d", out_dtype);
+  return FO_OK;
+}
+
+int act_of(int epi, int* has_bias) {
+  switch (epi) {
+    case FO_EPI_NONE: *has_bias = 0; return fo::ACT_NONE;
+    case FO_EPI_BIAS: *has_bias = 1; return fo::ACT_NONE;
+    case FO_EPI_BIAS_RELU: *has_bias = 1; return fo::ACT_RELU;
+    case FO_EPI_BIAS_GELU_TANH: *has_bias = 1; return fo::ACT_GELU_TANH;
+    case FO_EPI_BIAS_GELU_ERF: *has_bias = 1; return fo::ACT_GELU_ERF;
+    case FO_EPI_BIAS_LN: *has_bias = 1; return fo::ACT_NONE;
+    case FO_EPI_RELU: *has_bias = 0; return fo::ACT_RELU;
+  }
+  return -1;
+}
+
+size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+size_t ln_workspace(int64_t M, int64_t N, int bn) {
+  const int64_t tiles_m = (M + 127) / 128;
+  const int64_t tiles_n = (N + bn - 1) / bn;
+  return round_up(static_cast<size_t>(tiles_m) * 4, 256) + static_cast<size_t>(tiles_n * M) * 8;
+}
+
+void fill_common(fo::KParams& p, const DevInfo& di) {
+  p.status = di.status;
+  p.timeout_ns = g_timeout_ns.load();
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* fo_version(void) { return "b200fo 0.1.0 sm_100a abi 1"; }
+
+uint64_t fo_launch_count(void) { return g_launches.load(); }
+
+int fo_last_error(char* buf, size_t len) {
+  if (buf != nullptr && len > 0) {
+    strncpy(buf, g_err.c_str(), len - 1);
+    buf[len - 1] = '\0';
+  }
+  return g_err_code;
+}
+
+int fo_set_wait_timeout_ns(uint64_t ns) {
+  if (ns == 0) return fail(FO_EINVAL, "timeout must be > 0 ns");
+  g_timeout_ns.store(ns);
+  return ok();
+}
+
+size_t fo_config_smem_bytes(int32_t op, int32_t out_dtype, const FoTileCfg* cfg) {
+  if (check_cfg(op, out_dtype, cfg, nullptr, 0) != FO_OK) return 0;
+  return static_cast<size_t>(fo::smem_bytes_for(cfg->block_n, cfg->stages));
+}
+
+int fo_query_config_legal(int32_t op, int32_t out_dtype, const FoTileCfg* cfg, char* why,
+                          size_t why_len) {
+  if (why != nullptr && why_len > 0) why[0] = '\0';
+  if (op != 0 && op != 1) {
+    if (why != nullptr && why_len > 0) snprintf(why, why_len, "op must be 0 (gemm) or 1 (conv2d)");
+    return FO_EINVAL;
+  }
+  return check_cfg(op, out_dtype, cfg, why, why_len);
+}
+
+size_t fo_gemm_workspace_size(const FoGemmDesc* d, const FoTileCfg* cfg) {
+  if (d == nullptr || cfg == nullptr || d->epilogue != FO_EPI_BIAS_LN) return 0;
+  if (cfg->block_n != 64 && cfg->block_n != 128 && cfg->block_n != 256) return 0;
+  if (d->M <= 0 || d->N <= 0) return 0;
+  return ln_workspace(d->M, d->N, cfg->block_n);
+}
+
+int fo_gemm(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
+  if (d == nullptr) return fail(FO_EINVAL, "null descriptor");
+  char why[256];
+  if (check_cfg(0, d->out_dtype, cfg, why, sizeof(why)) != FO_OK) return fail(FO_EINVAL, "config: %s", why);
+  if (d->M < 0 || d->N < 0 || d->K < 0) return fail(FO_EINVAL, "negative shape M=%lld N=%lld K=%lld",
+                                                    (long long)d->M, (long long)d->N, (long long)d->K);
+  if (d->M > (1ll << 31) - 1 || d->N > (1ll << 31) - 1 || d->K > (1ll << 31) - 1)
+    return fail(FO_EINVAL, "shape exceeds 2^31-1");
+  if (d->in_dtype != FO_DT_F16 && d->in_dtype != FO_DT_BF16)
+    return fail(FO_EINVAL, "in_dtype must be FO_DT_F16 or FO_DT_BF16");
+  if (!valid_dt(d->out_dtype)) return fail(FO_EINVAL, "bad out_dtype %d", d->out_dtype);
+  if (d->b_layout != FO_B_KN && d->b_layout != FO_B_NK) return fail(FO_EINVAL, "bad b_layout %d", d->b_layout);
+  int has_bias = 0;
+  const int act = act_of(d->epilogue, &has_bias);
+  if (act < 0) return fail(FO_EINVAL, "bad epilogue %d", d->epilogue);
+  const bool ln = d->epilogue == FO_EPI_BIAS_LN;
+  if (has_bias && (d->bias == nullptr || !valid_dt(d->vec_dtype)))
+    return fail(FO_EINVAL, "epilogue %d needs a bias vector and a valid vec_dtype", d->epilogue);
+  if (d->M == 0 || d->N == 0) return ok();  // empty output: nothing to launch
+  const int ib = 2, ob = esize(d->out_dtype);
+  if (d->out == nullptr || !aligned16(d->out)) return fail(FO_EINVAL, "out must be a 16-byte aligned device pointer");
+  if (d->ldo < d->N || (d->ldo * ob) % 16 != 0)
+    return fail(FO_EINVAL, "ldo=%lld must be >= N=%lld and a multiple of %d elements (16-byte rows)",
+                (long long)d->ldo, (long long)d->N, 16 / ob);
+  if (d->K > 0) {
+    if (d->a == nullptr || d->b == nullptr || !aligned16(d->a) || !aligned16(d->b))
+      return fail(FO_EINVAL, "a and b must be 16-byte aligned device pointers");
+    if (d->lda < d->K || (d->lda * ib) % 16 != 0)
+      return fail(FO_EINVAL, "lda=%lld must be >= K=%lld and a multiple of 8 elements", (long long)d->lda,
+                  (long long)d->K);
+    const int64_t bmin = d->b_layout == FO_B_KN ? d->N : d->K;
+    if (d->ldb < bmin || (d->ldb * ib) % 16 != 0)
+      return fail(FO_EINVAL, "ldb=%lld must be >= %lld and a multiple of 8 elements", (long long)d->ldb,
+                  (long long)bmin);
+  }
+  if (ln) {
+    if (d->out_dtype == FO_DT_F32) return fail(FO_EINVAL, "LayerNorm output must be f16 or bf16");
+    if (d->gamma == nullptr || d->beta == nullptr) return fail(FO_EINVAL, "LayerNorm needs gamma and beta");
+    if (d->N % 8 != 0) return fail(FO_EINVAL, "LayerNorm needs N %% 8 == 0, got N=%lld", (long long)d->N);
+    const size_t need = ln_workspace(d->M, d->N, cfg->block_n);
+    if (d->workspace == nullptr || d->workspace_bytes < need || !aligned16(d->workspace))
+      return fail(FO_EINVAL, "LayerNorm needs a zero-initialised, 16-byte aligned workspace of %zu bytes", need);
+    if (!(d->eps >= 0.0f)) return fail(FO_EINVAL, "eps must be >= 0");
+  }
+  DevInfo di;
+  if (int rc = device_info(&di)) return rc;
+
+  fo::LaunchArgs la;
+  memset(&la, 0, sizeof(la));
+  fo::KParams& p = la.p;
+  const int bn = cfg->block_n;
+  p.M = static_cast<int>(d->M);
+  p.N = static_cast<int>(d->N);
+  p.K = static_cast<int>(d->K);
+  p.tiles_m = (p.M + 127) / 128;
+  p.tiles_n = (p.N + bn - 1) / bn;
+  p.num_tiles = p.tiles_m * p.tiles_n;
+  p.k_blocks = (p.K + 63) / 64;
+  p.group_m = ln ? 0 : cfg->group_m;
+  p.stages = cfg->stages;
+  p.ab_bf16 = d->in_dtype == FO_DT_BF16;
+  p.b_mn = d->b_layout == FO_B_KN;
+  p.has_bias = has_bias;
+  p.bias = d->bias;
+  p.gamma = d->gamma;
+  p.beta = d->beta;
+  p.vec_dtype = d->vec_dtype;
+  p.eps = d->eps;
+  p.out = d->out;
+  p.ldo = d->ldo;
+  if (ln) {
+    p.ln_counters = static_cast<int*>(d->workspace);
+    p.ln_stats = reinterpret_cast<float2*>(static_cast<char*>(d->workspace) +
+                                           round_up(static_cast<size_t>(p.tiles_m) * 4, 256));
+  }
+  fill_common(p, di);
+
+  if (p.K > 0) {
+    if (int rc = make_tmap(&la.tmA, d->in_dtype, d->a, d->K, d->M, d->lda * ib, 64, 128, "A")) return rc;
+    if (d->b_layout == FO_B_NK) {
+      if (int rc = make_tmap(&la.tmB, d->in_dtype, d->b, d->K, d->N, d->ldb * ib, 64, bn, "B")) return rc;
+    } else {
+      if (int rc = make_tmap(&la.tmB, d->in_dtype, d->b, d->N, d->K, d->ldb * ib, 64, 64, "B")) return rc;
+    }
+  }
+  if (int rc = make_tmap(&la.tmC, d->out_dtype, d->out, d->N, d->M, d->ldo * ob, 128 / ob, 32, "out")) return rc;
+
+  const int cap = cfg->max_ctas > 0 ? cfg->max_ctas : di.sms;
+  la.grid = p.num_tiles < cap ? p.num_tiles : cap;
+  la.smem = fo::smem_bytes_for(bn, cfg->stages);
+  la.stream = static_cast<cudaStream_t>(stream);
+  const int out_dt = d->out_dtype == FO_DT_F16 ? fo::DT_F16 : d->out_dtype == FO_DT_BF16 ? fo::DT_BF16 : fo::DT_F32;
+  cudaError_t e = ln ? fo::launch_ln_family(bn, out_dt, la) : fo::launch_gemm_family(bn, act, out_dt, la);
+  if (e != cudaSuccess) return fail(FO_ECUDA, "kernel launch failed: %s", cudaGetErrorString(e));
+  g_launches.fetch_add(1);
+  return ok();
+}
+
+int fo_conv2d(const FoConvDesc* d, const FoTileCfg* cfg, void* stream) {
+  if (d == nullptr) return fail(FO_EINVAL, "null descriptor");
+  char why[256];
+  if (check_cfg(1, d->out_dtype, cfg, why, sizeof(why)) != FO_OK) return fail(FO_EINVAL, "config: %s", why);
+  if (d->n < 0 || d->h <= 0 || d->w <= 0 || d->c <= 0 || d->f <= 0 || d->kh <= 0 || d->kw <= 0 ||
+      d->stride <= 0 || d->pad < 0 || d->dil <= 0)
+    return fail(FO_EINVAL, "bad conv geometry");
+  if (d->in_dtype != FO_DT_F16 && d->in_dtype != FO_DT_BF16)
+    return fail(FO_EINVAL, "in_dtype must be FO_DT_F16 or FO_DT_BF16");
+  if (!valid_dt(d->out_dtype)) return fail(FO_EINVAL, "bad out_dtype %d", d->out_dtype);
+  int has_bias = 0;
+  const int act = act_of(d->epilogue, &has_bias);
+  if (act != fo::ACT_NONE && act != fo::ACT_RELU)
+    return fail(FO_EINVAL, "conv2d epilogue must be NONE, BIAS, RELU or BIAS_RELU");
+  if (has_bias && (d->bias == nullptr || !valid_dt(d->vec_dtype)))
+    return fail(FO_EINVAL, "conv2d bias epilogue needs a bias vector and a valid vec_dtype");
+  const int oh = (d->h + 2 * d->pad - d->dil * (d->kh - 1) - 1) / d->stride + 1;
+  const int ow = (d->w + 2 * d->pad - d->dil * (d->kw - 1) - 1) / d->stride + 1;
+  if (oh <= 0 || ow <= 0) return fail(FO_EINVAL, "conv output is empty (oh=%d ow=%d)", oh, ow);
+  if (d->c % 8 != 0) return fail(FO_EINVAL, "conv2d needs C %% 8 == 0 (16-byte channel chunks), got C=%d", d->c);
+  const int ob = esize(d->out_dtype);
+  if ((static_cast<int64_t>(d->f) * ob) % 16 != 0 || d->f % 8 != 0)
+    return fail(FO_EINVAL, "conv2d needs F %% 8 == 0, got F=%d", d->f);
+  const int64_t M64 = static_cast<int64_t>(d->n) * oh * ow;
+  const int64_t K64 = static_cast<int64_t>(d->kh) * d->kw * d->c;
+  const int64_t xelems = static_cast<int64_t>(d->n) * d->h * d->w * d->c;
+  if (M64 > (1ll << 31) - 1 || xelems > (1ll << 40)) return fail(FO_EINVAL, "conv problem too large");
+  if (M64 == 0) return ok();
+  if (d->x == nullptr || d->wgt == nullptr || d->out == nullptr || !aligned16(d->x) || !aligned16(d->wgt) ||
+      !aligned16(d->out))
+    return fail(FO_EINVAL, "x, wgt and out must be 16-byte aligned device pointers");
+  DevInfo di;
+  if (int rc = device_info(&di)) return rc;
+
+  fo::LaunchArgs la;
+  memset(&la, 0, sizeof(la));
+  fo::KParams& p = la.p;
+  const int bn = cfg->block_n;
+  p.M = static_cast<int>(M64);
+  p.N = d->f;
+  p.K = static_cast<int>(K64);
+  p.tiles_m = (p.M + 127) / 128;
+  p.tiles_n = (p.N + bn - 1) / bn;
+  p.num_tiles = p.tiles_m * p.tiles_n;
+  p.c_blocks = (d->c + 63) / 64;
+  p.k_blocks = d->kh * d->kw * p.c_blocks;
+  p.group_m = cfg->group_m;
+  p.stages = cfg->stages;
+  p.ab_bf16 = d->in_dtype == FO_DT_BF16;
+  p.b_mn = 1;
+  p.has_bias = has_bias;
+  p.bias = d->bias;
+  p.vec_dtype = d->vec_dtype;
+  p.out = d->out;
+  p.ldo = d->f;
+  p.x = d->x;
+  p.H = d->h;
+  p.W = d->w;
+  p.C = d->c;
+  p.OH = oh;
+  p.OW = ow;
+  p.KH = d->kh;
+  p.KW = d->kw;
+  p.stride = d->stride;
+  p.pad = d->pad;
+  p.dil = d->dil;
+  fill_common(p, di);
+  if (int rc = make_tmap(&la.tmB, d->in_dtype, d->wgt, d->f, K64, static_cast<uint64_t>(d->f) * 2, 64, 64, "weights"))
+    return rc;
+  if (int rc = make_tmap(&la.tmC, d->out_dtype, d->out, d->f, M64, static_cast<uint64_t>(d->f) * ob, 128 / ob, 32,
+                         "out"))
+    return rc;
+  const int cap = cfg->max_ctas > 0 ? cfg->max_ctas : di.sms;
+  la.grid = p.num_tiles < cap ? p.num_tiles : cap;
+  la.smem = fo::smem_bytes_for(bn, cfg->stages);
+  la.stream = static_cast<cudaStream_t>(stream);
+  const int out_dt = d->out_dtype == FO_DT_F16 ? fo::DT_F16 : d->out_dtype == FO_DT_BF16 ? fo::DT_BF16 : fo::DT_F32;
+  cudaError_t e = fo::launch_conv_family(bn, act, out_dt, la);
+  if (e != cudaSuccess) return fail(FO_ECUDA, "kernel launch failed: %s", cudaGetErrorString(e));
+  g_launches.fetch_add(1);
+  return ok();
+}
+
+int fo_device_status(int32_t device, int32_t clear, int32_t* where) {
+  int prev = 0;
+  if (cudaGetDevice(&prev) != cudaSuccess) return fail(FO_ENODEVICE, "no CUDA device");
+  if (device < 0 || device >= kMaxDevices) return fail(FO_EINVAL, "bad device %d", device);
+  int* st = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    st = g_status[device];
+  }
+  if (where != nullptr) *where = 0;
+  if (st == nullptr) return 0;  // nothing launched on this device yet
+  if (prev != device) cudaSetDevice(device);
+  int h[4] = {0, 0, 0, 0};
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpy(h, st, sizeof(h), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && clear) e = cudaMemset(st, 0, sizeof(h));
+  if (e == cudaSuccess && clear) e = cudaDeviceSynchronize();
+  if (prev != device) cudaSetDevice(prev);
+  if (e != cudaSuccess) return fail(FO_ECUDA, "reading the device status failed: %s", cudaGetErrorString(e));
+  if (where != nullptr) *where = h[1];
+  return h[0] == fo::kStatusTimeout ? FO_ETIMEOUT : h[0];
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------- self-test
+namespace {
+
+__global__ void fo_wait_selftest_kernel(int* status, unsigned long long timeout_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  const uint32_t b = fo::smem_u32(&bar);
+  if (threadIdx.x == 0) {
+    fo::mbar_init(b, 1);
+    fo::fence_mbar_init();
+  }
+  __syncwarp();
+  // Nothing ever arrives on `bar`: the wait must run out and report it.
+  bool got = true;
+  if (threadIdx.x == 0) got = fo::mbar_wait(b, 0, timeout_ns, nullptr);
+  if (threadIdx.x == 0 && !got) {
+    status[0] = fo::kStatusTimeout;
+    status[1] = 0x7e57;
+  }
+}
+
+}  // namespace
+
+extern "C" int fo_selftest_wait_timeout(uint64_t timeout_ns, void* stream) {
+  if (timeout_ns == 0 || timeout_ns > 10000000000ull) return fail(FO_EINVAL, "timeout must be in (0, 10 s]");
+  DevInfo di;
+  if (int rc = device_info(&di)) return rc;
+  int* st = nullptr;
+  if (cudaMalloc(&st, 4 * sizeof(int)) != cudaSuccess) return fail(FO_ECUDA, "cudaMalloc failed");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaMemsetAsync(st, 0, 4 * sizeof(int), s);
+  fo_wait_selftest_kernel<<<1, 32, 0, s>>>(st, timeout_ns);
+  cudaError_t e = cudaGetLastError();
+  int h[4] = {0, 0, 0, 0};
+  if (e == cudaSuccess) e = cudaMemcpyAsync(h, st, sizeof(h), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  cudaFree(st);
+  if (e != cudaSuccess) return fail(FO_ECUDA, "self-test failed: %s", cudaGetErrorString(e));
+  g_launches.fetch_add(1);
+  if (h[0] == fo::kStatusTimeout) return fail(FO_ETIMEOUT, "bounded wait ran out after %llu ns as expected",
+                                              static_cast<unsigned long long>(timeout_ns));
+  return ok();
+}

@@ -1,0 +1,624 @@
+// fo_kernel.cuh -- the persistent, warp-specialised tcgen05 kernel behind every operator
+// of the library: gemm, gemm+bias(+act), gemm+bias+LayerNorm and conv2d (implicit GEMM).
+//
+// One CTA per SM loops over 128 x BN output tiles.  Warp roles:
+//   producer  : GEMM -- one thread issues TMA loads of A (128 x 64) and B (BN x 64) per
+//               k-block into a `stages`-deep shared-memory ring;
+//               conv -- a 128-thread warpgroup gathers the im2col rows of A with 16-byte
+//               cp.async (zero-fill gives the padding) while one thread TMA-loads the
+//               weight tile.
+//   mma       : one thread issues tcgen05.mma (M=128, N=BN, K=16) into one of two TMEM
+//               accumulators (2 x BN fp32 columns), so the epilogue of tile i overlaps
+//               the mainloop of tile i+1.
+//   epilogue  : four warps (one per TMEM lane quarter) read the accumulator with
+//               tcgen05.ld, apply bias / activation in fp32, convert, stage 32 x 128 B
+//               blocks in 128B-swizzled shared memory and write them with TMA stores.
+//               For LayerNorm each thread owns one output row, so exact per-row
+//               (mean, M2) of the fp32 tile is a register reduction; the last CTA to
+//               finish a 128-row block (global counter) merges the per-tile statistics
+//               (Chan et al.) and normalises the block in place.
+// Every wait is bounded (mbar_wait); a wait that runs out records FO_ETIMEOUT in the
+// device status word, raises a CTA-local abort flag, drains its in-flight copies and
+// returns.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "fo_ptx.cuh"
+
+namespace fo {
+
+enum : int { DT_F16 = 0, DT_BF16 = 1, DT_F32 = 2 };
+enum : int { ACT_NONE = 0, ACT_RELU = 1, ACT_GELU_TANH = 2, ACT_GELU_ERF = 3 };
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;  // 64 16-bit elements = one 128-byte swizzle row
+constexpr int kAStageBytes = kBM * kBK * 2;
+constexpr int kEpiWarps = 4;
+constexpr int kEpiBufBytes = 32 * 128;
+constexpr int kEpiBytes = kEpiWarps * 2 * kEpiBufBytes;
+constexpr int kMiscBytes = 1280;
+constexpr int kMaxStages = 8;
+
+// Status codes written into the device status word (first writer wins).
+constexpr int kStatusTimeout = 5;
+
+struct KParams {
+  int M, N, K;
+  int tiles_m, tiles_n, num_tiles, k_blocks;
+  int group_m;
+  int stages;
+  int ab_bf16;
+  int b_mn;
+  int has_bias;
+  const void* bias;
+  const void* gamma;
+  const void* beta;
+  int vec_dtype;
+  float eps;
+  float2* ln_stats;  // [tiles_n][M] (mean, M2) of each row over one N tile
+  int* ln_counters;  // [tiles_m] finished-tile counters, self-resetting
+  void* out;
+  long long ldo;
+  int* status;  // [0] = code, [1] = where, [2] = block
+  unsigned long long timeout_ns;
+  // implicit-GEMM conv geometry (NHWC)
+  const void* x;
+  int H, W, C, OH, OW, KH, KW, stride, pad, dil, c_blocks;
+};
+
+__host__ __device__ constexpr int b_stage_bytes(int bn) { return bn * kBK * 2; }
+__host__ __device__ constexpr int smem_bytes_for(int bn, int stages) {
+  return 1024 + stages * (kAStageBytes + b_stage_bytes(bn)) + kEpiBytes + kMiscBytes;
+}
+
+__device__ __forceinline__ void record_error(const KParams& p, int code, int where) {
+  if (atomicCAS(p.status, 0, code) == 0) {
+    p.status[1] = where;
+    p.status[2] = static_cast<int>(blockIdx.x);
+  }
+}
+
+__device__ __forceinline__ float load_vec(const void* ptr, int dt, int i) {
+  if (dt == DT_F32) return __ldg(reinterpret_cast<const float*>(ptr) + i);
+  const unsigned short raw = __ldg(reinterpret_cast<const unsigned short*>(ptr) + i);
+  if (dt == DT_BF16) return __bfloat162float(__ushort_as_bfloat16(raw));
+  return __half2float(__ushort_as_half(raw));
+}
+
+template <int ACT>
+__device__ __forceinline__ float apply_act(float x) {
+  if constexpr (ACT == ACT_RELU) {
+    return fmaxf(x, 0.0f);
+  } else if constexpr (ACT == ACT_GELU_TANH) {
+    // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))  -- end2end.py:37-38 new_gelu
+    const float u = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);
+    float t;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(u));
+    return 0.5f * x * (1.0f + t);
+  } else if constexpr (ACT == ACT_GELU_ERF) {
+    return 0.5f * x * (1.0f + erff(x * 0.7071067811865476f));
+  } else {
+    return x;
+  }
+}
+
+template <int DT>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  if constexpr (DT == DT_BF16) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  } else {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+}
+template <int DT>
+__device__ __forceinline__ float2 unpack2(uint32_t u) {
+  if constexpr (DT == DT_BF16) {
+    __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&u);
+    return __bfloat1622float2(h);
+  } else {
+    __half2 h = *reinterpret_cast<__half2*>(&u);
+    return __half22float2(h);
+  }
+}
+
+// Forces every later use of r[] to follow tcgen05.wait::ld.
+__device__ __forceinline__ void tc_wait_ld_regs(uint32_t (&r)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                 "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                 "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]),
+                 "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+                 "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]),
+                 "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
+
+__device__ __forceinline__ void tile_coords(const KParams& p, int t, int& tm, int& tn) {
+  if (p.group_m <= 0) {
+    tm = t / p.tiles_n;
+    tn = t - tm * p.tiles_n;
+    return;
+  }
+  const int per_group = p.group_m * p.tiles_n;
+  const int g = t / per_group;
+  const int r = t - g * per_group;
+  const int first_m = g * p.group_m;
+  const int gm = min(p.group_m, p.tiles_m - first_m);
+  tm = first_m + r % gm;
+  tn = r / gm;
+}
+
+// Chan et al. parallel merge of (count, mean, M2).
+__device__ __forceinline__ void chan_merge(float& cnt, float& mean, float& m2, float cb,
+                                           float mb, float m2b) {
+  if (cb <= 0.f) return;
+  const float tot = cnt + cb;
+  const float delta = mb - mean;
+  const float f = cb / tot;
+  mean = fmaf(delta, f, mean);
+  m2 = m2 + m2b + delta * delta * cnt * f;
+  cnt = tot;
+}
+
+constexpr uint64_t kDrainTimeoutNs = 1000000000ull;
+
+// Waits (bounded, ignoring the abort flag) until the most recent load into every stage of
+// the ring has landed, so no TMA write into shared memory is in flight when the CTA exits.
+// Load number q (0-based) went to stage q % stages as that stage's phase q / stages.
+__device__ __forceinline__ void drain_loads(uint32_t bar_full, int stages, int issued) {
+  for (int q = issued - 1; q >= 0 && q >= issued - stages; --q) {
+    mbar_wait(bar_full + 8 * (q % stages), static_cast<uint32_t>((q / stages) & 1),
+              kDrainTimeoutNs, nullptr);
+  }
+}
+
+template <int BN, int ACT, int OUT_DT, bool LN, bool CONV>
+__global__ void __launch_bounds__(CONV ? 288 : 192, 1)
+    fo_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                 const __grid_constant__ CUtensorMap tmC, const KParams p) {
+  constexpr int kProducerWarps = CONV ? 4 : 1;
+  constexpr int kMmaWarp = kProducerWarps;
+  constexpr int kFirstEpiWarp = kProducerWarps + 1;
+  constexpr int kBStage = b_stage_bytes(BN);
+  constexpr int kOutBytes = OUT_DT == DT_F32 ? 4 : 2;
+  constexpr int kCPC = 128 / kOutBytes;  // output columns per 128-byte chunk
+  constexpr int kChunks = BN / kCPC;
+  constexpr uint32_t kTmemCols = 2 * BN;
+  static_assert(!LN || OUT_DT != DT_F32, "LayerNorm output is 16-bit");
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const int stages = p.stages;
+  const uint32_t sA = smem_u32(smem);
+  const uint32_t sB = sA + stages * kAStageBytes;
+  const uint32_t sEpi = sB + stages * kBStage;
+  uint8_t* misc = smem + (sEpi - sA) + kEpiBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(misc);
+  const uint32_t bar_full = smem_u32(bars);                 // [kMaxStages]
+  const uint32_t bar_empty = smem_u32(bars + kMaxStages);   // [kMaxStages]
+  const uint32_t bar_tfull = smem_u32(bars + 2 * kMaxStages);   // [2]
+  const uint32_t bar_tempty = smem_u32(bars + 2 * kMaxStages + 2);  // [2]
+  const uint32_t bar_drain = smem_u32(bars + 2 * kMaxStages + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 8 * (2 * kMaxStages + 6));
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* ln_last = reinterpret_cast<volatile int*>(tmem_slot + 2);
+  volatile int* epi_stop = reinterpret_cast<volatile int*>(tmem_slot + 3);
+  float* row_mean = reinterpret_cast<float*>(misc + 256);
+  float* row_rstd = reinterpret_cast<float*>(misc + 768);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(bar_full + 8 * s, CONV ? 128 : 1);
+      mbar_init(bar_empty + 8 * s, 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(bar_tfull + 8 * a, 1);
+      mbar_init(bar_tempty + 8 * a, kEpiWarps);
+    }
+    mbar_init(bar_drain, 1);
+    *abort_flag = 0;
+    *ln_last = 0;
+    *epi_stop = 0;
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  if (threadIdx.x == 32 * kFirstEpiWarp) {
+    tma_prefetch_desc(&tmC);
+    if (p.k_blocks > 0) {  // with K = 0 the A / B maps are left unencoded
+      if (!CONV) tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint64_t tmo = p.timeout_ns;
+
+  if (warp < kProducerWarps) {
+    // ------------------------------------------------------------------ producer
+    if constexpr (!CONV) {
+      if (lane == 0) {
+        int s = 0;
+        uint32_t ph = 0;
+        int issued = 0;  // stage loads issued by this thread
+        bool ok = true;
+        for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+          int tm, tn;
+          tile_coords(p, t, tm, tn);
+          for (int kb = 0; kb < p.k_blocks; ++kb) {
+            if (!mbar_wait(bar_empty + 8 * s, ph ^ 1, tmo, abort_flag)) {
+              ok = false;
+              break;
+            }
+            const uint32_t fb = bar_full + 8 * s;
+            mbar_arrive_expect_tx(fb, kAStageBytes + kBStage);
+            tma_load_2d(sA + s * kAStageBytes, &tmA, fb, kb * kBK, tm * kBM);
+            if (p.b_mn) {
+#pragma unroll
+              for (int j = 0; j < BN / 64; ++j)
+                tma_load_2d(sB + s * kBStage + j * 64 * 128, &tmB, fb, tn * BN + j * 64, kb * kBK);
+            } else {
+              tma_load_2d(sB + s * kBStage, &tmB, fb, kb * kBK, tn * BN);
+            }
+            ++issued;
+            if (++s == stages) {
+              s = 0;
+              ph ^= 1;
+            }
+          }
+        }
+        if (!ok) {
+          record_error(p, kStatusTimeout, 0x10);
+          *abort_flag = 1;
+        }
+        drain_loads(bar_full, stages, issued);
+      }
+    } else {
+      // conv gather: thread i of the warpgroup owns row i (one output pixel) of the A tile.
+      const int i = threadIdx.x;  // 0..127
+      constexpr int kLag = 2;
+      int s = 0;
+      uint32_t ph = 0;
+      int issued = 0;  // cp.async groups committed by this thread
+      bool ok = true;
+      const int ohow = p.OH * p.OW;
+      const char* xb = reinterpret_cast<const char*>(p.x);
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        int tm, tn;
+        tile_coords(p, t, tm, tn);
+        const int m = tm * kBM + i;
+        const bool valid_m = m < p.M;
+        const int n_img = valid_m ? m / ohow : 0;
+        const int rem = valid_m ? m - n_img * ohow : 0;
+        const int oh = rem / p.OW;
+        const int ow = rem - oh * p.OW;
+        const int ih0 = oh * p.stride - p.pad;
+        const int iw0 = ow * p.stride - p.pad;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          const int tap = kb / p.c_blocks;
+          const int cb = kb - tap * p.c_blocks;
+          const int kh = tap / p.KW;
+          const int kw = tap - kh * p.KW;
+          if (!mbar_wait(bar_empty + 8 * s, ph ^ 1, tmo, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = bar_full + 8 * s;
+          if (i == 0) {
+            mbar_expect_tx(fb, kBStage);
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(sB + s * kBStage + j * 64 * 128, &tmB, fb, tn * BN + j * 64,
+                          tap * p.C + cb * kBK);
+          }
+          const int ih = ih0 + kh * p.dil;
+          const int iw = iw0 + kw * p.dil;
+          const bool inb = valid_m && ih >= 0 && ih < p.H && iw >= 0 && iw < p.W;
+          const int c0 = cb * kBK;
+          const char* src =
+              xb + ((static_cast<long long>(n_img) * p.H + (inb ? ih : 0)) * p.W + (inb ? iw : 0)) *
+                           static_cast<long long>(p.C) * 2 +
+                       static_cast<long long>(c0) * 2;
+          const uint32_t dst_row = sA + s * kAStageBytes + i * 128;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const bool v = inb && (c0 + j * 8) < p.C;
+            cp_async_16(dst_row + ((j ^ (i & 7)) << 4), v ? src + j * 16 : xb, v ? 16u : 0u);
+          }
+          cp_async_commit();
+          ++issued;
+          if (issued > kLag) {
+            cp_async_wait<kLag>();
+            fence_proxy_async_smem();
+            int ss = s - kLag;
+            if (ss < 0) ss += stages;
+            mbar_arrive(bar_full + 8 * ss);
+          }
+          if (++s == stages) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+      }
+      cp_async_wait_all();
+      fence_proxy_async_smem();
+      // Arrive for the groups still owed (the last min(issued, kLag) stages).
+      const int owed = issued < kLag ? issued : kLag;
+      for (int j = owed; j >= 1; --j) {
+        int ss = s - j;
+        if (ss < 0) ss += stages;
+        mbar_arrive(bar_full + 8 * ss);
+      }
+      if (!ok) {
+        record_error(p, kStatusTimeout, 0x11);
+        *abort_flag = 1;
+      }
+      if (i == 0) drain_loads(bar_full, stages, issued);  // the weight tiles
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(p.ab_bf16, p.b_mn, BN);
+      int s = 0;
+      uint32_t ph = 0;
+      int acc = 0;
+      uint32_t acc_ph = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        if (!mbar_wait(bar_tempty + 8 * acc, acc_ph ^ 1, tmo, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + acc * BN;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(bar_full + 8 * s, ph, tmo, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = sA + s * kAStageBytes;
+          const uint32_t b0 = sB + s * kBStage;
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t ad = sdesc_sw128(a0 + k * 32, 16, 1024);
+            const uint64_t bd = p.b_mn ? sdesc_sw128(b0 + k * 2048, 64 * 128, 1024)
+                                       : sdesc_sw128(b0 + k * 32, 16, 1024);
+            tc_mma_f16(d, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          tc_commit(bar_empty + 8 * s);
+          if (++s == stages) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit(bar_tfull + 8 * acc);
+        acc ^= 1;
+        if (acc == 0) acc_ph ^= 1;
+      }
+      if (!ok) {
+        record_error(p, kStatusTimeout, 0x20);
+        *abort_flag = 1;
+      }
+      // Drain: all issued MMAs complete before TMEM is released.
+      tc_commit(bar_drain);
+      mbar_wait(bar_drain, 0, kDrainTimeoutNs, nullptr);
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    const int ew = warp - kFirstEpiWarp;  // 0..3
+    const int quarter = warp & 3;         // TMEM lane quarter this warp may access
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t buf0 = sEpi + ew * 2 * kEpiBufBytes;
+    int acc = 0;
+    uint32_t acc_ph = 0;
+    uint32_t nstore = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+      int tm, tn;
+      tile_coords(p, t, tm, tn);
+      if (!mbar_wait(bar_tfull + 8 * acc, acc_ph, tmo, abort_flag)) {
+        ok = false;
+        *abort_flag = 1;
+        // Without LayerNorm the four warps are independent and this one can stop.  With
+        // LayerNorm they meet at named barriers, so it runs the tile to the next barrier
+        // and all four stop together on the snapshot taken there.
+        if constexpr (!LN) break;
+      }
+      tc_fence_after();
+      const int row0 = tm * kBM + quarter * 32;
+      const int col0 = tn * BN;
+      float st_cnt = 0.f, st_mean = 0.f, st_m2 = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < kChunks; ++c) {
+        const int cbase = col0 + c * kCPC;
+        float v[kCPC];
+        {
+          uint32_t r0[32];
+          tmem_ld_32x32b_x32(tmem_base + lane_off + acc * BN + c * kCPC, r0);
+          tc_wait_ld_regs(r0);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = p.k_blocks > 0 ? __uint_as_float(r0[i]) : 0.f;
+          if constexpr (kCPC == 64) {
+            uint32_t r1[32];
+            tmem_ld_32x32b_x32(tmem_base + lane_off + acc * BN + c * kCPC + 32, r1);
+            tc_wait_ld_regs(r1);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[32 + i] = p.k_blocks > 0 ? __uint_as_float(r1[i]) : 0.f;
+          }
+        }
+        if (c == kChunks - 1) {
+          // The accumulator buffer is free once every lane's loads of it have completed.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar_tempty + 8 * acc);
+        }
+        if (p.has_bias) {
+#pragma unroll
+          for (int h = 0; h < kCPC / 32; ++h) {
+            const int n = cbase + h * 32 + lane;
+            const float bl = n < p.N ? load_vec(p.bias, p.vec_dtype, n) : 0.f;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[h * 32 + i] += __shfl_sync(0xffffffffu, bl, i);
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < kCPC; ++i) v[i] = apply_act<ACT>(v[i]);
+        if constexpr (LN) {
+          const int cv = min(kCPC, p.N - cbase);
+          if (cv > 0) {
+            float sum = 0.f;
+#pragma unroll
+            for (int i = 0; i < kCPC; ++i) sum += (i < cv) ? v[i] : 0.f;
+            const float cm = sum / static_cast<float>(cv);
+            float q = 0.f;
+#pragma unroll
+            for (int i = 0; i < kCPC; ++i) {
+              const float d = v[i] - cm;
+              q += (i < cv) ? d * d : 0.f;
+            }
+            chan_merge(st_cnt, st_mean, st_m2, static_cast<float>(cv), cm, q);
+          }
+        }
+        // Stage the 32 x 128 B block in swizzled shared memory, then TMA-store it.
+        const uint32_t buf = buf0 + (nstore & 1) * kEpiBufBytes;
+        if (nstore >= 2) {
+          if (lane == 0) bulk_wait_read<1>();
+          __syncwarp();
+        }
+        const uint32_t rowp = buf + lane * 128;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          uint32_t w0, w1, w2, w3;
+          if constexpr (OUT_DT == DT_F32) {
+            w0 = __float_as_uint(v[4 * j + 0]);
+            w1 = __float_as_uint(v[4 * j + 1]);
+            w2 = __float_as_uint(v[4 * j + 2]);
+            w3 = __float_as_uint(v[4 * j + 3]);
+          } else {
+            w0 = pack2<OUT_DT>(v[8 * j + 0], v[8 * j + 1]);
+            w1 = pack2<OUT_DT>(v[8 * j + 2], v[8 * j + 3]);
+            w2 = pack2<OUT_DT>(v[8 * j + 4], v[8 * j + 5]);
+            w3 = pack2<OUT_DT>(v[8 * j + 6], v[8 * j + 7]);
+          }
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(rowp + ((j ^ (lane & 7)) << 4)),
+                       "r"(w0), "r"(w1), "r"(w2), "r"(w3)
+                       : "memory");
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, buf, cbase, row0);
+          bulk_commit();
+        }
+        ++nstore;
+      }
+      acc ^= 1;
+      if (acc == 0) acc_ph ^= 1;
+
+      if constexpr (LN) {
+        // Per-tile row statistics, then the row-block completion protocol.
+        const int row = row0 + lane;
+        if (row < p.M) p.ln_stats[static_cast<long long>(tn) * p.M + row] = make_float2(st_mean, st_m2);
+        if (lane == 0) {
+          bulk_wait<0>();
+          fence_proxy_async_global();
+        }
+        __threadfence();
+        __syncwarp();
+        named_bar_sync(1, 128);
+        if (ew == 0 && lane == 0) {
+          const int stop = *abort_flag;
+          if (!stop) {
+            __threadfence();
+            const int old = atomicAdd(p.ln_counters + tm, 1);
+            *ln_last = (old == p.tiles_n - 1) ? 1 : 0;
+          }
+          *epi_stop = stop;
+        }
+        named_bar_sync(1, 128);
+        if (*epi_stop) break;
+        if (*ln_last) {
+          __threadfence();
+          // 1) per-row mean / rstd from the tiles_n partial (mean, M2) pairs
+          const int r = ew * 32 + lane;
+          const int grow = tm * kBM + r;
+          if (grow < p.M) {
+            float cnt = 0.f, mean = 0.f, m2 = 0.f;
+            for (int j = 0; j < p.tiles_n; ++j) {
+              const float2 pm = __ldcg(p.ln_stats + static_cast<long long>(j) * p.M + grow);
+              const float cj = static_cast<float>(min(BN, p.N - j * BN));
+              chan_merge(cnt, mean, m2, cj, pm.x, pm.y);
+            }
+            row_mean[r] = mean;
+            row_rstd[r] = rsqrtf(m2 / static_cast<float>(p.N) + p.eps);
+          }
+          named_bar_sync(1, 128);
+          // 2) normalise the 128-row block in place: warp ew sweeps rows ew*32..+31,
+          //    each lane 8 consecutive columns of every 256-column slab.
+          typedef unsigned short u16;
+          u16* outp = reinterpret_cast<u16*>(p.out);
+          for (int cb = 0; cb * 256 < p.N; ++cb) {
+            const int col = cb * 256 + lane * 8;
+            if (col < p.N) {
+              float g[8], b[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                g[e] = load_vec(p.gamma, p.vec_dtype, col + e);
+                b[e] = load_vec(p.beta, p.vec_dtype, col + e);
+              }
+#pragma unroll 4
+              for (int rr = 0; rr < 32; ++rr) {
+                const int lr = ew * 32 + rr;
+                const int gr = tm * kBM + lr;
+                if (gr < p.M) {
+                  uint4* addr = reinterpret_cast<uint4*>(outp + gr * p.ldo + col);
+                  uint4 y = __ldcg(addr);
+                  const float mu = row_mean[lr], rs = row_rstd[lr];
+                  uint32_t w[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) {
+                    const float2 f = unpack2<OUT_DT>(w[e]);
+                    w[e] = pack2<OUT_DT>(fmaf((f.x - mu) * rs, g[2 * e], b[2 * e]),
+                                         fmaf((f.y - mu) * rs, g[2 * e + 1], b[2 * e + 1]));
+                  }
+                  __stcg(addr, make_uint4(w[0], w[1], w[2], w[3]));
+                }
+              }
+            }
+          }
+          if (ew == 0 && lane == 0) p.ln_counters[tm] = 0;
+          named_bar_sync(1, 128);
+        }
+      }
+    }
+    if (!ok) {
+      record_error(p, kStatusTimeout, 0x30);
+      *abort_flag = 1;
+    }
+    if (lane == 0) bulk_wait<0>();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace fo

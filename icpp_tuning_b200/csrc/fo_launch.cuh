@@ -1,0 +1,33 @@
+// fo_launch.cuh -- host-side launch of one fo_tc_kernel instantiation.  Each family of
+// instantiations (gemm, gemm+LayerNorm, conv) is compiled in its own translation unit.
+#pragma once
+#include <cuda_runtime.h>
+
+#include "fo_kernel.cuh"
+
+namespace fo {
+
+struct LaunchArgs {
+  CUtensorMap tmA, tmB, tmC;
+  KParams p;
+  int grid;
+  int smem;
+  cudaStream_t stream;
+};
+
+template <int BN, int ACT, int OUT_DT, bool LN, bool CONV>
+cudaError_t launch_tc(const LaunchArgs& a) {
+  auto kern = fo_tc_kernel<BN, ACT, OUT_DT, LN, CONV>;
+  // The attribute is per device; setting it on every call costs well under a microsecond.
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, a.smem);
+  if (e != cudaSuccess) return e;
+  kern<<<a.grid, CONV ? 288 : 192, a.smem, a.stream>>>(a.tmA, a.tmB, a.tmC, a.p);
+  return cudaGetLastError();
+}
+
+// Returns cudaErrorInvalidValue for a combination this build does not instantiate.
+cudaError_t launch_gemm_family(int bn, int act, int out_dt, const LaunchArgs& a);
+cudaError_t launch_ln_family(int bn, int out_dt, const LaunchArgs& a);
+cudaError_t launch_conv_family(int bn, int act, int out_dt, const LaunchArgs& a);
+
+}  // namespace fo
