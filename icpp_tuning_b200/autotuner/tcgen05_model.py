@@ -1,0 +1,161 @@
+"""Cost model of the sm_100a kernels in this package (TuneConfig.kind == "tcgen05").
+
+The reference's factors (kernel/autotuner/cost_model.py:544-757) describe a
+register-tiled kernel: outputs per thread, occupancy from registers, warps per block.
+None of those exist in a persistent, warp-specialised tcgen05 kernel: the accumulator
+lives in TMEM, one CTA owns an SM, and the warp split is fixed.  This module keeps the
+reference's shape -- a product of seven factors in (0, 1], the same factor names, the
+same `score_formula` entry point -- but derives each factor from a time model of one SM
+running this design (docs/cost_model.md of the reference describes the factor idea):
+
+  eff_mainloop      tile padding of M / N / K x tensor-pipe rate of a 128 x BN x 16 MMA
+                    (narrow N re-reads A from shared memory more often per FLOP)
+  eff_memory        compute time / HBM time, with operand re-reads across waves set by
+                    the tile raster (group_m) and the 126 MB L2
+  eff_parallel      SM-time actually used: wave quantisation of the persistent grid over
+                    148 SMs, plus the fixed launch / prologue / drain time
+  eff_pipeline      whether `stages` k-blocks in flight cover the TMA latency
+  eff_implicit_conv conv only: im2col gather bandwidth of the cp.async producer
+  eff_epilogue      overlap of the epilogue (TMEM -> registers -> TMA store) with the
+                    next tile's mainloop (two TMEM accumulators)
+  eff_reduction     LayerNorm only: the in-place normalisation pass of each row block
+
+score = product = (ideal tensor time) / (predicted time).  The constants in CONSTANTS
+are fitted to B200 measurements of these kernels.
+"""
+from __future__ import annotations
+
+import math
+
+from .cost_model import OpSpec, TuneConfig
+from .gpu_spec import GPUSpec
+
+CONSTANTS = {
+    # relative tensor-pipe rate of one 128 x BN x 16 MMA (shared-memory operand traffic)
+    "mma_rate_bn": {256: 1.0, 128: 0.93, 64: 0.72},
+    "tma_latency_s": 1.2e-6,  # global -> shared latency a stage ring has to cover
+    "epi_bytes_per_s_sm": 120e9,  # epilogue store throughput of one SM (TMEM ld + TMA store)
+    "ln_bytes_per_s_sm": 90e9,  # normalisation pass read+write throughput of one SM
+    "gather_bytes_per_s_sm": 150e9,  # cp.async im2col gather throughput of one SM
+    "fixed_s": 6.0e-6,  # launch + TMEM alloc + pipeline fill + last epilogue
+    "l2_fraction": 0.6,  # share of L2 that holds one wave's operand working set
+}
+
+
+def _cdiv(a: int, b: int) -> int:
+    return -(-a // b)
+
+
+def _sm_rate(hw: GPUSpec) -> float:
+    return hw.peak_fp16_tflops * 1e12 / max(1, hw.num_sm)
+
+
+def _traffic_bytes(op: OpSpec, c: TuneConfig, hw: GPUSpec, ctas: int) -> float:
+    """HBM bytes: operands re-read once per wave in which they are not L2-resident."""
+    ml = op.mainloop
+    tiles_m, tiles_n = _cdiv(op.M, c.block_M), _cdiv(op.N, c.block_N)
+    a_row = c.block_M * op.K * ml.input_element_bytes   # one 128-row block of A
+    b_col = c.block_N * op.K * ml.weight_element_bytes  # one BN-column block of B
+    if ml.kind == "implicit_gemm_conv":
+        a_total = ml.input_elements * ml.input_element_bytes  # input read once (halo in L2)
+    else:
+        a_total = tiles_m * a_row
+    b_total = tiles_n * b_col
+    out = ml.output_elements * ml.output_element_bytes
+    l2 = hw.l2_cache_size * CONSTANTS["l2_fraction"]
+    if a_total + b_total <= l2:
+        return a_total + b_total + out
+    # Operands larger than L2: each wave re-reads the blocks it touches.
+    g = c.group_size_m if c.group_size_m > 0 else 1
+    if c.group_size_m > 0:
+        rows_per_wave = min(tiles_m, g)
+        cols_per_wave = min(tiles_n, _cdiv(ctas, rows_per_wave))
+    else:
+        cols_per_wave = min(tiles_n, ctas)
+        rows_per_wave = max(1, _cdiv(ctas, tiles_n))
+    waves = _cdiv(tiles_m * tiles_n, ctas)
+    per_wave = rows_per_wave * a_row + cols_per_wave * b_col
+    return max(a_total + b_total, waves * per_wave) + out
+
+
+def _model(op: OpSpec, c: TuneConfig, hw: GPUSpec) -> dict:
+    K = CONSTANTS
+    ml = op.mainloop
+    bm, bn, bk = c.block_M, c.block_N, c.block_K
+    tiles_m, tiles_n = _cdiv(op.M, bm), _cdiv(op.N, bn)
+    k_blocks = max(1, _cdiv(op.K, bk))
+    tiles = tiles_m * tiles_n
+    sms = hw.num_sm
+    ctas = max(1, min(tiles, c.max_ctas if c.max_ctas > 0 else sms))
+    waves = _cdiv(tiles, ctas)
+    rate = _sm_rate(hw)
+
+    # -- mainloop: padded MMA work of one tile at the BN-dependent tensor rate
+    e_bn = K["mma_rate_bn"].get(bn, 0.6)
+    padding = (op.M * op.N * op.K) / float(tiles_m * bm * tiles_n * bn * k_blocks * bk)
+    t_kb = 2.0 * bm * bn * bk / (rate * e_bn)
+    # -- pipeline: stages - 1 loads in flight while one stage is consumed
+    e_pipe = min(1.0, (c.num_stages - 1) * t_kb / K["tma_latency_s"])
+    # -- conv: the cp.async producer gathers bm x bk 16-bit elements per k-block
+    e_conv = 1.0
+    if ml.kind == "implicit_gemm_conv":
+        t_gather = bm * bk * ml.input_element_bytes / K["gather_bytes_per_s_sm"]
+        e_conv = min(1.0, t_kb / t_gather)
+    t_kb_eff = t_kb / (e_pipe * e_conv)
+    t_tile_mma = k_blocks * t_kb_eff
+    # -- epilogue: overlapped with the next tile's mainloop through two accumulators
+    t_epi = bm * bn * ml.output_element_bytes / K["epi_bytes_per_s_sm"]
+    e_epi = t_tile_mma / max(t_tile_mma, t_epi)
+    t_tile = max(t_tile_mma, t_epi)
+    # -- LayerNorm: one normalisation pass (read + write) per 128-row block
+    t_ln = 0.0
+    if op.has_reduction_epilogue:
+        per_block = bm * op.N * ml.output_element_bytes * 2 / K["ln_bytes_per_s_sm"]
+        # a block's pass overlaps up to two tiles of the CTA's own mainloop
+        stall = max(0.0, per_block - 2 * t_tile_mma) + 0.25 * per_block
+        t_ln = stall * tiles_m / ctas
+    t_work = waves * t_tile
+    e_red = t_work / (t_work + t_ln)
+    # -- parallel: SM-time used by the persistent grid, plus fixed cost
+    quant = tiles / float(waves * sms)
+    t_comp = t_work + t_ln + K["fixed_s"]
+    e_par = quant * (t_work + t_ln) / t_comp
+    # -- memory: HBM time of the operand traffic against the compute time
+    traffic = _traffic_bytes(op, c, hw, ctas)
+    t_mem = traffic / (hw.mem_bandwidth_gbps * 1e9)
+    e_mem = min(1.0, t_comp / max(t_comp, t_mem))
+    e_main = padding * e_bn
+    factors = {
+        "eff_mainloop": e_main, "eff_memory": e_mem, "eff_parallel": e_par,
+        "eff_pipeline": e_pipe, "eff_implicit_conv": e_conv, "eff_epilogue": e_epi,
+        "eff_reduction": e_red,
+    }
+    score = 1.0
+    for v in factors.values():
+        score *= v
+    t_pred = max(t_comp, t_mem)
+    return {
+        "score": score, **factors,
+        "projection": {
+            "tiles_M": tiles_m, "tiles_N": tiles_n, "tiles_K": k_blocks, "grid_size": ctas,
+            "num_tiles": tiles, "waves": waves, "wave_fill": tiles / float(waves * ctas),
+            "predicted_s": t_pred, "predicted_tflops": ml.mainloop_flops / t_pred / 1e12,
+            "hbm_bytes": traffic, "t_tile_s": t_tile, "t_epilogue_s": t_epi,
+            "shared_mem_bytes_per_tile": c.shared_mem_bytes, "tmem_columns": c.tmem_columns,
+        },
+    }
+
+
+def score_tcgen05(op: OpSpec, config: TuneConfig, hw: GPUSpec) -> float:
+    return _model(op, config, hw)["score"]
+
+
+def score_tcgen05_detailed(op: OpSpec, config: TuneConfig, hw: GPUSpec) -> dict:
+    return _model(op, config, hw)
+
+
+def predicted_seconds(op: OpSpec, config: TuneConfig, hw: GPUSpec) -> float:
+    return _model(op, config, hw)["projection"]["predicted_s"]
+
+
+__all__ = ["CONSTANTS", "predicted_seconds", "score_tcgen05", "score_tcgen05_detailed"]

@@ -1,0 +1,53 @@
+"""Raw config spaces of the sm_100a kernels and their descriptor base class.
+
+A raw config is the dict the operator modules pass to the kernel (and that
+`select_best` returns): block_M (tcgen05 M = 128), block_N (64 / 128 / 256), block_K (64
+= one 128-byte swizzle row of 16-bit elements), num_stages, thread_num (6 warps for
+GEMMs, 9 for conv: producer / MMA / 4 epilogue) and group_m (tile raster).  Legality is
+the C ABI's (fo_query_config_legal): shared memory <= 227 KB, TMEM <= 512 columns.
+"""
+from __future__ import annotations
+
+from typing import Any, Dict, List, Sequence
+
+from .cost_model import TuneConfig
+from .interface import TileLangKernelBase
+
+GEMM_THREADS = 192
+CONV_THREADS = 288
+SMEM_LIMIT = 232448
+
+
+def smem_bytes(block_n: int, stages: int, block_m: int = 128, block_k: int = 64) -> int:
+    """Dynamic shared memory of one CTA (= fo_config_smem_bytes of the C ABI)."""
+    return 1024 + stages * (block_m + block_n) * block_k * 2 + 32768 + 1536
+
+
+def max_stages(block_n: int) -> int:
+    s = 8
+    while s > 2 and smem_bytes(block_n, s) > SMEM_LIMIT:
+        s -= 1
+    return s
+
+
+def tcgen05_configs(block_ns: Sequence[int] = (64, 128, 256), group_ms: Sequence[int] = (0, 8),
+                    conv: bool = False, stages: Sequence[int] = ()) -> List[Dict[str, Any]]:
+    out = []
+    for bn in block_ns:
+        top = max_stages(bn)
+        st = sorted({s for s in (stages or (3, 4, top)) if (3 if conv else 2) <= s <= top})
+        for s in st:
+            for g in group_ms:
+                out.append({"block_M": 128, "block_N": bn, "block_K": 64, "num_stages": s,
+                            "thread_num": CONV_THREADS if conv else GEMM_THREADS, "group_m": g})
+    return out
+
+
+class Tcgen05Descriptor(TileLangKernelBase):
+    """Descriptor base for the sm_100a kernels: raw configs map to kind="tcgen05"."""
+
+    def raw_config_to_tune_config(self, raw: Dict[str, Any]) -> TuneConfig:
+        return TuneConfig(block_M=raw["block_M"], block_N=raw["block_N"], block_K=raw["block_K"],
+                          num_stages=raw["num_stages"], num_warps=raw["thread_num"] // 32,
+                          group_size_m=raw.get("group_m", 0), kind="tcgen05",
+                          max_ctas=raw.get("max_ctas", 0))

@@ -37,7 +37,8 @@ constexpr int kAStageBytes = kBM * kBK * 2;
 constexpr int kEpiWarps = 4;
 constexpr int kEpiBufBytes = 32 * 128;
 constexpr int kEpiBytes = kEpiWarps * 2 * kEpiBufBytes;
-constexpr int kMiscBytes = 1280;
+constexpr int kMiscBytes = 1536;
+constexpr int kNormSlots = 4;  // LayerNorm: row blocks queued for the normalizer warps
 constexpr int kMaxStages = 8;
 
 // Status codes written into the device status word (first writer wins).
@@ -177,7 +178,7 @@ __device__ __forceinline__ void drain_loads(uint32_t bar_full, int stages, int i
 }
 
 template <int BN, int ACT, int OUT_DT, bool LN, bool CONV>
-__global__ void __launch_bounds__(CONV ? 288 : 192, 1)
+__global__ void __launch_bounds__(LN ? 320 : (CONV ? 288 : 192), 1)
     fo_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const __grid_constant__ CUtensorMap tmC, const KParams p) {
   constexpr int kProducerWarps = CONV ? 4 : 1;
@@ -198,18 +199,23 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
   const uint32_t sB = sA + stages * kAStageBytes;
   const uint32_t sEpi = sB + stages * kBStage;
   uint8_t* misc = smem + (sEpi - sA) + kEpiBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(misc);
-  const uint32_t bar_full = smem_u32(bars);                 // [kMaxStages]
-  const uint32_t bar_empty = smem_u32(bars + kMaxStages);   // [kMaxStages]
-  const uint32_t bar_tfull = smem_u32(bars + 2 * kMaxStages);   // [2]
-  const uint32_t bar_tempty = smem_u32(bars + 2 * kMaxStages + 2);  // [2]
-  const uint32_t bar_drain = smem_u32(bars + 2 * kMaxStages + 4);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 8 * (2 * kMaxStages + 6));
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  volatile int* ln_last = reinterpret_cast<volatile int*>(tmem_slot + 2);
-  volatile int* epi_stop = reinterpret_cast<volatile int*>(tmem_slot + 3);
-  float* row_mean = reinterpret_cast<float*>(misc + 256);
-  float* row_rstd = reinterpret_cast<float*>(misc + 768);
+  // misc: [0,64) full[8] | [64,128) empty[8] | [128,144) tfull[2] | [144,160) tempty[2]
+  //       | [160,168) drain | [168,200) norm_full[4] | [200,232) norm_empty[4]
+  //       | [232,248) norm_slot[4] | [248,264) tmem addr + flags | [512,1536) row stats
+  const uint32_t mb = smem_u32(misc);
+  const uint32_t bar_full = mb;
+  const uint32_t bar_empty = mb + 64;
+  const uint32_t bar_tfull = mb + 128;
+  const uint32_t bar_tempty = mb + 144;
+  const uint32_t bar_drain = mb + 160;
+  const uint32_t bar_nfull = mb + 168;
+  const uint32_t bar_nempty = mb + 200;
+  volatile int* norm_slot = reinterpret_cast<volatile int*>(misc + 232);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 248);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 252);
+  volatile int* epi_stop = reinterpret_cast<volatile int*>(misc + 256);
+  float* row_mean = reinterpret_cast<float*>(misc + 512);
+  float* row_rstd = reinterpret_cast<float*>(misc + 1024);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -224,8 +230,11 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
       mbar_init(bar_tempty + 8 * a, kEpiWarps);
     }
     mbar_init(bar_drain, 1);
+    for (int q = 0; q < kNormSlots; ++q) {
+      mbar_init(bar_nfull + 8 * q, 1);
+      mbar_init(bar_nempty + 8 * q, 4);
+    }
     *abort_flag = 0;
-    *ln_last = 0;
     *epi_stop = 0;
     fence_mbar_init();
   }
@@ -417,7 +426,7 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
       tc_commit(bar_drain);
       mbar_wait(bar_drain, 0, kDrainTimeoutNs, nullptr);
     }
-  } else {
+  } else if (warp < kFirstEpiWarp + kEpiWarps) {
     // ------------------------------------------------------------------ epilogue
     const int ew = warp - kFirstEpiWarp;  // 0..3
     const int quarter = warp & 3;         // TMEM lane quarter this warp may access
@@ -427,6 +436,8 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
     uint32_t acc_ph = 0;
     uint32_t nstore = 0;
     bool ok = true;
+    int nq = 0;  // LayerNorm hand-off ring position (used by thread ew == 0, lane == 0)
+    uint32_t nq_ph = 0;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
       int tm, tn;
       tile_coords(p, t, tm, tn);
@@ -541,68 +552,41 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
         __syncwarp();
         named_bar_sync(1, 128);
         if (ew == 0 && lane == 0) {
-          const int stop = *abort_flag;
+          int stop = *abort_flag;
           if (!stop) {
             __threadfence();
             const int old = atomicAdd(p.ln_counters + tm, 1);
-            *ln_last = (old == p.tiles_n - 1) ? 1 : 0;
+            if (old == p.tiles_n - 1) {
+              // Last tile of this 128-row block: every slice's statistics and biased
+              // values are in memory.  Reset the counter for the next launch and queue
+              // the block for this CTA's normalizer warps.
+              __threadfence();
+              p.ln_counters[tm] = 0;
+              if (mbar_wait(bar_nempty + 8 * nq, nq_ph ^ 1, tmo, abort_flag)) {
+                norm_slot[nq] = tm;
+                mbar_arrive(bar_nfull + 8 * nq);
+                if (++nq == kNormSlots) {
+                  nq = 0;
+                  nq_ph ^= 1;
+                }
+              } else {
+                record_error(p, kStatusTimeout, 0x31);
+                *abort_flag = 1;
+                stop = 1;
+              }
+            }
           }
           *epi_stop = stop;
         }
         named_bar_sync(1, 128);
         if (*epi_stop) break;
-        if (*ln_last) {
-          __threadfence();
-          // 1) per-row mean / rstd from the tiles_n partial (mean, M2) pairs
-          const int r = ew * 32 + lane;
-          const int grow = tm * kBM + r;
-          if (grow < p.M) {
-            float cnt = 0.f, mean = 0.f, m2 = 0.f;
-            for (int j = 0; j < p.tiles_n; ++j) {
-              const float2 pm = __ldcg(p.ln_stats + static_cast<long long>(j) * p.M + grow);
-              const float cj = static_cast<float>(min(BN, p.N - j * BN));
-              chan_merge(cnt, mean, m2, cj, pm.x, pm.y);
-            }
-            row_mean[r] = mean;
-            row_rstd[r] = rsqrtf(m2 / static_cast<float>(p.N) + p.eps);
-          }
-          named_bar_sync(1, 128);
-          // 2) normalise the 128-row block in place: warp ew sweeps rows ew*32..+31,
-          //    each lane 8 consecutive columns of every 256-column slab.
-          typedef unsigned short u16;
-          u16* outp = reinterpret_cast<u16*>(p.out);
-          for (int cb = 0; cb * 256 < p.N; ++cb) {
-            const int col = cb * 256 + lane * 8;
-            if (col < p.N) {
-              float g[8], b[8];
-#pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                g[e] = load_vec(p.gamma, p.vec_dtype, col + e);
-                b[e] = load_vec(p.beta, p.vec_dtype, col + e);
-              }
-#pragma unroll 4
-              for (int rr = 0; rr < 32; ++rr) {
-                const int lr = ew * 32 + rr;
-                const int gr = tm * kBM + lr;
-                if (gr < p.M) {
-                  uint4* addr = reinterpret_cast<uint4*>(outp + gr * p.ldo + col);
-                  uint4 y = __ldcg(addr);
-                  const float mu = row_mean[lr], rs = row_rstd[lr];
-                  uint32_t w[4] = {y.x, y.y, y.z, y.w};
-#pragma unroll
-                  for (int e = 0; e < 4; ++e) {
-                    const float2 f = unpack2<OUT_DT>(w[e]);
-                    w[e] = pack2<OUT_DT>(fmaf((f.x - mu) * rs, g[2 * e], b[2 * e]),
-                                         fmaf((f.y - mu) * rs, g[2 * e + 1], b[2 * e + 1]));
-                  }
-                  __stcg(addr, make_uint4(w[0], w[1], w[2], w[3]));
-                }
-              }
-            }
-          }
-          if (ew == 0 && lane == 0) p.ln_counters[tm] = 0;
-          named_bar_sync(1, 128);
-        }
+      }
+    }
+    if constexpr (LN) {
+      // Tell the normalizer warps there is no more work.
+      if (ew == 0 && lane == 0 && mbar_wait(bar_nempty + 8 * nq, nq_ph ^ 1, tmo, abort_flag)) {
+        norm_slot[nq] = -1;
+        mbar_arrive(bar_nfull + 8 * nq);
       }
     }
     if (!ok) {
@@ -611,6 +595,85 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
     }
     if (lane == 0) bulk_wait<0>();
     __syncwarp();
+  }
+
+  else if constexpr (LN) {
+    // ------------------------------------------------------------------ normalizer
+    // Four warps normalise queued 128-row blocks in place while the other roles keep
+    // computing tiles.  Warp nw owns rows nw*32..+31 of the block; its lanes cover 8
+    // consecutive columns of each 256-column slab and keep 16 rows of loads in flight.
+    const int nw = warp - (kFirstEpiWarp + kEpiWarps);  // 0..3
+    int nq = 0;
+    uint32_t nq_ph = 0;
+    typedef unsigned short u16;
+    u16* outp = reinterpret_cast<u16*>(p.out);
+    while (true) {
+      if (!mbar_wait(bar_nfull + 8 * nq, nq_ph, tmo, abort_flag)) {
+        if (!*abort_flag) {
+          record_error(p, kStatusTimeout, 0x40);
+          *abort_flag = 1;
+        }
+        break;
+      }
+      const int tm = norm_slot[nq];
+      if (tm < 0) break;
+      __threadfence();
+      // 1) this lane's row: merge the tiles_n slices' (mean, M2) into mean / rstd
+      const int r = nw * 32 + lane;
+      const int grow = tm * kBM + r;
+      if (grow < p.M) {
+        float cnt = 0.f, mean = 0.f, m2 = 0.f;
+        for (int j = 0; j < p.tiles_n; ++j) {
+          const float2 pm = __ldcg(p.ln_stats + static_cast<long long>(j) * p.M + grow);
+          chan_merge(cnt, mean, m2, static_cast<float>(min(BN, p.N - j * BN)), pm.x, pm.y);
+        }
+        row_mean[r] = mean;
+        row_rstd[r] = rsqrtf(m2 / static_cast<float>(p.N) + p.eps);
+      }
+      __syncwarp();
+      // 2) y = (x - mean) * rstd * gamma + beta over the warp's 32 rows
+      const int row_base = tm * kBM + nw * 32;
+      const int rows_here = min(32, p.M - row_base);
+      for (int cb = 0; cb * 256 < p.N; ++cb) {
+        const int col = cb * 256 + lane * 8;
+        if (col >= p.N) continue;
+        float g[8], b[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          g[e] = load_vec(p.gamma, p.vec_dtype, col + e);
+          b[e] = load_vec(p.beta, p.vec_dtype, col + e);
+        }
+        for (int r0 = 0; r0 < rows_here; r0 += 16) {
+          uint4 y[16];
+#pragma unroll
+          for (int u = 0; u < 16; ++u) {
+            if (r0 + u < rows_here)
+              y[u] = __ldcg(reinterpret_cast<const uint4*>(outp + (row_base + r0 + u) * p.ldo + col));
+          }
+#pragma unroll
+          for (int u = 0; u < 16; ++u) {
+            if (r0 + u < rows_here) {
+              const float mu = row_mean[nw * 32 + r0 + u], rs = row_rstd[nw * 32 + r0 + u];
+              uint32_t w[4] = {y[u].x, y[u].y, y[u].z, y[u].w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 f = unpack2<OUT_DT>(w[e]);
+                w[e] = pack2<OUT_DT>(fmaf((f.x - mu) * rs, g[2 * e], b[2 * e]),
+                                     fmaf((f.y - mu) * rs, g[2 * e + 1], b[2 * e + 1]));
+              }
+              __stcg(reinterpret_cast<uint4*>(outp + (row_base + r0 + u) * p.ldo + col),
+                     make_uint4(w[0], w[1], w[2], w[3]));
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_nempty + 8 * nq);
+      if (++nq == kNormSlots) {
+        nq = 0;
+        nq_ph ^= 1;
+      }
+    }
   }
 
   tc_fence_before();

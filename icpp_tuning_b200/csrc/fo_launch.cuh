@@ -3,6 +3,8 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include "fo_kernel.cuh"
 
 namespace fo {
@@ -18,10 +20,18 @@ struct LaunchArgs {
 template <int BN, int ACT, int OUT_DT, bool LN, bool CONV>
 cudaError_t launch_tc(const LaunchArgs& a) {
   auto kern = fo_tc_kernel<BN, ACT, OUT_DT, LN, CONV>;
-  // The attribute is per device; setting it on every call costs well under a microsecond.
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, a.smem);
-  if (e != cudaSuccess) return e;
-  kern<<<a.grid, CONV ? 288 : 192, a.smem, a.stream>>>(a.tmA, a.tmB, a.tmC, a.p);
+  // Opt in to the full 227 KB of dynamic shared memory once per device.
+  static std::atomic<uint64_t> opted{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  if ((opted.load(std::memory_order_acquire) & bit) == 0) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+    if (e != cudaSuccess) return e;
+    opted.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  constexpr int kThreads = LN ? 320 : (CONV ? 288 : 192);
+  kern<<<a.grid, kThreads, a.smem, a.stream>>>(a.tmA, a.tmB, a.tmC, a.p);
   return cudaGetLastError();
 }
 

@@ -62,9 +62,9 @@ def _stream(dev: torch.device, stream) -> int:
     return s.cuda_stream
 
 
-def default_config(M: int, N: int, K: int, epilogue: str = "none") -> N.FoTileCfg:
+def default_config(M: int, n: int, K: int, epilogue: str = "none") -> N.FoTileCfg:
     """A reasonable tile when the caller does not pass one (the autotuner picks better)."""
-    bn = 256 if N > 128 else (128 if N > 64 else 64)
+    bn = 256 if n > 128 else (128 if n > 64 else 64)
     stages = {256: 4, 128: 6, 64: 8}[bn]
     return N.tile_cfg(block_n=bn, stages=stages, group_m=0 if epilogue == "bias_layernorm" else 8)
 

@@ -1,0 +1,83 @@
+"""Y = LayerNorm_N(A @ B + bias) * gamma + beta (reference
+kernel/tilelang/gemm/gemm_bias_layernorm.py).
+
+The reference runs two kernels: a GEMM+bias writing fp32 to HBM (:52-90) and a
+standalone LayerNorm that reads it back twice (:93-164).  Here one persistent kernel
+does both: each epilogue thread owns one output row of a 128 x BN tile, computes the
+exact fp32 (mean, M2) of its row slice from TMEM, writes the biased tile once, and the
+last CTA to finish a 128-row block merges the slices' statistics (Chan et al.) and
+normalises the block in place while it is still in L2.
+
+Reference surface kept: get_gemm_configs(K), torch_baseline(...), build_fused_kernel(M,
+N, K, gemm_config=None, block_M_ln=16, block_N_ln=128, thread_num_ln=128, eps=1e-5) ->
+fused_kernel(A, B, bias, gamma, beta) -> Y, DESCRIPTOR.  block_M_ln / thread_num_ln
+configured the reference's separate LN kernel and are accepted and ignored; the
+reference's `N % block_N_ln == 0` assertion (:99) is kept.
+"""
+from __future__ import annotations
+
+from typing import Any, Dict, List, Optional
+
+import torch
+
+from .. import fused
+from ..autotuner.cost_model import make_matmul_spec
+from ..autotuner.interface import select_best
+from ..autotuner.tcgen05_space import Tcgen05Descriptor, tcgen05_configs
+from .gemm import _check_shape
+
+
+def torch_baseline(A, B, bias, gamma, beta):
+    """The reference's expected result (gemm_bias_layernorm.py:44-50), eager PyTorch."""
+    N = B.shape[1]
+    x = (A @ B).to(torch.float32) + bias.unsqueeze(0)
+    x = torch.nn.functional.layer_norm(x, (N,), weight=gamma.float(), bias=beta.float())
+    return x.to(torch.float16)
+
+
+def get_gemm_configs(K: int = 0) -> List[Dict[str, Any]]:
+    # The last CTA of a row block normalises it: row-major raster keeps a block's tiles
+    # in one wave, so group_m is 0.
+    return tcgen05_configs(group_ms=(0,))
+
+
+class GemmBiasLayerNormDescriptor(Tcgen05Descriptor):
+    @property
+    def name(self) -> str:
+        return "gemm_bias_layernorm"
+
+    def make_op_spec(self, raw_config=None, M=0, N=0, K=0, out_bytes: int = 2, **kw):
+        return make_matmul_spec(M=M, N=N, K=K, primitives=["bias_add", "row_layernorm"],
+                                output_element_bytes=out_bytes)
+
+    def get_raw_configs(self, K=0, **kw):
+        return get_gemm_configs(K)
+
+
+DESCRIPTOR = GemmBiasLayerNormDescriptor()
+
+
+def build_fused_kernel(M: int, N: int, K: int, gemm_config: Optional[Dict[str, Any]] = None,
+                       block_M_ln: int = 16, block_N_ln: int = 128, thread_num_ln: int = 128,
+                       eps: float = 1e-5, out_dtype: torch.dtype = torch.float16, b_layout: str = "kn",
+                       device: Optional[torch.device] = None):
+    """Returns fused_kernel(A, B, bias, gamma, beta) -> Y[M, N] (out_dtype, fp16 default
+    as in the reference).  The statistics workspace is allocated here, once, on `device`
+    (default: the current CUDA device), zeroed, and reused by every call; the kernel
+    leaves it zeroed.  Calls that share one built kernel must not overlap on the GPU."""
+    assert N % block_N_ln == 0, f"N={N} must be divisible by block_N_ln={block_N_ln}"
+    if gemm_config is None:
+        gemm_config, _ = select_best(DESCRIPTOR, M=M, N=N, K=K,
+                                     out_bytes=torch.empty((), dtype=out_dtype).element_size())
+    cfg = fused.as_tile_cfg(gemm_config)
+    dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+    ws = torch.zeros(max(16, fused.ln_workspace_bytes(M, N, cfg)), dtype=torch.uint8, device=dev)
+
+    def fused_kernel(A, B, bias, gamma, beta, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        _check_shape(A, B, M, N, K, b_layout)
+        return fused.gemm(A, B, b_layout=b_layout, epilogue="bias_layernorm", bias=bias, gamma=gamma,
+                          beta=beta, eps=eps, out=out, out_dtype=out_dtype, workspace=ws, config=cfg)
+
+    fused_kernel.config = gemm_config
+    fused_kernel.workspace = ws
+    return fused_kernel

@@ -1,0 +1,79 @@
+"""gemm + bias + LayerNorm fused kernel against the oracle, through the C ABI."""
+import pytest
+import torch
+
+from icpp_tuning_b200 import _native as N
+from icpp_tuning_b200 import fused
+from icpp_tuning_b200.gemm import gemm_bias_layernorm as gbln
+from oracle import ref_ops as R
+from tests.gpu_util import TOL_LN, assert_close, cuda, gen, randn, status_clean
+
+pytestmark = pytest.mark.gpu
+
+
+def _inputs(seed, M, Nn, K, dt=torch.bfloat16, layout="nk", shift=0.0):
+    g = gen(seed)
+    x = randn(g, M, K, dtype=dt)
+    w = randn(g, *((Nn, K) if layout == "nk" else (K, Nn)), dtype=dt, scale=K ** -0.5)
+    bias = randn(g, Nn, dtype=dt, scale=0.02, shift=shift)
+    gamma = randn(g, Nn, dtype=dt, scale=0.02, shift=1.0)
+    beta = randn(g, Nn, dtype=dt, scale=0.02)
+    return x, w, bias, gamma, beta
+
+
+@pytest.mark.parametrize("bn", [64, 128, 256])
+@pytest.mark.parametrize("odt", [torch.bfloat16, torch.float16])
+def test_ln_ragged(bn, odt):
+    M, Nn, K = 300, 1000, 192  # N not a multiple of BN, M not of 128
+    dt = odt
+    x, w, bias, gamma, beta = _inputs(10, M, Nn, K, dt)
+    cfg = N.tile_cfg(bn, {256: 4, 128: 6, 64: 8}[bn], 0)
+    ws = torch.zeros(fused.ln_workspace_bytes(M, Nn, cfg), dtype=torch.uint8, device="cuda")
+    for _ in range(3):  # the workspace must come back zeroed every call
+        out = fused.gemm(*cuda(x, w), b_layout="nk", epilogue="bias_layernorm", bias=bias.cuda(),
+                         gamma=gamma.cuda(), beta=beta.cuda(), workspace=ws, out_dtype=odt, config=cfg)
+        assert_close(out, R.gemm_bias_layernorm(x, w, bias, gamma, beta, b_layout="nk", out_dtype=odt), TOL_LN)
+        tiles_m = (M + 127) // 128
+        assert int(ws[: tiles_m * 4].view(torch.int32).abs().sum()) == 0
+    status_clean()
+
+
+def test_ln_large_mean_offset():
+    """Rows whose mean is far from zero: the centred (Chan) statistics stay accurate
+    where E[x^2] - E[x]^2 (the reference LN kernel, gemm_bias_layernorm.py:143) loses bits."""
+    M, Nn, K = 256, 2048, 256
+    x, w, bias, gamma, beta = _inputs(11, M, Nn, K, shift=30.0)
+    k = gbln.build_fused_kernel(M, Nn, K, out_dtype=torch.bfloat16, b_layout="nk")
+    out = k(*cuda(x, w, bias, gamma, beta))
+    ref = R.gemm_bias_layernorm(x, w, bias, gamma, beta, b_layout="nk", out_dtype=torch.float32, upcast=True)
+    assert_close(out, ref, TOL_LN)
+
+
+def test_reference_api_shape_and_assert():
+    with pytest.raises(AssertionError):
+        gbln.build_fused_kernel(128, 1000, 64, block_N_ln=128)
+    M, Nn, K = 64, 256, 128
+    g = gen(12)
+    A, B = randn(g, M, K, dtype=torch.float16), randn(g, K, Nn, dtype=torch.float16, scale=K ** -0.5)
+    bias, gamma, beta = (randn(g, Nn, dtype=torch.float16, scale=0.02),
+                         randn(g, Nn, dtype=torch.float16, scale=0.02, shift=1.0),
+                         randn(g, Nn, dtype=torch.float16, scale=0.02))
+    k = gbln.build_fused_kernel(M, Nn, K)  # reference defaults: fp16 out, B [K, N]
+    out = k(*cuda(A, B, bias, gamma, beta))
+    assert out.dtype == torch.float16
+    assert_close(out, R.gemm_bias_layernorm(A, B, bias, gamma, beta), TOL_LN)
+
+
+def test_config4_ln_full():
+    """Config 4: M=16384, K=4096, N=4096 bf16, X ~ N(0,1), W ~ N(0,1)/sqrt(K), seed 3."""
+    M, Nn, K = 16384, 4096, 4096
+    x, w, bias, gamma, beta = _inputs(3, M, Nn, K)
+    k = gbln.build_fused_kernel(M, Nn, K, out_dtype=torch.bfloat16, b_layout="nk")
+    out = k(*cuda(x, w, bias, gamma, beta))
+    rows = torch.arange(0, M, 97)
+    ref = R.gemm_bias_layernorm(x[rows], w, bias, gamma, beta, b_layout="nk", out_dtype=torch.bfloat16)
+    assert_close(out[rows.cuda()], ref, TOL_LN)
+    # every row normalised: mean ~ beta-mean, unit variance before the affine transform
+    y = (out.float() - beta.cuda().float()) / gamma.cuda().float()
+    assert y.mean(dim=1).abs().max() < 0.05 and (y.var(dim=1, unbiased=False) - 1).abs().max() < 0.05
+    status_clean()

@@ -1,0 +1,91 @@
+"""The sm_100a descriptors: every raw config is legal for the C ABI, the Python shared
+memory / TMEM model equals the library's, and the BASELINE shapes get a config."""
+import pytest
+
+from icpp_tuning_b200 import _native as N
+from icpp_tuning_b200.autotuner.cost_model import TuneConfig
+from icpp_tuning_b200.autotuner.gpu_spec import known_gpu
+from icpp_tuning_b200.autotuner.interface import rank_all, select_best
+from icpp_tuning_b200.autotuner import search_space as ss
+from icpp_tuning_b200.autotuner.tcgen05_space import smem_bytes, tcgen05_configs
+from icpp_tuning_b200.conv import conv2d, conv2d_relu
+from icpp_tuning_b200.gemm import gemm, gemm_bias_act, gemm_bias_layernorm
+
+B200 = known_gpu("B200")
+SHAPES = [
+    (gemm_bias_act.DESCRIPTOR, dict(M=1024, N=1024, K=1024)),
+    (gemm.DESCRIPTOR, dict(M=4096, N=4096, K=4096)),
+    (gemm_bias_act.DESCRIPTORS["gelu_tanh"], dict(M=8192, N=16384, K=4096)),
+    (gemm_bias_layernorm.DESCRIPTOR, dict(M=16384, N=4096, K=4096)),
+    (conv2d_relu.DESCRIPTOR, dict(N=256, C=128, H=28, W=28, OC=128, KH=3, KW=3, stride=1, padding=1)),
+]
+
+
+@pytest.mark.parametrize("conv", [False, True])
+def test_every_config_legal_for_the_library(conv):
+    for raw in tcgen05_configs(conv=conv, stages=range(2, 9)):
+        cfg = N.tile_cfg(block_n=raw["block_N"], stages=raw["num_stages"], group_m=raw["group_m"])
+        ok, why = N.config_legal(1 if conv else 0, N.FO_DT_BF16, cfg)
+        assert ok, why
+        assert N.config_smem_bytes(1 if conv else 0, N.FO_DT_BF16, cfg) == smem_bytes(raw["block_N"], raw["num_stages"])
+        tc = TuneConfig(128, raw["block_N"], 64, raw["num_stages"], raw["thread_num"] // 32, kind="tcgen05")
+        assert tc.shared_mem_bytes == smem_bytes(raw["block_N"], raw["num_stages"])
+        assert tc.is_valid_for_backend("tcgen05")
+
+
+def test_library_rejects_illegal_configs():
+    for bn, st, why in [(256, 5, "shared memory"), (96, 4, "block_n"), (128, 1, "stages"), (128, 9, "stages")]:
+        ok, msg = N.config_legal(0, N.FO_DT_BF16, N.tile_cfg(block_n=bn, stages=st))
+        assert not ok and why in msg
+    ok, msg = N.config_legal(0, N.FO_DT_BF16, N.tile_cfg(block_n=128, stages=4, block_m=64))
+    assert not ok and "block_m" in msg
+    ok, msg = N.config_legal(1, N.FO_DT_BF16, N.tile_cfg(block_n=128, stages=2))
+    assert not ok  # conv producer needs >= 3 stages
+
+
+@pytest.mark.parametrize("desc,shape", SHAPES, ids=lambda v: getattr(v, "name", ""))
+def test_baseline_shapes_select_legal(desc, shape):
+    raw, score = select_best(desc, hw=B200, **shape)
+    assert 0.0 < score <= 1.0
+    op = 1 if "conv" in desc.name else 0
+    ok, why = N.config_legal(op, N.FO_DT_BF16, N.tile_cfg(block_n=raw["block_N"], stages=raw["num_stages"],
+                                                          group_m=raw["group_m"]))
+    assert ok, why
+    rk = rank_all(desc, hw=B200, detailed=True, **shape)
+    assert rk[0]["score"] == score
+    assert rk[0]["detail"]["projection"]["predicted_tflops"] > 0
+
+
+def test_layernorm_configs_use_row_major_raster():
+    assert {c["group_m"] for c in gemm_bias_layernorm.get_gemm_configs(4096)} == {0}
+
+
+def test_search_space_tcgen05_prunes_to_library_legal():
+    space = ss.generate_search_space("matmul", B200, backend="tcgen05", mode="exhaustive")
+    assert space
+    for c in space:
+        ok, why = N.config_legal(0, N.FO_DT_BF16, N.tile_cfg(block_n=c.block_N, stages=c.num_stages,
+                                                              group_m=c.group_size_m))
+        assert ok, why
+    full = ss.generate_exhaustive_configs("matmul", "tcgen05")
+    assert len(full) > len(space)  # some stage counts exceed 227 KB
+
+
+def test_search_space_legacy_backends_run():
+    # The reference's generate_search_space raises AttributeError (search_space.py:194).
+    a100 = known_gpu("A100")
+    for backend in ("tilelang", "triton"):
+        for op in ("matmul", "conv2d"):
+            space = ss.generate_search_space(op, a100, backend=backend, mode="exhaustive")
+            assert space and all(c.is_valid_for_backend(backend) for c in space)
+    cold = ss.generate_search_space("matmul", a100, backend="tilelang", mode="cold", seed=0)
+    assert cold
+
+
+def test_lcm_marginal_uniformity():
+    pools = {"a": [1, 2, 3], "b": [10, 20], "c": [7, 8, 9, 10]}
+    cfgs = ss.lcm_marginal_sample(pools, seed=1)
+    assert len(cfgs) == 12
+    for k, vals in pools.items():
+        counts = {v: sum(1 for c in cfgs if c[k] == v) for v in vals}
+        assert len(set(counts.values())) == 1
