@@ -268,76 +268,109 @@ def _cpu_name() -> str:
     return "unknown"
 
 
-def per_op_table(args) -> list:
-    """Device-timed TFLOP/s of all five BASELINE workloads (config 2 is the headline)."""
+def workloads(dev) -> dict:
+    """The five BASELINE workloads: name -> (builder, FLOPs).  A builder allocates the
+    seeded inputs on `dev` and returns a zero-argument callable running one step."""
     from icpp_tuning_b200.conv import conv2d_relu
-    from icpp_tuning_b200.gemm import gemm_bias_act, gemm_bias_layernorm
+    from icpp_tuning_b200.gemm import gemm, gemm_bias_act, gemm_bias_layernorm
 
+    def c1():
+        g = torch.Generator().manual_seed(0)
+        a = (torch.rand(1024, 1024, generator=g) * 2 - 1).half().to(dev)
+        b = (torch.rand(1024, 1024, generator=g) * 2 - 1).half().to(dev)
+        bias = (torch.randn(1024, generator=g) * 0.1).half().to(dev)
+        k = gemm_bias_act.build_kernel(1024, 1024, 1024, act="relu", out_dtype=torch.float16)
+        return lambda: k(a, b, bias)
+
+    def c2():
+        a, bt = (t.to(dev) for t in _inputs(1, 0))
+        k = gemm.build_kernel(4096, 4096, 4096, out_dtype=torch.bfloat16, b_layout="nk")
+        return lambda: k(a, bt)
+
+    def c3():
+        g = torch.Generator().manual_seed(2)
+        x = torch.randn(8192, 4096, generator=g).bfloat16().to(dev)
+        w = (torch.randn(16384, 4096, generator=g) * 0.02).bfloat16().to(dev)
+        bias = (torch.randn(16384, generator=g) * 0.02).bfloat16().to(dev)
+        k = gemm_bias_act.build_kernel(8192, 16384, 4096, act="gelu_tanh", out_dtype=torch.bfloat16, b_layout="nk")
+        return lambda: k(x, w, bias)
+
+    def c4():
+        g = torch.Generator().manual_seed(3)
+        x = torch.randn(16384, 4096, generator=g).bfloat16().to(dev)
+        w = (torch.randn(4096, 4096, generator=g) / 64).bfloat16().to(dev)
+        bias = (torch.randn(4096, generator=g) * 0.02).bfloat16().to(dev)
+        gam = (1 + torch.randn(4096, generator=g) * 0.02).bfloat16().to(dev)
+        bet = (torch.randn(4096, generator=g) * 0.02).bfloat16().to(dev)
+        k = gemm_bias_layernorm.build_fused_kernel(16384, 4096, 4096, out_dtype=torch.bfloat16, b_layout="nk")
+        return lambda: k(x, w, bias, gam, bet)
+
+    def c5():
+        g = torch.Generator().manual_seed(4)
+        x = torch.randn(256, 28, 28, 128, generator=g).bfloat16().to(dev)
+        wt = (torch.randn(3, 3, 128, 128, generator=g) / (9 * 128) ** 0.5).bfloat16().to(dev)
+        bias = (torch.randn(128, generator=g) * 0.1).bfloat16().to(dev)
+        y = torch.empty(256, 28, 28, 128, dtype=torch.bfloat16, device=dev)
+        k = conv2d_relu.build_conv2d_relu_kernel(256, 128, 28, 28, 128, 3, 3, 1, 1, 1)
+        return lambda: k(x, wt, y, bias=bias)
+
+    return {
+        "config1": ("gemm_bias_relu 1024^3 fp16", c1, 2.0 * 1024 ** 3),
+        "config2": ("gemm 4096^3 bf16", c2, 2.0 * 4096 ** 3),
+        "config3": ("gemm_bias_gelu_tanh 8192x16384x4096 bf16", c3, 2.0 * 8192 * 16384 * 4096),
+        "config4": ("gemm_bias_layernorm 16384x4096x4096 bf16", c4, 2.0 * 16384 * 4096 * 4096),
+        "config5": ("conv2d_bias_relu 256x28x28x128->128 3x3 bf16", c5, 2.0 * 256 * 28 * 28 * 128 * 128 * 9),
+    }
+
+
+def time_steps(fn, steps: int, flush) -> float:
+    """Mean device ms of fn over `steps`, L2 flushed and the queue padded before each."""
+    tot = 0.0
+    for _ in range(steps):
+        flush.zero_()
+        torch.cuda._sleep(QUEUE_PAD_CYCLES)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        e.synchronize()
+        tot += s.elapsed_time(e)
+    return tot / steps
+
+
+def per_op_table(args) -> list:
+    """Device-timed TFLOP/s of all five BASELINE workloads (config2 is the headline)."""
     dev = torch.device("cuda", torch.cuda.current_device())
     peak = _peaks()[0]
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    steps = max(5, min(args.steps, 20))
     res = []
-
-    def timeit(name, fn, flops, steps):
+    for key, (name, build, flops) in workloads(dev).items():
+        fn = build()
         for _ in range(3):
             fn()
         torch.cuda.synchronize()
-        tot = 0.0
-        for _ in range(steps):
-            flush.zero_()
-            torch.cuda._sleep(QUEUE_PAD_CYCLES)
-            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s.record()
-            fn()
-            e.record()
-            e.synchronize()
-            tot += s.elapsed_time(e)
-        ms = tot / steps
+        ms = time_steps(fn, steps, flush)
         tf = flops / (ms / 1e3) / 1e12
-        res.append({"op": name, "ms": round(ms, 5), "tflops": round(tf, 2), "frac_measured": round(tf / peak, 4),
-                    "frac_nominal": round(tf / 2250.0, 4)})
-
-    steps = max(5, min(args.steps, 20))
-    g = torch.Generator().manual_seed(0)
-    a = (torch.rand(1024, 1024, generator=g) * 2 - 1).half().to(dev)
-    b = (torch.rand(1024, 1024, generator=g) * 2 - 1).half().to(dev)
-    bias = (torch.randn(1024, generator=g) * 0.1).half().to(dev)
-    k1 = gemm_bias_act.build_kernel(1024, 1024, 1024, act="relu", out_dtype=torch.float16)
-    timeit("config1 gemm_bias_relu 1024^3 fp16", lambda: k1(a, b, bias), 2.0 * 1024 ** 3, steps)
-    del a, b
-    ah, bth = _inputs(1, 0)
-    a, bt = ah.to(dev), bth.to(dev)
-    from icpp_tuning_b200.gemm import gemm
-    k2 = gemm.build_kernel(4096, 4096, 4096, out_dtype=torch.bfloat16, b_layout="nk")
-    timeit("config2 gemm 4096^3 bf16", lambda: k2(a, bt), 2.0 * 4096 ** 3, steps)
-    del a, bt
-    g = torch.Generator().manual_seed(2)
-    x = torch.randn(8192, 4096, generator=g).bfloat16().to(dev)
-    w = (torch.randn(16384, 4096, generator=g) * 0.02).bfloat16().to(dev)
-    bias = (torch.randn(16384, generator=g) * 0.02).bfloat16().to(dev)
-    k3 = gemm_bias_act.build_kernel(8192, 16384, 4096, act="gelu_tanh", out_dtype=torch.bfloat16, b_layout="nk")
-    timeit("config3 gemm_bias_gelu_tanh 8192x16384x4096 bf16", lambda: k3(x, w, bias), 2.0 * 8192 * 16384 * 4096,
-           steps)
-    del x, w
-    g = torch.Generator().manual_seed(3)
-    x = torch.randn(16384, 4096, generator=g).bfloat16().to(dev)
-    w = (torch.randn(4096, 4096, generator=g) / 64).bfloat16().to(dev)
-    bias = (torch.randn(4096, generator=g) * 0.02).bfloat16().to(dev)
-    gam = (1 + torch.randn(4096, generator=g) * 0.02).bfloat16().to(dev)
-    bet = (torch.randn(4096, generator=g) * 0.02).bfloat16().to(dev)
-    k4 = gemm_bias_layernorm.build_fused_kernel(16384, 4096, 4096, out_dtype=torch.bfloat16, b_layout="nk")
-    timeit("config4 gemm_bias_layernorm 16384x4096x4096 bf16", lambda: k4(x, w, bias, gam, bet),
-           2.0 * 16384 * 4096 * 4096, steps)
-    del x, w
-    g = torch.Generator().manual_seed(4)
-    x = torch.randn(256, 28, 28, 128, generator=g).bfloat16().to(dev)
-    wt = (torch.randn(3, 3, 128, 128, generator=g) / (9 * 128) ** 0.5).bfloat16().to(dev)
-    bias = (torch.randn(128, generator=g) * 0.1).bfloat16().to(dev)
-    y = torch.empty(256, 28, 28, 128, dtype=torch.bfloat16, device=dev)
-    k5 = conv2d_relu.build_conv2d_relu_kernel(256, 128, 28, 28, 128, 3, 3, 1, 1, 1)
-    timeit("config5 conv2d_bias_relu 256x28x28x128->128 3x3 bf16", lambda: k5(x, wt, y, bias=bias),
-           2.0 * 256 * 28 * 28 * 128 * 128 * 9, steps)
+        res.append({"op": f"{key} {name}", "ms": round(ms, 5), "tflops": round(tf, 2),
+                    "frac_measured": round(tf / peak, 4), "frac_nominal": round(tf / 2250.0, 4)})
+        del fn
+        torch.cuda.empty_cache()
     return res
+
+
+def profile_op(args):
+    """--profile --op configN: W warm-up steps then K timed steps of one workload, for ncu."""
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    name, build, flops = workloads(dev)[args.op]
+    fn = build()
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    ms = time_steps(fn, args.steps, flush)
+    print(json.dumps({"profile_run": args.op, "workload": name, "ms": ms, "tflops": flops / (ms / 1e3) / 1e12}))
 
 
 def run_reference(args):
@@ -381,6 +414,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--no-ops", action="store_true", help="skip the per-op table of all five workloads")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
+    ap.add_argument("--op", default="config2", choices=["config1", "config2", "config3", "config4", "config5"],
+                    help="with --profile: the workload to run")
     ap.add_argument("--profile", action="store_true",
                     help="timed steps only (no e2e, CPU baseline, per-op table or clock hold): for ncu")
     args = ap.parse_args()
@@ -388,6 +423,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.profile and args.op != "config2":
+        profile_op(args)
     else:
         run_ours(args)
 

@@ -164,7 +164,7 @@ size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 size_t ln_workspace(int64_t M, int64_t N, int bn) {
   const int64_t tiles_m = (M + 127) / 128;
   const int64_t tiles_n = (N + bn - 1) / bn;
-  return round_up(static_cast<size_t>(tiles_m) * 4, 256) + static_cast<size_t>(tiles_n * M) * 8;
+  return round_up(static_cast<size_t>(tiles_m) * 4, 256) + static_cast<size_t>(tiles_n * M) * 16;
 }
 
 void fill_common(fo::KParams& p, const DevInfo& di) {
@@ -288,7 +288,7 @@ int fo_gemm(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
   p.ldo = d->ldo;
   if (ln) {
     p.ln_counters = static_cast<int*>(d->workspace);
-    p.ln_stats = reinterpret_cast<float2*>(static_cast<char*>(d->workspace) +
+    p.ln_stats = reinterpret_cast<float4*>(static_cast<char*>(d->workspace) +
                                            round_up(static_cast<size_t>(p.tiles_m) * 4, 256));
   }
   fill_common(p, di);

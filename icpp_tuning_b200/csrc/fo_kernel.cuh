@@ -57,7 +57,7 @@ struct KParams {
   const void* beta;
   int vec_dtype;
   float eps;
-  float2* ln_stats;  // [tiles_n][M] (mean, M2) of each row over one N tile
+  float4* ln_stats;  // [tiles_n][M] (mean, M2, shift, 0) of each row over one N tile
   int* ln_counters;  // [tiles_m] finished-tile counters, self-resetting
   void* out;
   long long ldo;
@@ -453,6 +453,7 @@ __global__ void __launch_bounds__(LN ? 320 : (CONV ? 288 : 192), 1)
       const int row0 = tm * kBM + quarter * 32;
       const int col0 = tn * BN;
       float st_cnt = 0.f, st_mean = 0.f, st_m2 = 0.f;
+      float shift = 0.f;  // LayerNorm: the tile is stored centred on its first chunk's mean
 #pragma unroll 1
       for (int c = 0; c < kChunks; ++c) {
         const int cbase = col0 + c * kCPC;
@@ -502,7 +503,12 @@ __global__ void __launch_bounds__(LN ? 320 : (CONV ? 288 : 192), 1)
               q += (i < cv) ? d * d : 0.f;
             }
             chan_merge(st_cnt, st_mean, st_m2, static_cast<float>(cv), cm, q);
+            if (c == 0) shift = cm;
           }
+          // Store x - shift: the bf16/fp16 rounding then scales with the row's spread,
+          // not with its mean; the normaliser adds (shift - row mean) back in fp32.
+#pragma unroll
+          for (int i = 0; i < kCPC; ++i) v[i] -= shift;
         }
         // Stage the 32 x 128 B block in swizzled shared memory, then TMA-store it.
         const uint32_t buf = buf0 + (nstore & 1) * kEpiBufBytes;
@@ -543,7 +549,7 @@ __global__ void __launch_bounds__(LN ? 320 : (CONV ? 288 : 192), 1)
       if constexpr (LN) {
         // Per-tile row statistics, then the row-block completion protocol.
         const int row = row0 + lane;
-        if (row < p.M) p.ln_stats[static_cast<long long>(tn) * p.M + row] = make_float2(st_mean, st_m2);
+        if (row < p.M) p.ln_stats[static_cast<long long>(tn) * p.M + row] = make_float4(st_mean, st_m2, shift, 0.f);
         if (lane == 0) {
           bulk_wait<0>();
           fence_proxy_async_global();
@@ -624,7 +630,7 @@ __global__ void __launch_bounds__(LN ? 320 : (CONV ? 288 : 192), 1)
       if (grow < p.M) {
         float cnt = 0.f, mean = 0.f, m2 = 0.f;
         for (int j = 0; j < p.tiles_n; ++j) {
-          const float2 pm = __ldcg(p.ln_stats + static_cast<long long>(j) * p.M + grow);
+          const float4 pm = __ldcg(p.ln_stats + static_cast<long long>(j) * p.M + grow);
           chan_merge(cnt, mean, m2, static_cast<float>(min(BN, p.N - j * BN)), pm.x, pm.y);
         }
         row_mean[r] = mean;
@@ -643,23 +649,27 @@ __global__ void __launch_bounds__(LN ? 320 : (CONV ? 288 : 192), 1)
           g[e] = load_vec(p.gamma, p.vec_dtype, col + e);
           b[e] = load_vec(p.beta, p.vec_dtype, col + e);
         }
+        const float4* tile_stats = p.ln_stats + static_cast<long long>(col / BN) * p.M;
         for (int r0 = 0; r0 < rows_here; r0 += 16) {
           uint4 y[16];
+          float sh[16];
 #pragma unroll
           for (int u = 0; u < 16; ++u) {
-            if (r0 + u < rows_here)
+            if (r0 + u < rows_here) {
               y[u] = __ldcg(reinterpret_cast<const uint4*>(outp + (row_base + r0 + u) * p.ldo + col));
+              sh[u] = __ldcg(tile_stats + row_base + r0 + u).z;
+            }
           }
 #pragma unroll
           for (int u = 0; u < 16; ++u) {
             if (r0 + u < rows_here) {
-              const float mu = row_mean[nw * 32 + r0 + u], rs = row_rstd[nw * 32 + r0 + u];
+              const float off = sh[u] - row_mean[nw * 32 + r0 + u], rs = row_rstd[nw * 32 + r0 + u];
               uint32_t w[4] = {y[u].x, y[u].y, y[u].z, y[u].w};
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
                 const float2 f = unpack2<OUT_DT>(w[e]);
-                w[e] = pack2<OUT_DT>(fmaf((f.x - mu) * rs, g[2 * e], b[2 * e]),
-                                     fmaf((f.y - mu) * rs, g[2 * e + 1], b[2 * e + 1]));
+                w[e] = pack2<OUT_DT>(fmaf((f.x + off) * rs, g[2 * e], b[2 * e]),
+                                     fmaf((f.y + off) * rs, g[2 * e + 1], b[2 * e + 1]));
               }
               __stcg(reinterpret_cast<uint4*>(outp + (row_base + r0 + u) * p.ldo + col),
                      make_uint4(w[0], w[1], w[2], w[3]));

@@ -70,8 +70,8 @@ def test_gemm_layernorm_needs_workspace():
     d = _desc(epilogue=N.FO_EPI_BIAS_LN, bias=1 << 20, gamma=1 << 20, beta=1 << 20)
     assert _call(d) == N.FO_EINVAL and "workspace" in N.last_error()
     need = N.lib().fo_gemm_workspace_size(ctypes.byref(d), ctypes.byref(N.tile_cfg(256, 4, 0)))
-    # counters for 2 row blocks padded to 256 B + (mean, M2) per row per N tile
-    assert need == 256 + 256 * 1 * 8
+    # counters for 2 row blocks padded to 256 B + (mean, M2, shift, pad) per row per N tile
+    assert need == 256 + 256 * 1 * 16
 
 
 def test_gemm_bad_config():
