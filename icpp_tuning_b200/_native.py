@@ -24,12 +24,14 @@ FO_DT_F16, FO_DT_BF16, FO_DT_F32 = 0, 1, 2
 FO_B_KN, FO_B_NK = 0, 1
 (FO_EPI_NONE, FO_EPI_BIAS, FO_EPI_BIAS_RELU, FO_EPI_BIAS_GELU_TANH, FO_EPI_BIAS_GELU_ERF,
  FO_EPI_BIAS_LN, FO_EPI_RELU) = range(7)
+FO_NOALLOC_LN_SCRATCH_BYTES = 8 << 20
 
 # Every symbol include/b200fo.h declares; tests check the library exports all of them.
 EXPORTED = (
     "fo_gemm", "fo_gemm_workspace_size", "fo_conv2d", "fo_query_config_legal",
     "fo_config_smem_bytes", "fo_device_status", "fo_set_wait_timeout_ns",
     "fo_selftest_wait_timeout", "fo_last_error", "fo_version", "fo_launch_count",
+    "fo_gemm_bias_layernorm_noalloc",
 )
 
 
@@ -75,6 +77,8 @@ def _declare(l: ctypes.CDLL) -> None:
     P = ctypes.POINTER
     l.fo_gemm.argtypes = [P(FoGemmDesc), P(FoTileCfg), ctypes.c_void_p]
     l.fo_gemm.restype = ctypes.c_int
+    l.fo_gemm_bias_layernorm_noalloc.argtypes = [P(FoGemmDesc), P(FoTileCfg), ctypes.c_void_p]
+    l.fo_gemm_bias_layernorm_noalloc.restype = ctypes.c_int
     l.fo_gemm_workspace_size.argtypes = [P(FoGemmDesc), P(FoTileCfg)]
     l.fo_gemm_workspace_size.restype = ctypes.c_size_t
     l.fo_conv2d.argtypes = [P(FoConvDesc), P(FoTileCfg), ctypes.c_void_p]

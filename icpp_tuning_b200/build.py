@@ -20,7 +20,7 @@ INCLUDE = ROOT / "include"
 LIB = PKG / "libb200fo.so"
 OBJ = PKG / "_build"
 
-SOURCES = ["fo_api.cu", "fo_family_gemm.cu", "fo_family_ln.cu", "fo_family_conv.cu"]
+SOURCES = ["fo_api.cu", "fo_family_gemm.cu", "fo_family_ln.cu", "fo_family_conv.cu", "fo_noalloc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-O3",
          "--expt-relaxed-constexpr", f"-I{INCLUDE}", f"-I{CSRC}"]

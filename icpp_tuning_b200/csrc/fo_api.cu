@@ -174,6 +174,11 @@ void fill_common(fo::KParams& p, const DevInfo& di) {
 
 }  // namespace
 
+void fo::set_last_error(int code, const char* msg) {
+  g_err = msg != nullptr ? msg : "";
+  g_err_code = code;
+}
+
 extern "C" {
 
 const char* fo_version(void) { return "b200fo 0.1.0 sm_100a abi 1"; }

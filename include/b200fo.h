@@ -145,6 +145,21 @@ int fo_selftest_wait_timeout(uint64_t timeout_ns, void* stream);
 /* Message of the last failure on this host thread (copied into buf); returns its code. */
 int fo_last_error(char* buf, size_t len);
 
+/* Scratch held by fo_gemm_bias_layernorm_noalloc on every GPU that loads the library. */
+#define FO_NOALLOC_LN_SCRATCH_BYTES (8u << 20)
+
+/* No counterpart in the reference.  fo_gemm with FO_EPI_BIAS_LN for callers that cannot
+ * allocate device memory -- e.g. a serving process that reserves its whole memory budget
+ * at start-up, or a plugin interface that passes inputs and outputs but no allocator.
+ * Same arguments and result as fo_gemm (desc->workspace is ignored); the LayerNorm
+ * statistics live in a static __device__ array of FO_NOALLOC_LN_SCRATCH_BYTES per GPU
+ * instead, and nothing is allocated: no cudaMalloc, no cudaFree.  Problems needing more
+ * scratch (fo_gemm_workspace_size > FO_NOALLOC_LN_SCRATCH_BYTES) fail with FO_EINVAL.
+ * The first call on a device looks up the array's address (make it before any stream
+ * capture).  All calls share the array: calls that overlap on the GPU race and must be
+ * serialised.  Wait timeouts go to a private status word, not fo_device_status. */
+int fo_gemm_bias_layernorm_noalloc(const FoGemmDesc* desc, const FoTileCfg* cfg, void* stream);
+
 /* Library version string, e.g. "b200fo 0.1.0 sm_100a abi 1". */
 const char* fo_version(void);
 
