@@ -262,7 +262,7 @@ int fo_gemm(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
     if (d->N % 8 != 0) return fail(FO_EINVAL, "LayerNorm needs N %% 8 == 0, got N=%lld", (long long)d->N);
     const size_t need = ln_workspace(d->M, d->N, cfg->block_n);
     if (d->workspace == nullptr || d->workspace_bytes < need || !aligned16(d->workspace))
-      return fail(FO_EINVAL, "LayerNorm needs a zero-initialised, 16-byte aligned workspace of %zu bytes", need);
+      return fail(FO_EINVAL, "LayerNorm needs a 16-byte aligned workspace of %zu bytes", need);
     if (!(d->eps >= 0.0f)) return fail(FO_EINVAL, "eps must be >= 0");
   }
   DevInfo di;
@@ -279,7 +279,7 @@ int fo_gemm(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
   p.tiles_n = (p.N + bn - 1) / bn;
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.k_blocks = (p.K + 63) / 64;
-  p.group_m = ln ? 0 : cfg->group_m;
+  p.group_m = cfg->group_m;
   p.stages = cfg->stages;
   p.ab_bf16 = d->in_dtype == FO_DT_BF16;
   p.b_mn = d->b_layout == FO_B_KN;
@@ -292,7 +292,6 @@ int fo_gemm(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
   p.out = d->out;
   p.ldo = d->ldo;
   if (ln) {
-    p.ln_counters = static_cast<int*>(d->workspace);
     p.ln_stats = reinterpret_cast<float4*>(static_cast<char*>(d->workspace) +
                                            round_up(static_cast<size_t>(p.tiles_m) * 4, 256));
   }
@@ -315,7 +314,7 @@ int fo_gemm(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
   const int out_dt = d->out_dtype == FO_DT_F16 ? fo::DT_F16 : d->out_dtype == FO_DT_BF16 ? fo::DT_BF16 : fo::DT_F32;
   cudaError_t e = ln ? fo::launch_ln_family(bn, out_dt, la) : fo::launch_gemm_family(bn, act, out_dt, la);
   if (e != cudaSuccess) return fail(FO_ECUDA, "kernel launch failed: %s", cudaGetErrorString(e));
-  g_launches.fetch_add(1);
+  g_launches.fetch_add(ln ? 2 : 1);  // LayerNorm: GEMM kernel + normalisation kernel
   return ok();
 }
 

@@ -1,13 +1,24 @@
-// Instantiations of the GEMM + bias + LayerNorm kernels (16-bit outputs).
+// Instantiations of the GEMM + bias + LayerNorm kernels (16-bit outputs): the tcgen05
+// kernel writes the biased rows and per-slice statistics, fo_ln_normalize_kernel follows.
 #include "fo_launch.cuh"
 
 namespace fo {
 
+// GEMM + bias + slice statistics, then the stream-ordered normalisation pass.
+template <int BN, int OUT>
+static cudaError_t gemm_then_normalize(const LaunchArgs& a) {
+  cudaError_t e = launch_tc<BN, ACT_NONE, OUT, true, false>(a);
+  if (e != cudaSuccess) return e;
+  const int blocks = (a.p.M + 7) / 8;
+  fo_ln_normalize_kernel<OUT><<<blocks, 256, 0, a.stream>>>(a.p, BN);
+  return cudaGetLastError();
+}
+
 template <int BN>
 static cudaError_t by_out(int out_dt, const LaunchArgs& a) {
   switch (out_dt) {
-    case DT_F16: return launch_tc<BN, ACT_NONE, DT_F16, true, false>(a);
-    case DT_BF16: return launch_tc<BN, ACT_NONE, DT_BF16, true, false>(a);
+    case DT_F16: return gemm_then_normalize<BN, DT_F16>(a);
+    case DT_BF16: return gemm_then_normalize<BN, DT_BF16>(a);
   }
   return cudaErrorInvalidValue;
 }

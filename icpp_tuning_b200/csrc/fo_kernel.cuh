@@ -14,9 +14,9 @@
 //               tcgen05.ld, apply bias / activation in fp32, convert, stage 32 x 128 B
 //               blocks in 128B-swizzled shared memory and write them with TMA stores.
 //               For LayerNorm each thread owns one output row, so exact per-row
-//               (mean, M2) of the fp32 tile is a register reduction; the last CTA to
-//               finish a 128-row block (global counter) merges the per-tile statistics
-//               (Chan et al.) and normalises the block in place.
+//               (mean, M2) of the fp32 tile slice is a register reduction; the slice
+//               is stored centred on a shift and fo_ln_normalize_kernel (next on the
+//               stream) merges the slices' statistics (Chan et al.) and normalises.
 // Every wait is bounded (mbar_wait); a wait that runs out records FO_ETIMEOUT in the
 // device status word, raises a CTA-local abort flag, drains its in-flight copies and
 // returns.
@@ -38,7 +38,6 @@ constexpr int kEpiWarps = 4;
 constexpr int kEpiBufBytes = 32 * 128;
 constexpr int kEpiBytes = kEpiWarps * 2 * kEpiBufBytes;
 constexpr int kMiscBytes = 1536;
-constexpr int kNormSlots = 4;  // LayerNorm: row blocks queued for the normalizer warps
 constexpr int kMaxStages = 8;
 
 // Status codes written into the device status word (first writer wins).
@@ -58,7 +57,6 @@ struct KParams {
   int vec_dtype;
   float eps;
   float4* ln_stats;  // [tiles_n][M] (mean, M2, shift, 0) of each row over one N tile
-  int* ln_counters;  // [tiles_m] finished-tile counters, self-resetting
   void* out;
   long long ldo;
   int* status;  // [0] = code, [1] = where, [2] = block
@@ -178,7 +176,7 @@ __device__ __forceinline__ void drain_loads(uint32_t bar_full, int stages, int i
 }
 
 template <int BN, int ACT, int OUT_DT, bool LN, bool CONV>
-__global__ void __launch_bounds__(LN ? 320 : (CONV ? 288 : 192), 1)
+__global__ void __launch_bounds__(CONV ? 288 : 192, 1)
     fo_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const __grid_constant__ CUtensorMap tmC, const KParams p) {
   constexpr int kProducerWarps = CONV ? 4 : 1;
@@ -200,22 +198,15 @@ __global__ void __launch_bounds__(LN ? 320 : (CONV ? 288 : 192), 1)
   const uint32_t sEpi = sB + stages * kBStage;
   uint8_t* misc = smem + (sEpi - sA) + kEpiBytes;
   // misc: [0,64) full[8] | [64,128) empty[8] | [128,144) tfull[2] | [144,160) tempty[2]
-  //       | [160,168) drain | [168,200) norm_full[4] | [200,232) norm_empty[4]
-  //       | [232,248) norm_slot[4] | [248,264) tmem addr + flags | [512,1536) row stats
+  //       | [160,168) drain | [248,256) tmem addr + abort flag
   const uint32_t mb = smem_u32(misc);
   const uint32_t bar_full = mb;
   const uint32_t bar_empty = mb + 64;
   const uint32_t bar_tfull = mb + 128;
   const uint32_t bar_tempty = mb + 144;
   const uint32_t bar_drain = mb + 160;
-  const uint32_t bar_nfull = mb + 168;
-  const uint32_t bar_nempty = mb + 200;
-  volatile int* norm_slot = reinterpret_cast<volatile int*>(misc + 232);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 248);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 252);
-  volatile int* epi_stop = reinterpret_cast<volatile int*>(misc + 256);
-  float* row_mean = reinterpret_cast<float*>(misc + 512);
-  float* row_rstd = reinterpret_cast<float*>(misc + 1024);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -230,12 +221,7 @@ __global__ void __launch_bounds__(LN ? 320 : (CONV ? 288 : 192), 1)
       mbar_init(bar_tempty + 8 * a, kEpiWarps);
     }
     mbar_init(bar_drain, 1);
-    for (int q = 0; q < kNormSlots; ++q) {
-      mbar_init(bar_nfull + 8 * q, 1);
-      mbar_init(bar_nempty + 8 * q, 4);
-    }
     *abort_flag = 0;
-    *epi_stop = 0;
     fence_mbar_init();
   }
   if (warp == kMmaWarp) {
@@ -436,18 +422,12 @@ __global__ void __launch_bounds__(LN ? 320 : (CONV ? 288 : 192), 1)
     uint32_t acc_ph = 0;
     uint32_t nstore = 0;
     bool ok = true;
-    int nq = 0;  // LayerNorm hand-off ring position (used by thread ew == 0, lane == 0)
-    uint32_t nq_ph = 0;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
       int tm, tn;
       tile_coords(p, t, tm, tn);
       if (!mbar_wait(bar_tfull + 8 * acc, acc_ph, tmo, abort_flag)) {
         ok = false;
-        *abort_flag = 1;
-        // Without LayerNorm the four warps are independent and this one can stop.  With
-        // LayerNorm they meet at named barriers, so it runs the tile to the next barrier
-        // and all four stop together on the snapshot taken there.
-        if constexpr (!LN) break;
+        break;
       }
       tc_fence_after();
       const int row0 = tm * kBM + quarter * 32;
@@ -547,52 +527,10 @@ __global__ void __launch_bounds__(LN ? 320 : (CONV ? 288 : 192), 1)
       if (acc == 0) acc_ph ^= 1;
 
       if constexpr (LN) {
-        // Per-tile row statistics, then the row-block completion protocol.
+        // Per-tile row statistics; fo_ln_normalize_kernel (launched next on the same
+        // stream) merges them and normalises every row in place.
         const int row = row0 + lane;
         if (row < p.M) p.ln_stats[static_cast<long long>(tn) * p.M + row] = make_float4(st_mean, st_m2, shift, 0.f);
-        if (lane == 0) {
-          bulk_wait<0>();
-          fence_proxy_async_global();
-        }
-        __threadfence();
-        __syncwarp();
-        named_bar_sync(1, 128);
-        if (ew == 0 && lane == 0) {
-          int stop = *abort_flag;
-          if (!stop) {
-            __threadfence();
-            const int old = atomicAdd(p.ln_counters + tm, 1);
-            if (old == p.tiles_n - 1) {
-              // Last tile of this 128-row block: every slice's statistics and biased
-              // values are in memory.  Reset the counter for the next launch and queue
-              // the block for this CTA's normalizer warps.
-              __threadfence();
-              p.ln_counters[tm] = 0;
-              if (mbar_wait(bar_nempty + 8 * nq, nq_ph ^ 1, tmo, abort_flag)) {
-                norm_slot[nq] = tm;
-                mbar_arrive(bar_nfull + 8 * nq);
-                if (++nq == kNormSlots) {
-                  nq = 0;
-                  nq_ph ^= 1;
-                }
-              } else {
-                record_error(p, kStatusTimeout, 0x31);
-                *abort_flag = 1;
-                stop = 1;
-              }
-            }
-          }
-          *epi_stop = stop;
-        }
-        named_bar_sync(1, 128);
-        if (*epi_stop) break;
-      }
-    }
-    if constexpr (LN) {
-      // Tell the normalizer warps there is no more work.
-      if (ew == 0 && lane == 0 && mbar_wait(bar_nempty + 8 * nq, nq_ph ^ 1, tmo, abort_flag)) {
-        norm_slot[nq] = -1;
-        mbar_arrive(bar_nfull + 8 * nq);
       }
     }
     if (!ok) {
@@ -603,94 +541,68 @@ __global__ void __launch_bounds__(LN ? 320 : (CONV ? 288 : 192), 1)
     __syncwarp();
   }
 
-  else if constexpr (LN) {
-    // ------------------------------------------------------------------ normalizer
-    // Four warps normalise queued 128-row blocks in place while the other roles keep
-    // computing tiles.  Warp nw owns rows nw*32..+31 of the block; its lanes cover 8
-    // consecutive columns of each 256-column slab and keep 16 rows of loads in flight.
-    const int nw = warp - (kFirstEpiWarp + kEpiWarps);  // 0..3
-    int nq = 0;
-    uint32_t nq_ph = 0;
-    typedef unsigned short u16;
-    u16* outp = reinterpret_cast<u16*>(p.out);
-    while (true) {
-      if (!mbar_wait(bar_nfull + 8 * nq, nq_ph, tmo, abort_flag)) {
-        if (!*abort_flag) {
-          record_error(p, kStatusTimeout, 0x40);
-          *abort_flag = 1;
-        }
-        break;
-      }
-      const int tm = norm_slot[nq];
-      if (tm < 0) break;
-      __threadfence();
-      // 1) this lane's row: merge the tiles_n slices' (mean, M2) into mean / rstd
-      const int r = nw * 32 + lane;
-      const int grow = tm * kBM + r;
-      if (grow < p.M) {
-        float cnt = 0.f, mean = 0.f, m2 = 0.f;
-        for (int j = 0; j < p.tiles_n; ++j) {
-          const float4 pm = __ldcg(p.ln_stats + static_cast<long long>(j) * p.M + grow);
-          chan_merge(cnt, mean, m2, static_cast<float>(min(BN, p.N - j * BN)), pm.x, pm.y);
-        }
-        row_mean[r] = mean;
-        row_rstd[r] = rsqrtf(m2 / static_cast<float>(p.N) + p.eps);
-      }
-      __syncwarp();
-      // 2) y = (x - mean) * rstd * gamma + beta over the warp's 32 rows
-      const int row_base = tm * kBM + nw * 32;
-      const int rows_here = min(32, p.M - row_base);
-      for (int cb = 0; cb * 256 < p.N; ++cb) {
-        const int col = cb * 256 + lane * 8;
-        if (col >= p.N) continue;
-        float g[8], b[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          g[e] = load_vec(p.gamma, p.vec_dtype, col + e);
-          b[e] = load_vec(p.beta, p.vec_dtype, col + e);
-        }
-        const float4* tile_stats = p.ln_stats + static_cast<long long>(col / BN) * p.M;
-        for (int r0 = 0; r0 < rows_here; r0 += 16) {
-          uint4 y[16];
-          float sh[16];
-#pragma unroll
-          for (int u = 0; u < 16; ++u) {
-            if (r0 + u < rows_here) {
-              y[u] = __ldcg(reinterpret_cast<const uint4*>(outp + (row_base + r0 + u) * p.ldo + col));
-              sh[u] = __ldcg(tile_stats + row_base + r0 + u).z;
-            }
-          }
-#pragma unroll
-          for (int u = 0; u < 16; ++u) {
-            if (r0 + u < rows_here) {
-              const float off = sh[u] - row_mean[nw * 32 + r0 + u], rs = row_rstd[nw * 32 + r0 + u];
-              uint32_t w[4] = {y[u].x, y[u].y, y[u].z, y[u].w};
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float2 f = unpack2<OUT_DT>(w[e]);
-                w[e] = pack2<OUT_DT>(fmaf((f.x + off) * rs, g[2 * e], b[2 * e]),
-                                     fmaf((f.y + off) * rs, g[2 * e + 1], b[2 * e + 1]));
-              }
-              __stcg(reinterpret_cast<uint4*>(outp + (row_base + r0 + u) * p.ldo + col),
-                     make_uint4(w[0], w[1], w[2], w[3]));
-            }
-          }
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar_nempty + 8 * nq);
-      if (++nq == kNormSlots) {
-        nq = 0;
-        nq_ph ^= 1;
-      }
-    }
-  }
-
   tc_fence_before();
   __syncthreads();
   if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// Second pass of the fused LayerNorm: one warp per output row.  The lanes merge the
+// row's tiles_n slice statistics (Chan et al.) into mean / rstd with a butterfly of
+// shuffles, then normalise the row in place: y = (x_stored + shift - mean) * rstd *
+// gamma + beta, where shift is the value the GEMM epilogue subtracted before storing
+// that slice.  Each lane keeps 8 x 16-byte loads in flight.  Grid-wide and
+// stream-ordered after the GEMM kernel, so it runs at full-chip bandwidth on rows that
+// are mostly still in L2.
+template <int OUT_DT>
+__global__ void __launch_bounds__(256) fo_ln_normalize_kernel(const KParams p, int bn) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + warp;
+  if (row >= p.M) return;
+  float cnt = 0.f, mean = 0.f, m2 = 0.f;
+  for (int j = lane; j < p.tiles_n; j += 32) {
+    const float4 pm = __ldcg(p.ln_stats + static_cast<long long>(j) * p.M + row);
+    chan_merge(cnt, mean, m2, static_cast<float>(min(bn, p.N - j * bn)), pm.x, pm.y);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float c2 = __shfl_xor_sync(0xffffffffu, cnt, o);
+    const float m2b = __shfl_xor_sync(0xffffffffu, m2, o);
+    const float mb = __shfl_xor_sync(0xffffffffu, mean, o);
+    chan_merge(cnt, mean, m2, c2, mb, m2b);
+  }
+  const float rs = rsqrtf(m2 / static_cast<float>(p.N) + p.eps);
+  unsigned short* rowp = reinterpret_cast<unsigned short*>(p.out) + static_cast<long long>(row) * p.ldo;
+  const int slabs = (p.N + 255) / 256;
+  for (int s0 = 0; s0 < slabs; s0 += 8) {
+    uint4 y[8];
+    float off[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int col = (s0 + u) * 256 + lane * 8;
+      if (s0 + u < slabs && col < p.N) {
+        y[u] = __ldcg(reinterpret_cast<const uint4*>(rowp + col));
+        off[u] = __ldcg(p.ln_stats + static_cast<long long>(col / bn) * p.M + row).z - mean;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int col = (s0 + u) * 256 + lane * 8;
+      if (s0 + u < slabs && col < p.N) {
+        uint32_t w[4] = {y[u].x, y[u].y, y[u].z, y[u].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = unpack2<OUT_DT>(w[e]);
+          const int c = col + 2 * e;
+          w[e] = pack2<OUT_DT>(
+              fmaf((f.x + off[u]) * rs, load_vec(p.gamma, p.vec_dtype, c), load_vec(p.beta, p.vec_dtype, c)),
+              fmaf((f.y + off[u]) * rs, load_vec(p.gamma, p.vec_dtype, c + 1), load_vec(p.beta, p.vec_dtype, c + 1)));
+        }
+        __stcg(reinterpret_cast<uint4*>(rowp + col), make_uint4(w[0], w[1], w[2], w[3]));
+      }
+    }
   }
 }
 

@@ -30,7 +30,7 @@ cudaError_t launch_tc(const LaunchArgs& a) {
     if (e != cudaSuccess) return e;
     opted.fetch_or(bit, std::memory_order_acq_rel);
   }
-  constexpr int kThreads = LN ? 320 : (CONV ? 288 : 192);
+  constexpr int kThreads = CONV ? 288 : 192;
   kern<<<a.grid, kThreads, a.smem, a.stream>>>(a.tmA, a.tmB, a.tmC, a.p);
   return cudaGetLastError();
 }

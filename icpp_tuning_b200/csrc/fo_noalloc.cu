@@ -5,7 +5,7 @@
 // they are running: a serving process that reserves its whole device-memory budget at
 // start-up and must never grow it, or a host framework whose plugin interface hands the
 // operator its inputs and outputs but no allocator.  fo_gemm's LayerNorm epilogue needs
-// scratch memory for its per-row statistics and row-block counters, which those callers
+// scratch memory for its per-row slice statistics, which those callers
 // cannot provide.  This entry point takes that scratch from a file-scope __device__
 // array of fixed size instead, and it allocates nothing: no cudaMalloc, no cudaFree, no
 // allocating library routine.  (fo_gemm also allocates a small status word on the first
@@ -16,10 +16,10 @@
 //     need more (fo_gemm_workspace_size > 8 MiB, e.g. M * ceil(N / block_n) > ~520k) is
 //     rejected with FO_EINVAL and a message naming both sizes;
 //   * every GPU that loads this library holds the 8 MiB array until the process exits;
-//   * every call shares the one array per device and it keeps the last call's contents:
-//     the row-block counters are cleared on the stream before each launch, and calls
-//     whose executions overlap on the GPU (different streams, or other threads) race on
-//     the array -- serialise them;
+//   * every call shares the one array per device and it keeps the last call's contents;
+//     nothing in it has to start at zero (each call writes every statistic it later
+//     reads), but calls whose executions overlap on the GPU (different streams, or other
+//     threads) race on the array -- serialise them;
 //   * the first call on a device resolves the array's device address with
 //     cudaGetSymbolAddress (once per device, with that device current); make that first
 //     call before any stream capture begins;
@@ -170,9 +170,9 @@ int run(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
   p.eps = d->eps;
   p.out = d->out;
   p.ldo = d->ldo;
-  const size_t counter_bytes = round_up(static_cast<size_t>(p.tiles_m) * 4, 256);
-  p.ln_counters = static_cast<int*>(scratch);
-  p.ln_stats = reinterpret_cast<float4*>(static_cast<char*>(scratch) + counter_bytes);
+  // Same layout as fo_gemm's workspace: a reserved 256-byte-aligned header, then the stats.
+  const size_t header_bytes = round_up(static_cast<size_t>(p.tiles_m) * 4, 256);
+  p.ln_stats = reinterpret_cast<float4*>(static_cast<char*>(scratch) + header_bytes);
   p.status = status;
   p.timeout_ns = 2000000000ull;
 
@@ -187,8 +187,6 @@ int run(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
   if (int rc = tmap(&la.tmC, d->out_dtype, d->out, d->N, d->M, d->ldo * 2, 64, 32)) return rc;
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // The array keeps the last call's contents: start every call with zeroed counters.
-  if (cudaMemsetAsync(scratch, 0, counter_bytes, st) != cudaSuccess) return say(FO_ECUDA, "cudaMemsetAsync failed");
   const int cap = cfg->max_ctas > 0 ? cfg->max_ctas : sms;
   la.grid = p.num_tiles < cap ? p.num_tiles : cap;
   la.smem = fo::smem_bytes_for(bn, cfg->stages);

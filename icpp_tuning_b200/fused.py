@@ -94,8 +94,8 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, b_layout: str = "kn", epilogue: st
     """out = epilogue(a @ B) with fp32 accumulation.
 
     a: [M, K]; b: [K, N] when b_layout == "kn" (reference layout), [N, K] when "nk".
-    epilogue: one of EPILOGUES.  "bias_layernorm" needs gamma, beta and a zero-initialised
-    workspace of ln_workspace_bytes(M, N, config) bytes (the library re-zeroes it).
+    epilogue: one of EPILOGUES.  "bias_layernorm" needs gamma, beta and a workspace of
+    ln_workspace_bytes(M, N, config) bytes for the per-row slice statistics.
     """
     dev = _require_cuda(a, b, bias, gamma, beta, out, workspace)
     if b_layout not in ("kn", "nk"):

@@ -2,11 +2,13 @@
 kernel/tilelang/gemm/gemm_bias_layernorm.py).
 
 The reference runs two kernels: a GEMM+bias writing fp32 to HBM (:52-90) and a
-standalone LayerNorm that reads it back twice (:93-164).  Here one persistent kernel
-does both: each epilogue thread owns one output row of a 128 x BN tile, computes the
-exact fp32 (mean, M2) of its row slice from TMEM, writes the biased tile once, and the
-last CTA to finish a 128-row block merges the slices' statistics (Chan et al.) and
-normalises the block in place while it is still in L2.
+standalone LayerNorm that reads it back twice (:93-164) with var = E[x^2] - mean^2.
+Here the statistics are fused into the GEMM: each epilogue thread owns one output row
+of a 128 x BN tile, computes the exact fp32 (mean, M2) of its row slice from TMEM and
+writes the biased slice once, in the output dtype, centred on a per-slice shift.  A
+light stream-ordered pass (one warp per row) then merges the slices' statistics (Chan
+et al.) and normalises every row in place while it is mostly still in L2: the data
+crosses HBM as 16-bit once each way instead of as fp32 three times.
 
 Reference surface kept: get_gemm_configs(K), torch_baseline(...), build_fused_kernel(M,
 N, K, gemm_config=None, block_M_ln=16, block_N_ln=128, thread_num_ln=128, eps=1e-5) ->
@@ -36,9 +38,7 @@ def torch_baseline(A, B, bias, gamma, beta):
 
 
 def get_gemm_configs(K: int = 0) -> List[Dict[str, Any]]:
-    # The last CTA of a row block normalises it: row-major raster keeps a block's tiles
-    # in one wave, so group_m is 0.
-    return tcgen05_configs(group_ms=(0,))
+    return tcgen05_configs()
 
 
 class GemmBiasLayerNormDescriptor(Tcgen05Descriptor):
@@ -63,15 +63,15 @@ def build_fused_kernel(M: int, N: int, K: int, gemm_config: Optional[Dict[str, A
                        device: Optional[torch.device] = None):
     """Returns fused_kernel(A, B, bias, gamma, beta) -> Y[M, N] (out_dtype, fp16 default
     as in the reference).  The statistics workspace is allocated here, once, on `device`
-    (default: the current CUDA device), zeroed, and reused by every call; the kernel
-    leaves it zeroed.  Calls that share one built kernel must not overlap on the GPU."""
+    (default: the current CUDA device) and reused by every call.  Calls that share one
+    built kernel must not overlap on the GPU."""
     assert N % block_N_ln == 0, f"N={N} must be divisible by block_N_ln={block_N_ln}"
     if gemm_config is None:
         gemm_config, _ = select_best(DESCRIPTOR, M=M, N=N, K=K,
                                      out_bytes=torch.empty((), dtype=out_dtype).element_size())
     cfg = fused.as_tile_cfg(gemm_config)
     dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
-    ws = torch.zeros(max(16, fused.ln_workspace_bytes(M, N, cfg)), dtype=torch.uint8, device=dev)
+    ws = torch.empty(max(16, fused.ln_workspace_bytes(M, N, cfg)), dtype=torch.uint8, device=dev)
 
     def fused_kernel(A, B, bias, gamma, beta, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         _check_shape(A, B, M, N, K, b_layout)

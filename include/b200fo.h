@@ -70,8 +70,9 @@ typedef struct FoTileCfg {
 /* One GEMM-family call.  A[M,K] row-major (row stride lda elements).  B per b_layout
  * with row stride ldb.  out[M,N] row-major with row stride ldo.  bias/gamma/beta are
  * length-N vectors of type vec_dtype (may be NULL when the epilogue does not read them).
- * For FO_EPI_BIAS_LN the caller provides workspace (fo_gemm_workspace_size bytes,
- * zero-filled before its first use; the library leaves it zeroed after each call). */
+ * For FO_EPI_BIAS_LN the caller provides workspace (fo_gemm_workspace_size bytes, any
+ * contents) for the per-row slice statistics; the call then launches two kernels: the
+ * GEMM writing biased rows + statistics, and the in-place normalisation pass. */
 typedef struct FoGemmDesc {
   int64_t M, N, K;
   const void* a;

@@ -28,13 +28,12 @@ def test_ln_ragged(bn, odt):
     dt = odt
     x, w, bias, gamma, beta = _inputs(10, M, Nn, K, dt)
     cfg = N.tile_cfg(bn, {256: 4, 128: 6, 64: 8}[bn], 0)
-    ws = torch.zeros(fused.ln_workspace_bytes(M, Nn, cfg), dtype=torch.uint8, device="cuda")
-    for _ in range(3):  # the workspace must come back zeroed every call
+    # arbitrary starting contents: every call writes each statistic before reading it
+    ws = torch.full((fused.ln_workspace_bytes(M, Nn, cfg),), 0x7F, dtype=torch.uint8, device="cuda")
+    for _ in range(3):
         out = fused.gemm(*cuda(x, w), b_layout="nk", epilogue="bias_layernorm", bias=bias.cuda(),
                          gamma=gamma.cuda(), beta=beta.cuda(), workspace=ws, out_dtype=odt, config=cfg)
         assert_close(out, R.gemm_bias_layernorm(x, w, bias, gamma, beta, b_layout="nk", out_dtype=odt), TOL_LN)
-        tiles_m = (M + 127) // 128
-        assert int(ws[: tiles_m * 4].view(torch.int32).abs().sum()) == 0
     status_clean()
 
 

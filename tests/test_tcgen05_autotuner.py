@@ -56,8 +56,8 @@ def test_baseline_shapes_select_legal(desc, shape):
     assert rk[0]["detail"]["projection"]["predicted_tflops"] > 0
 
 
-def test_layernorm_configs_use_row_major_raster():
-    assert {c["group_m"] for c in gemm_bias_layernorm.get_gemm_configs(4096)} == {0}
+def test_layernorm_configs_cover_both_rasters():
+    assert {c["group_m"] for c in gemm_bias_layernorm.get_gemm_configs(4096)} == {0, 8}
 
 
 def test_search_space_tcgen05_prunes_to_library_legal():
