@@ -8,6 +8,7 @@
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -121,6 +122,51 @@ int make_tmap(CUtensorMap* m, int dt, const void* base, uint64_t inner, uint64_t
                 what, static_cast<int>(r), static_cast<unsigned long long>(outer),
                 static_cast<unsigned long long>(inner), static_cast<unsigned long long>(row_bytes));
   return FO_OK;
+}
+
+PFN_cuTensorMapEncodeIm2col_v12000 encode_im2col_fn() {
+  static PFN_cuTensorMapEncodeIm2col_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeIm2col_v12000>(p);
+  });
+  return fn;
+}
+
+// im2col-mode map over x[n][h][w][c]: each load walks 128 consecutive filter-origin
+// positions through the bounding box [-pad, dim - 1 + pad - (k - 1) * dil] of W, then
+// H, then N (stepping by the conv stride) and fetches 64 channels per position.  Returns
+// false when the driver rejects the geometry (the gather producer is used instead).
+bool make_im2col_map(CUtensorMap* m, const FoConvDesc* d) {
+  auto fn = encode_im2col_fn();
+  if (fn == nullptr) return false;
+  const int lw = -d->pad, lh = -d->pad;
+  const int uw = d->pad - (d->kw - 1) * d->dil, uh = d->pad - (d->kh - 1) * d->dil;
+  if (lw < -128 || uw > 127 || uh > 127 || uw < -128 || uh < -128) return false;
+  if ((d->kw - 1) * d->dil > 255 || (d->kh - 1) * d->dil > 255) return false;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(d->c), static_cast<cuuint64_t>(d->w),
+                        static_cast<cuuint64_t>(d->h), static_cast<cuuint64_t>(d->n)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(d->c) * 2, static_cast<cuuint64_t>(d->w) * d->c * 2,
+                           static_cast<cuuint64_t>(d->h) * d->w * d->c * 2};
+  int lower[2] = {lw, lh};
+  int upper[2] = {uw, uh};
+  cuuint32_t estr[4] = {1, static_cast<cuuint32_t>(d->stride), static_cast<cuuint32_t>(d->stride), 1};
+  CUresult r = fn(m, tma_dt(d->in_dtype), 4, const_cast<void*>(d->x), dims, strides, lower, upper, 64, 128, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+bool conv_gather_forced() {
+  static const bool v = [] {
+    const char* e = getenv("FO_CONV_GATHER");
+    return e != nullptr && e[0] == '1';
+  }();
+  return v;
 }
 
 int check_cfg(int op, int out_dtype, const FoTileCfg* cfg, char* why, size_t why_len) {
@@ -259,6 +305,7 @@ int fo_gemm(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
   if (ln) {
     if (d->out_dtype == FO_DT_F32) return fail(FO_EINVAL, "LayerNorm output must be f16 or bf16");
     if (d->gamma == nullptr || d->beta == nullptr) return fail(FO_EINVAL, "LayerNorm needs gamma and beta");
+    if (!aligned16(d->gamma) || !aligned16(d->beta)) return fail(FO_EINVAL, "gamma and beta must be 16-byte aligned");
     if (d->N % 8 != 0) return fail(FO_EINVAL, "LayerNorm needs N %% 8 == 0, got N=%lld", (long long)d->N);
     const size_t need = ln_workspace(d->M, d->N, cfg->block_n);
     if (d->workspace == nullptr || d->workspace_bytes < need || !aligned16(d->workspace))
@@ -385,6 +432,7 @@ int fo_conv2d(const FoConvDesc* d, const FoTileCfg* cfg, void* stream) {
   p.pad = d->pad;
   p.dil = d->dil;
   fill_common(p, di);
+  p.conv_tma = (d->stride <= 8 && !conv_gather_forced() && make_im2col_map(&la.tmA, d)) ? 1 : 0;
   if (int rc = make_tmap(&la.tmB, d->in_dtype, d->wgt, d->f, K64, static_cast<uint64_t>(d->f) * 2, 64, 64, "weights"))
     return rc;
   if (int rc = make_tmap(&la.tmC, d->out_dtype, d->out, d->f, M64, static_cast<uint64_t>(d->f) * ob, 128 / ob, 32,

@@ -64,6 +64,7 @@ struct KParams {
   // implicit-GEMM conv geometry (NHWC)
   const void* x;
   int H, W, C, OH, OW, KH, KW, stride, pad, dil, c_blocks;
+  int conv_tma;  // 1: A tiles by TMA im2col loads (tmA); 0: cp.async gather
 };
 
 __host__ __device__ constexpr int b_stage_bytes(int bn) { return bn * kBK * 2; }
@@ -213,7 +214,7 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
-      mbar_init(bar_full + 8 * s, CONV ? 128 : 1);
+      mbar_init(bar_full + 8 * s, (CONV && !p.conv_tma) ? 128 : 1);
       mbar_init(bar_empty + 8 * s, 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -231,7 +232,7 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
   if (threadIdx.x == 32 * kFirstEpiWarp) {
     tma_prefetch_desc(&tmC);
     if (p.k_blocks > 0) {  // with K = 0 the A / B maps are left unencoded
-      if (!CONV) tma_prefetch_desc(&tmA);
+      if (!CONV || p.conv_tma) tma_prefetch_desc(&tmA);
       tma_prefetch_desc(&tmB);
     }
   }
@@ -276,6 +277,54 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
         }
         if (!ok) {
           record_error(p, kStatusTimeout, 0x10);
+          *abort_flag = 1;
+        }
+        drain_loads(bar_full, stages, issued);
+      }
+    } else if (p.conv_tma) {
+      // conv, TMA im2col: one thread loads each 128-pixel x 64-channel A tile of the
+      // current filter tap with one instruction, and the weight tile beside it.
+      if (threadIdx.x == 0) {
+        int s = 0;
+        uint32_t ph = 0;
+        int issued = 0;
+        bool ok = true;
+        const int ohow = p.OH * p.OW;
+        for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+          int tm, tn;
+          tile_coords(p, t, tm, tn);
+          const int m0 = tm * kBM;
+          const int n_img = m0 / ohow;
+          const int rem = m0 - n_img * ohow;
+          const int oh = rem / p.OW;
+          const int ow = rem - oh * p.OW;
+          const int w0 = ow * p.stride - p.pad;
+          const int h0 = oh * p.stride - p.pad;
+          for (int kb = 0; kb < p.k_blocks; ++kb) {
+            const int tap = kb / p.c_blocks;
+            const int cb = kb - tap * p.c_blocks;
+            const int kh = tap / p.KW;
+            const int kw = tap - kh * p.KW;
+            if (!mbar_wait(bar_empty + 8 * s, ph ^ 1, tmo, abort_flag)) {
+              ok = false;
+              break;
+            }
+            const uint32_t fb = bar_full + 8 * s;
+            mbar_arrive_expect_tx(fb, kAStageBytes + kBStage);
+            tma_load_im2col_4d(sA + s * kAStageBytes, &tmA, fb, cb * kBK, w0, h0, n_img,
+                               static_cast<uint16_t>(kw * p.dil), static_cast<uint16_t>(kh * p.dil));
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(sB + s * kBStage + j * 64 * 128, &tmB, fb, tn * BN + j * 64, tap * p.C + cb * kBK);
+            ++issued;
+            if (++s == stages) {
+              s = 0;
+              ph ^= 1;
+            }
+          }
+        }
+        if (!ok) {
+          record_error(p, kStatusTimeout, 0x12);
           *abort_flag = 1;
         }
         drain_loads(bar_full, stages, issued);
@@ -549,6 +598,24 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
   }
 }
 
+// Eight consecutive elements of a parameter vector (16-byte aligned start) as floats.
+__device__ __forceinline__ void load_vec8(const void* ptr, int dt, int i, float (&f)[8]) {
+  if (dt == DT_F32) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(ptr) + i / 4);
+    const float4 b = __ldg(reinterpret_cast<const float4*>(ptr) + i / 4 + 1);
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+    return;
+  }
+  const uint4 u = __ldg(reinterpret_cast<const uint4*>(ptr) + i / 8);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 v = dt == DT_BF16 ? unpack2<DT_BF16>(w[e]) : unpack2<DT_F16>(w[e]);
+    f[2 * e] = v.x;
+    f[2 * e + 1] = v.y;
+  }
+}
+
 // Second pass of the fused LayerNorm: one warp per output row.  The lanes merge the
 // row's tiles_n slice statistics (Chan et al.) into mean / rstd with a butterfly of
 // shuffles, then normalise the row in place: y = (x_stored + shift - mean) * rstd *
@@ -591,14 +658,15 @@ __global__ void __launch_bounds__(256) fo_ln_normalize_kernel(const KParams p, i
     for (int u = 0; u < 8; ++u) {
       const int col = (s0 + u) * 256 + lane * 8;
       if (s0 + u < slabs && col < p.N) {
+        float g[8], b[8];
+        load_vec8(p.gamma, p.vec_dtype, col, g);
+        load_vec8(p.beta, p.vec_dtype, col, b);
         uint32_t w[4] = {y[u].x, y[u].y, y[u].z, y[u].w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float2 f = unpack2<OUT_DT>(w[e]);
-          const int c = col + 2 * e;
-          w[e] = pack2<OUT_DT>(
-              fmaf((f.x + off[u]) * rs, load_vec(p.gamma, p.vec_dtype, c), load_vec(p.beta, p.vec_dtype, c)),
-              fmaf((f.y + off[u]) * rs, load_vec(p.gamma, p.vec_dtype, c + 1), load_vec(p.beta, p.vec_dtype, c + 1)));
+          w[e] = pack2<OUT_DT>(fmaf((f.x + off[u]) * rs, g[2 * e], b[2 * e]),
+                               fmaf((f.y + off[u]) * rs, g[2 * e + 1], b[2 * e + 1]));
         }
         __stcg(reinterpret_cast<uint4*>(rowp + col), make_uint4(w[0], w[1], w[2], w[3]));
       }

@@ -118,6 +118,7 @@ int run(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
   if (d->vec_dtype < FO_DT_F16 || d->vec_dtype > FO_DT_F32) return say(FO_EINVAL, "bad vec_dtype");
   if (d->b_layout != FO_B_KN && d->b_layout != FO_B_NK) return say(FO_EINVAL, "bad b_layout");
   if (d->bias == nullptr || d->gamma == nullptr || d->beta == nullptr) return say(FO_EINVAL, "LayerNorm needs bias, gamma and beta");
+  if (!a16(d->gamma) || !a16(d->beta)) return say(FO_EINVAL, "gamma and beta must be 16-byte aligned");
   if (d->N % 8 != 0) return say(FO_EINVAL, "LayerNorm needs N % 8 == 0");
   if (d->out == nullptr || !a16(d->out) || d->ldo < d->N || (d->ldo * 2) % 16 != 0)
     return say(FO_EINVAL, "out must be 16-byte aligned with ldo >= N and a multiple of 8");
