@@ -30,7 +30,7 @@ def max_stages(block_n: int) -> int:
     return s
 
 
-def tcgen05_configs(block_ns: Sequence[int] = (64, 128, 256), group_ms: Sequence[int] = (0, 8),
+def tcgen05_configs(block_ns: Sequence[int] = (64, 128, 256), group_ms: Sequence[int] = (0, 8, 16),
                     conv: bool = False, stages: Sequence[int] = ()) -> List[Dict[str, Any]]:
     out = []
     for bn in block_ns:

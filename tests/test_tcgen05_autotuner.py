@@ -57,7 +57,7 @@ def test_baseline_shapes_select_legal(desc, shape):
 
 
 def test_layernorm_configs_cover_both_rasters():
-    assert {c["group_m"] for c in gemm_bias_layernorm.get_gemm_configs(4096)} == {0, 8}
+    assert {c["group_m"] for c in gemm_bias_layernorm.get_gemm_configs(4096)} == {0, 8, 16}
 
 
 def test_search_space_tcgen05_prunes_to_library_legal():
