@@ -207,6 +207,50 @@ int act_of(int epi, int* has_bias) {
 
 size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// Work split of a GEMM over `cap` persistent CTAs.  Whole tiles fill as many complete
+// waves as they can; the tiles of a last, less than half-full wave (or of a problem with
+// fewer tiles than CTAs) are split along K into up to 8 parts so every CTA has work.
+struct SplitPlan {
+  int grid, num_units, dp_units, split, kb_per_part, split_tiles;
+};
+
+SplitPlan plan_split(int tiles, int k_blocks, int cap, bool allow) {
+  SplitPlan pl{tiles < cap ? tiles : cap, tiles, tiles, 1, k_blocks, 0};
+  if (!allow || k_blocks < 2 || tiles <= 0) return pl;
+  const int full = tiles >= cap ? tiles / cap : 0;
+  const int left = tiles - full * cap;
+  if (left == 0 || 2 * left > cap) return pl;
+  int split = cap / left;
+  if (split > 8) split = 8;
+  if (split > k_blocks) split = k_blocks;
+  if (split < 2) return pl;
+  const int kbp = (k_blocks + split - 1) / split;
+  split = (k_blocks + kbp - 1) / kbp;  // no empty parts
+  if (split < 2) return pl;
+  pl.split = split;
+  pl.kb_per_part = kbp;
+  pl.split_tiles = left;
+  pl.dp_units = full * cap;
+  pl.num_units = pl.dp_units + left * split;
+  pl.grid = pl.num_units < cap ? pl.num_units : cap;
+  return pl;
+}
+
+size_t split_workspace(const SplitPlan& pl, int bn) {
+  if (pl.split < 2) return 0;
+  return round_up(static_cast<size_t>(pl.split_tiles) * 4 * sizeof(int), 256) +
+         static_cast<size_t>(pl.split_tiles) * pl.split * 128 * bn * sizeof(float);
+}
+
+int sm_count_or_default() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess &&
+      n > 0)
+    return n;
+  cudaGetLastError();
+  return 148;
+}
+
 size_t ln_workspace(int64_t M, int64_t N, int bn) {
   const int64_t tiles_m = (M + 127) / 128;
   const int64_t tiles_n = (N + bn - 1) / bn;
@@ -261,10 +305,15 @@ int fo_query_config_legal(int32_t op, int32_t out_dtype, const FoTileCfg* cfg, c
 }
 
 size_t fo_gemm_workspace_size(const FoGemmDesc* d, const FoTileCfg* cfg) {
-  if (d == nullptr || cfg == nullptr || d->epilogue != FO_EPI_BIAS_LN) return 0;
+  if (d == nullptr || cfg == nullptr) return 0;
   if (cfg->block_n != 64 && cfg->block_n != 128 && cfg->block_n != 256) return 0;
   if (d->M <= 0 || d->N <= 0) return 0;
-  return ln_workspace(d->M, d->N, cfg->block_n);
+  if (d->epilogue == FO_EPI_BIAS_LN) return ln_workspace(d->M, d->N, cfg->block_n);
+  // Other epilogues: room for the split-K tail (optional; without it there is no split).
+  const int bn = cfg->block_n;
+  const int tiles = static_cast<int>(((d->M + 127) / 128) * ((d->N + bn - 1) / bn));
+  const int cap = cfg->max_ctas > 0 ? cfg->max_ctas : sm_count_or_default();
+  return split_workspace(plan_split(tiles, static_cast<int>((d->K + 63) / 64), cap, true), bn);
 }
 
 int fo_gemm(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
@@ -355,7 +404,20 @@ int fo_gemm(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
   if (int rc = make_tmap(&la.tmC, d->out_dtype, d->out, d->N, d->M, d->ldo * ob, 128 / ob, 32, "out")) return rc;
 
   const int cap = cfg->max_ctas > 0 ? cfg->max_ctas : di.sms;
-  la.grid = p.num_tiles < cap ? p.num_tiles : cap;
+  SplitPlan pl = plan_split(p.num_tiles, p.k_blocks, cap, !ln);
+  const size_t split_need = split_workspace(pl, bn);
+  if (split_need == 0 || d->workspace == nullptr || d->workspace_bytes < split_need || !aligned16(d->workspace))
+    pl = plan_split(p.num_tiles, p.k_blocks, cap, false);  // no room for partials: whole tiles only
+  p.num_units = pl.num_units;
+  p.dp_units = pl.dp_units;
+  p.split = pl.split;
+  p.kb_per_part = pl.kb_per_part;
+  if (pl.split > 1) {
+    p.split_cnt = static_cast<int*>(d->workspace);
+    p.split_ws = reinterpret_cast<float*>(static_cast<char*>(d->workspace) +
+                                          round_up(static_cast<size_t>(pl.split_tiles) * 4 * sizeof(int), 256));
+  }
+  la.grid = pl.grid;
   la.smem = fo::smem_bytes_for(bn, cfg->stages);
   la.stream = static_cast<cudaStream_t>(stream);
   const int out_dt = d->out_dtype == FO_DT_F16 ? fo::DT_F16 : d->out_dtype == FO_DT_BF16 ? fo::DT_BF16 : fo::DT_F32;
@@ -440,6 +502,9 @@ int fo_conv2d(const FoConvDesc* d, const FoTileCfg* cfg, void* stream) {
     return rc;
   const int cap = cfg->max_ctas > 0 ? cfg->max_ctas : di.sms;
   la.grid = p.num_tiles < cap ? p.num_tiles : cap;
+  p.num_units = p.dp_units = p.num_tiles;  // whole tiles
+  p.split = 1;
+  p.kb_per_part = p.k_blocks;
   la.smem = fo::smem_bytes_for(bn, cfg->stages);
   la.stream = static_cast<cudaStream_t>(stream);
   const int out_dt = d->out_dtype == FO_DT_F16 ? fo::DT_F16 : d->out_dtype == FO_DT_BF16 ? fo::DT_BF16 : fo::DT_F32;

@@ -65,6 +65,11 @@ struct KParams {
   const void* x;
   int H, W, C, OH, OW, KH, KW, stride, pad, dil, c_blocks;
   int conv_tma;  // 1: A tiles by TMA im2col loads (tmA); 0: cp.async gather
+  // work units: units [0, dp_units) are whole tiles; the remaining tiles are split along K
+  // into `split` parts of kb_per_part k-blocks, reduced through split_ws / split_cnt.
+  int num_units, dp_units, split, kb_per_part;
+  float* split_ws;  // [split tile][part][BN columns][128 rows] fp32 partial accumulators
+  int* split_cnt;   // [split tile][4 row quarters] arrival counters, self-resetting
 };
 
 __host__ __device__ constexpr int b_stage_bytes(int bn) { return bn * kBK * 2; }
@@ -150,6 +155,33 @@ __device__ __forceinline__ void tile_coords(const KParams& p, int t, int& tm, in
   const int gm = min(p.group_m, p.tiles_m - first_m);
   tm = first_m + r % gm;
   tn = r / gm;
+}
+
+struct Unit {
+  int tm, tn, kb0, kb1;
+  int st;    // index of the split tile, or -1 for a whole tile
+  int part;  // K part of a split tile
+};
+
+__device__ __forceinline__ Unit unit_of(const KParams& p, int u) {
+  Unit r;
+  int tile;
+  if (u < p.dp_units) {
+    tile = u;
+    r.kb0 = 0;
+    r.kb1 = p.k_blocks;
+    r.st = -1;
+    r.part = 0;
+  } else {
+    const int v = u - p.dp_units;
+    r.st = v / p.split;
+    r.part = v - r.st * p.split;
+    tile = p.dp_units + r.st;
+    r.kb0 = r.part * p.kb_per_part;
+    r.kb1 = min(p.k_blocks, r.kb0 + p.kb_per_part);
+  }
+  tile_coords(p, tile, r.tm, r.tn);
+  return r;
 }
 
 // Chan et al. parallel merge of (count, mean, M2).
@@ -250,10 +282,10 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
         uint32_t ph = 0;
         int issued = 0;  // stage loads issued by this thread
         bool ok = true;
-        for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
-          int tm, tn;
-          tile_coords(p, t, tm, tn);
-          for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int u = blockIdx.x; u < p.num_units && ok; u += gridDim.x) {
+          const Unit un = unit_of(p, u);
+          const int tm = un.tm, tn = un.tn;
+          for (int kb = un.kb0; kb < un.kb1; ++kb) {
             if (!mbar_wait(bar_empty + 8 * s, ph ^ 1, tmo, abort_flag)) {
               ok = false;
               break;
@@ -290,9 +322,9 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
         int issued = 0;
         bool ok = true;
         const int ohow = p.OH * p.OW;
-        for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
-          int tm, tn;
-          tile_coords(p, t, tm, tn);
+        for (int u = blockIdx.x; u < p.num_units && ok; u += gridDim.x) {
+          const Unit un = unit_of(p, u);
+          const int tm = un.tm, tn = un.tn;
           const int m0 = tm * kBM;
           const int n_img = m0 / ohow;
           const int rem = m0 - n_img * ohow;
@@ -300,7 +332,7 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
           const int ow = rem - oh * p.OW;
           const int w0 = ow * p.stride - p.pad;
           const int h0 = oh * p.stride - p.pad;
-          for (int kb = 0; kb < p.k_blocks; ++kb) {
+          for (int kb = un.kb0; kb < un.kb1; ++kb) {
             const int tap = kb / p.c_blocks;
             const int cb = kb - tap * p.c_blocks;
             const int kh = tap / p.KW;
@@ -339,9 +371,9 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
       bool ok = true;
       const int ohow = p.OH * p.OW;
       const char* xb = reinterpret_cast<const char*>(p.x);
-      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
-        int tm, tn;
-        tile_coords(p, t, tm, tn);
+      for (int u = blockIdx.x; u < p.num_units && ok; u += gridDim.x) {
+        const Unit un = unit_of(p, u);
+        const int tm = un.tm, tn = un.tn;
         const int m = tm * kBM + i;
         const bool valid_m = m < p.M;
         const int n_img = valid_m ? m / ohow : 0;
@@ -350,7 +382,7 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
         const int ow = rem - oh * p.OW;
         const int ih0 = oh * p.stride - p.pad;
         const int iw0 = ow * p.stride - p.pad;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = un.kb0; kb < un.kb1; ++kb) {
           const int tap = kb / p.c_blocks;
           const int cb = kb - tap * p.c_blocks;
           const int kh = tap / p.KW;
@@ -420,14 +452,15 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
       int acc = 0;
       uint32_t acc_ph = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+      for (int u = blockIdx.x; u < p.num_units && ok; u += gridDim.x) {
+        const Unit un = unit_of(p, u);
         if (!mbar_wait(bar_tempty + 8 * acc, acc_ph ^ 1, tmo, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d = tmem_base + acc * BN;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = un.kb0; kb < un.kb1; ++kb) {
           if (!mbar_wait(bar_full + 8 * s, ph, tmo, abort_flag)) {
             ok = false;
             break;
@@ -440,7 +473,7 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
             const uint64_t ad = sdesc_sw128(a0 + k * 32, 16, 1024);
             const uint64_t bd = p.b_mn ? sdesc_sw128(b0 + k * 2048, 64 * 128, 1024)
                                        : sdesc_sw128(b0 + k * 32, 16, 1024);
-            tc_mma_f16(d, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            tc_mma_f16(d, ad, bd, idesc, (kb != un.kb0 || k != 0) ? 1u : 0u);
           }
           tc_commit(bar_empty + 8 * s);
           if (++s == stages) {
@@ -471,9 +504,10 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
     uint32_t acc_ph = 0;
     uint32_t nstore = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
-      int tm, tn;
-      tile_coords(p, t, tm, tn);
+    for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
+      const Unit un = unit_of(p, u);
+      const int tm = un.tm, tn = un.tn;
+      const bool has_k = un.kb1 > un.kb0;
       if (!mbar_wait(bar_tfull + 8 * acc, acc_ph, tmo, abort_flag)) {
         ok = false;
         break;
@@ -481,6 +515,37 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
       tc_fence_after();
       const int row0 = tm * kBM + quarter * 32;
       const int col0 = tn * BN;
+      // Split tile: publish this part's fp32 partial ([column][128 rows], coalesced), then
+      // the warp whose arrival completes its row quarter adds the other parts and runs
+      // the epilogue; the other warps release the accumulator and move on.
+      float* split_tile = nullptr;
+      if (un.st >= 0) {
+        split_tile = p.split_ws + static_cast<long long>(un.st) * p.split * BN * 128;
+        float* mine = split_tile + static_cast<long long>(un.part) * BN * 128 + quarter * 32 + lane;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tmem_base + lane_off + acc * BN + c * 32, r);
+          tc_wait_ld_regs(r);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) __stcg(mine + (c * 32 + i) * 128, __uint_as_float(r[i]));
+        }
+        __threadfence();
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) last = atomicAdd(p.split_cnt + un.st * 4 + quarter, 1) == p.split - 1;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (!last) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar_tempty + 8 * acc);
+          acc ^= 1;
+          if (acc == 0) acc_ph ^= 1;
+          continue;
+        }
+        __threadfence();
+        if (lane == 0) p.split_cnt[un.st * 4 + quarter] = 0;
+      }
       float st_cnt = 0.f, st_mean = 0.f, st_m2 = 0.f;
       float shift = 0.f;  // LayerNorm: the tile is stored centred on its first chunk's mean
 #pragma unroll 1
@@ -492,13 +557,21 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
           tmem_ld_32x32b_x32(tmem_base + lane_off + acc * BN + c * kCPC, r0);
           tc_wait_ld_regs(r0);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = p.k_blocks > 0 ? __uint_as_float(r0[i]) : 0.f;
+          for (int i = 0; i < 32; ++i) v[i] = has_k ? __uint_as_float(r0[i]) : 0.f;
           if constexpr (kCPC == 64) {
             uint32_t r1[32];
             tmem_ld_32x32b_x32(tmem_base + lane_off + acc * BN + c * kCPC + 32, r1);
             tc_wait_ld_regs(r1);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[32 + i] = p.k_blocks > 0 ? __uint_as_float(r1[i]) : 0.f;
+            for (int i = 0; i < 32; ++i) v[32 + i] = has_k ? __uint_as_float(r1[i]) : 0.f;
+          }
+        }
+        if (split_tile != nullptr) {
+          for (int q = 0; q < p.split; ++q) {
+            if (q == un.part) continue;
+            const float* other = split_tile + static_cast<long long>(q) * BN * 128 + quarter * 32 + lane;
+#pragma unroll
+            for (int i = 0; i < kCPC; ++i) v[i] += __ldcg(other + (c * kCPC + i) * 128);
           }
         }
         if (c == kChunks - 1) {

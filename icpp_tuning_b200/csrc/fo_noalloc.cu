@@ -190,6 +190,9 @@ int run(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int cap = cfg->max_ctas > 0 ? cfg->max_ctas : sms;
   la.grid = p.num_tiles < cap ? p.num_tiles : cap;
+  p.num_units = p.dp_units = p.num_tiles;  // whole tiles
+  p.split = 1;
+  p.kb_per_part = p.k_blocks;
   la.smem = fo::smem_bytes_for(bn, cfg->stages);
   la.stream = st;
   cudaError_t e = fo::launch_ln_family(bn, d->out_dtype == FO_DT_F16 ? fo::DT_F16 : fo::DT_BF16, la);

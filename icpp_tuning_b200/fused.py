@@ -79,11 +79,17 @@ def as_tile_cfg(cfg) -> N.FoTileCfg:
                       block_m=int(cfg.get("block_M", 128)), block_k=int(cfg.get("block_K", 64)))
 
 
-def ln_workspace_bytes(M: int, N_: int, cfg) -> int:
+def workspace_bytes(M: int, N_: int, K: int, epilogue: str, cfg) -> int:
+    """Workspace fo_gemm uses for this problem: LayerNorm statistics (required) or, for
+    the other epilogues, fp32 partials of the split-K tail (optional, zero-filled)."""
     d = N.FoGemmDesc()
-    d.M, d.N, d.epilogue = M, N_, N.FO_EPI_BIAS_LN
+    d.M, d.N, d.K, d.epilogue = M, N_, K, EPILOGUES[epilogue]
     c = as_tile_cfg(cfg)
     return int(N.lib().fo_gemm_workspace_size(ctypes.byref(d), ctypes.byref(c)))
+
+
+def ln_workspace_bytes(M: int, N_: int, cfg) -> int:
+    return workspace_bytes(M, N_, 0, "bias_layernorm", cfg)
 
 
 def gemm(a: torch.Tensor, b: torch.Tensor, *, b_layout: str = "kn", epilogue: str = "none",
@@ -95,7 +101,9 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, b_layout: str = "kn", epilogue: st
 
     a: [M, K]; b: [K, N] when b_layout == "kn" (reference layout), [N, K] when "nk".
     epilogue: one of EPILOGUES.  "bias_layernorm" needs gamma, beta and a workspace of
-    ln_workspace_bytes(M, N, config) bytes for the per-row slice statistics.
+    ln_workspace_bytes(M, N, config) bytes for the per-row slice statistics.  The other
+    epilogues accept an optional zero-filled workspace of workspace_bytes(...) bytes that
+    lets the kernel split the tiles of a partial last wave along K.
     """
     dev = _require_cuda(a, b, bias, gamma, beta, out, workspace)
     if b_layout not in ("kn", "nk"):

@@ -112,7 +112,11 @@ typedef struct FoConvDesc {
  * gemm_bias_layernorm.py:167-188).  Launches one persistent kernel on `stream`. */
 int fo_gemm(const FoGemmDesc* desc, const FoTileCfg* cfg, void* stream);
 
-/* Bytes of workspace fo_gemm needs for this (desc, cfg); 0 unless FO_EPI_BIAS_LN. */
+/* Bytes of workspace fo_gemm uses for this (desc, cfg).  FO_EPI_BIAS_LN: required (per-row
+ * slice statistics, any contents).  Other epilogues: optional room for fp32 partials of a
+ * split-K tail -- the tiles of a last, less than half-full wave (or of a problem with
+ * fewer tiles than SMs) split along K over idle SMs; it must be zero-filled before its
+ * first use and is left zeroed.  Without it (or with 0 returned) tiles are never split. */
 size_t fo_gemm_workspace_size(const FoGemmDesc* desc, const FoTileCfg* cfg);
 
 /* Replaces: build_conv2d_kernel(...)(X, W, Y) (kernel/tilelang/conv/conv2d.py:282-290,

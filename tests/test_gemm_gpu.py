@@ -148,3 +148,27 @@ def test_config3_gemm_bias_gelu_mlp():
     rows = torch.arange(0, 8192, 61)
     assert_close(out[rows.cuda()], R.gemm_bias_act(x[rows], w, bias, "gelu_tanh", "nk"), TOL)
     status_clean()
+
+
+@pytest.mark.parametrize("M,Nn,K,bn,layout", [
+    (126, 2304, 768, 64, "kn"),       # 36 tiles on 148 SMs: split 4 ways along K
+    (4096, 4096, 4096, 256, "nk"),    # 512 tiles: the 68-tile last wave split 2 ways
+    (300, 520, 200, 128, "kn"),       # K of 4 k-blocks: uneven parts
+])
+def test_split_k_tail(M, Nn, K, bn, layout):
+    a, b, bias = _inputs(9, M, Nn, K, torch.bfloat16, layout)
+    cfg = N.tile_cfg(bn, {256: 4, 128: 6, 64: 8}[bn], 8)
+    nbytes = fused.workspace_bytes(M, Nn, K, "bias_gelu_tanh", cfg)
+    assert nbytes > 0
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    a_d, b_d, bias_d = cuda(a, b, bias)
+    whole = fused.gemm(a_d, b_d, b_layout=layout, epilogue="bias_gelu_tanh", bias=bias_d, config=cfg)
+    for _ in range(2):
+        split = fused.gemm(a_d, b_d, b_layout=layout, epilogue="bias_gelu_tanh", bias=bias_d, workspace=ws,
+                           config=cfg)
+        torch.testing.assert_close(split.float(), whole.float(), atol=1e-2, rtol=1e-2)
+    rows = slice(0, M, max(1, M // 64))
+    assert_close(split[rows], R.gemm_bias_act(a[rows], b, bias, "gelu_tanh", layout), TOL)
+    # the arrival counters at the start of the workspace come back zeroed
+    assert int(ws[:256].view(torch.int32).abs().sum()) == 0
+    status_clean()
