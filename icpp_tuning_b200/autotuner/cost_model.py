@@ -155,14 +155,14 @@ class TuneConfig:
         if self.kind == "tcgen05":
             # A and B stage rings + 4 warps x 2 x 4 KB epilogue staging + barriers / stats
             # + 1 KB alignment slack; equals fo_config_smem_bytes() of the C ABI.
-            return (1024 + self.num_stages * (self.block_M + self.block_N) * self.block_K * 2
-                    + 32768 + 1536)
+            b_cols = self.block_N // 2 if self.block_M == 256 else self.block_N
+            return 1024 + self.num_stages * (128 + b_cols) * self.block_K * 2 + 32768 + 1536
         return (self.block_M * self.block_K * 2 + self.block_K * self.block_N * 2) * self.num_stages
 
     @property
     def tmem_columns(self) -> int:
         """TMEM columns the kernel allocates: two fp32 accumulators of block_N columns."""
-        return 2 * self.block_N if self.kind == "tcgen05" else 0
+        return 2 * self.block_N if self.kind == "tcgen05" else 0  # per CTA (pairs too)
 
     @property
     def regs_per_thread_estimate(self) -> int:
@@ -174,8 +174,9 @@ class TuneConfig:
         """Static legality of the tile for a backend (the reference calls this method
         from search_space.py:194 but never defines it)."""
         if backend == "tcgen05":
-            return (self.kind == "tcgen05" and self.block_M == 128 and self.block_K == 64
-                    and self.block_N in (64, 128, 256) and 2 <= self.num_stages <= 8
+            return (self.kind == "tcgen05" and self.block_M in (128, 256) and self.block_K == 64
+                    and self.block_N in (64, 128, 256) and not (self.block_M == 256 and self.block_N < 128)
+                    and 2 <= self.num_stages <= 8
                     and self.tmem_columns <= 512 and self.shared_mem_bytes <= 232448)
         if backend == "triton":
             pow2 = lambda v: v >= 16 and (v & (v - 1)) == 0  # noqa: E731

@@ -32,10 +32,11 @@ _TRITON_CONV2D_PARAMS = {"block_M": [32, 64, 128], "block_N": [32, 64, 128], "bl
                          "num_stages": [2, 3, 4, 5], "num_warps": [2, 4, 8]}
 _TILELANG_CONV2D_PARAMS = {"block_M": [32, 48, 64, 96, 128], "block_N": [32, 64, 128],
                            "block_K": [16, 32, 64], "num_stages": [2, 3, 4], "num_warps": [4, 8]}
-# sm_100a kernels: tcgen05 M = 128, one 128-byte swizzle row of K, fixed role split.
-_TCGEN05_MATMUL_PARAMS = {"block_M": [128], "block_N": [64, 128, 256], "block_K": [64],
+# sm_100a kernels: tcgen05 M = 128 (one CTA) or 256 (a CTA pair, cta_group::2), one
+# 128-byte swizzle row of K, fixed role split.
+_TCGEN05_MATMUL_PARAMS = {"block_M": [128, 256], "block_N": [64, 128, 256], "block_K": [64],
                           "num_stages": [2, 3, 4, 5, 6, 7, 8], "num_warps": [6], "group_size_m": [0, 8, 16]}
-_TCGEN05_CONV2D_PARAMS = {"block_M": [128], "block_N": [64, 128, 256], "block_K": [64],
+_TCGEN05_CONV2D_PARAMS = {"block_M": [128, 256], "block_N": [64, 128, 256], "block_K": [64],
                           "num_stages": [3, 4, 5, 6, 7, 8], "num_warps": [9], "group_size_m": [0]}
 
 MIN_OCCUPANCY_THRESHOLD = 0.2
@@ -95,7 +96,9 @@ def generate_exhaustive_configs(op_type: str = "matmul", backend: str = "tilelan
     def rec(i, cur):
         if i == len(names):
             c = _to_tune_config(cur, backend)
-            if c.is_valid_for_backend(backend) or (backend == "tcgen05" and c.kind == "tcgen05"):
+            # tcgen05: shape legality here; the shared-memory budget is pruning level L1
+            shape_ok = c.kind == "tcgen05" and not (c.block_M == 256 and c.block_N < 128)
+            if c.is_valid_for_backend(backend) or (backend == "tcgen05" and shape_ok):
                 out.append(c)
             return
         for v in pools[names[i]]:

@@ -35,6 +35,8 @@ CONSTANTS = {
     # measured on B200 (4096^3 bf16, same stages / raster): BN=256 1267, BN=128 836,
     # BN=64 462 TFLOP/s -- narrow tiles are bound by shared-memory operand traffic
     "mma_rate_bn": {256: 1.0, 128: 0.66, 64: 0.37},
+    # CTA pairs (block_M 256): each SM reads half of B, so narrow tiles lose less
+    "mma_rate_bn_pair": {256: 1.05, 128: 0.9},
     "hbm_efficiency": 0.8,  # achievable fraction of the HBM figure in the GPU spec
     "mem_overlap": 0.35,  # share of the shorter of (compute, HBM) time that does not overlap
     "tma_latency_s": 1.2e-6,  # global -> shared latency a stage ring has to cover
@@ -88,16 +90,18 @@ def _model(op: OpSpec, c: TuneConfig, hw: GPUSpec) -> dict:
     K = CONSTANTS
     ml = op.mainloop
     bm, bn, bk = c.block_M, c.block_N, c.block_K
+    pair = bm == 256
     tiles_m, tiles_n = _cdiv(op.M, bm), _cdiv(op.N, bn)
     k_blocks = max(1, _cdiv(op.K, bk))
     tiles = tiles_m * tiles_n
-    sms = hw.num_sm
-    ctas = max(1, min(tiles, c.max_ctas if c.max_ctas > 0 else sms))
+    sms = hw.num_sm // 2 if pair else hw.num_sm  # persistent units: SMs or SM pairs
+    cap = (c.max_ctas // 2 if pair else c.max_ctas) if c.max_ctas > 0 else sms
+    ctas = max(1, min(tiles, cap))
     waves = _cdiv(tiles, ctas)
-    rate = _sm_rate(hw)
+    rate = _sm_rate(hw) * (2 if pair else 1)
 
     # -- mainloop: padded MMA work of one tile at the BN-dependent tensor rate
-    e_bn = K["mma_rate_bn"].get(bn, 0.6)
+    e_bn = (K["mma_rate_bn_pair"] if pair else K["mma_rate_bn"]).get(bn, 0.6)
     padding = (op.M * op.N * op.K) / float(tiles_m * bm * tiles_n * bn * k_blocks * bk)
     t_kb = 2.0 * bm * bn * bk / (rate * e_bn)
     # -- pipeline: stages - 1 loads in flight while one stage is consumed

@@ -19,27 +19,33 @@ SMEM_LIMIT = 232448
 
 
 def smem_bytes(block_n: int, stages: int, block_m: int = 128, block_k: int = 64) -> int:
-    """Dynamic shared memory of one CTA (= fo_config_smem_bytes of the C ABI)."""
-    return 1024 + stages * (block_m + block_n) * block_k * 2 + 32768 + 1536
+    """Dynamic shared memory of one CTA (= fo_config_smem_bytes of the C ABI).  block_m
+    256 is a CTA pair: each CTA holds 128 rows of A and half of the B tile."""
+    b_cols = block_n // 2 if block_m == 256 else block_n
+    return 1024 + stages * (128 + b_cols) * block_k * 2 + 32768 + 1536
 
 
-def max_stages(block_n: int) -> int:
+def max_stages(block_n: int, block_m: int = 128) -> int:
     s = 8
-    while s > 2 and smem_bytes(block_n, s) > SMEM_LIMIT:
+    while s > 2 and smem_bytes(block_n, s, block_m) > SMEM_LIMIT:
         s -= 1
     return s
 
 
 def tcgen05_configs(block_ns: Sequence[int] = (64, 128, 256), group_ms: Sequence[int] = (0, 8, 16),
-                    conv: bool = False, stages: Sequence[int] = ()) -> List[Dict[str, Any]]:
+                    conv: bool = False, stages: Sequence[int] = (),
+                    block_ms: Sequence[int] = (128, 256)) -> List[Dict[str, Any]]:
     out = []
-    for bn in block_ns:
-        top = max_stages(bn)
-        st = sorted({s for s in (stages or (3, 4, top)) if (3 if conv else 2) <= s <= top})
-        for s in st:
-            for g in group_ms:
-                out.append({"block_M": 128, "block_N": bn, "block_K": 64, "num_stages": s,
-                            "thread_num": CONV_THREADS if conv else GEMM_THREADS, "group_m": g})
+    for bm in block_ms:
+        for bn in block_ns:
+            if bm == 256 and bn < 128:
+                continue
+            top = max_stages(bn, bm)
+            st = sorted({s for s in (stages or (3, 4, top)) if (3 if conv else 2) <= s <= top})
+            for s in st:
+                for g in group_ms:
+                    out.append({"block_M": bm, "block_N": bn, "block_K": 64, "num_stages": s,
+                                "thread_num": CONV_THREADS if conv else GEMM_THREADS, "group_m": g})
     return out
 
 

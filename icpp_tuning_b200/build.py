@@ -20,7 +20,15 @@ INCLUDE = ROOT / "include"
 LIB = PKG / "libb200fo.so"
 OBJ = PKG / "_build"
 
-SOURCES = ["fo_api.cu", "fo_family_gemm.cu", "fo_family_ln.cu", "fo_family_conv.cu", "fo_noalloc.cu"]
+# (source, object name, extra flags)
+SOURCES = [
+    ("fo_api.cu", "fo_api", []),
+    ("fo_family_gemm.cu", "fo_family_gemm", ["-DFO_PAIR=0"]),
+    ("fo_family_gemm.cu", "fo_family_gemm_pair", ["-DFO_PAIR=1"]),
+    ("fo_family_ln.cu", "fo_family_ln", []),
+    ("fo_family_conv.cu", "fo_family_conv", []),
+    ("fo_noalloc.cu", "fo_noalloc", []),
+]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-O3",
          "--expt-relaxed-constexpr", f"-I{INCLUDE}", f"-I{CSRC}"]
@@ -34,7 +42,7 @@ def nvcc() -> str:
 
 
 def _deps() -> list[Path]:
-    return [CSRC / s for s in SOURCES] + list(CSRC.glob("*.cuh")) + [INCLUDE / "b200fo.h"]
+    return [CSRC / s for s, _, _ in SOURCES] + list(CSRC.glob("*.cuh")) + [INCLUDE / "b200fo.h"]
 
 
 def up_to_date() -> bool:
@@ -44,9 +52,10 @@ def up_to_date() -> bool:
     return all(p.stat().st_mtime <= t for p in _deps())
 
 
-def _compile(src: str, verbose: bool) -> Path:
-    obj = OBJ / (Path(src).stem + ".o")
-    cmd = [nvcc(), *ARCH, *FLAGS, "-c", str(CSRC / src), "-o", str(obj)]
+def _compile(item, verbose: bool) -> Path:
+    src, name, extra = item
+    obj = OBJ / (name + ".o")
+    cmd = [nvcc(), *ARCH, *FLAGS, *extra, "-c", str(CSRC / src), "-o", str(obj)]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     r = subprocess.run(cmd, capture_output=True, text=True)

@@ -175,7 +175,9 @@ int check_cfg(int op, int out_dtype, const FoTileCfg* cfg, char* why, size_t why
     return FO_EINVAL;
   };
   if (cfg == nullptr) return say("null config%d", 0);
-  if (cfg->block_m != 128) return say("block_m must be 128 (tcgen05 M with cta_group::1), got %d", cfg->block_m);
+  if (cfg->block_m != 128 && cfg->block_m != 256)
+    return say("block_m must be 128 (one CTA) or 256 (a CTA pair, tcgen05 cta_group::2), got %d", cfg->block_m);
+  if (cfg->block_m == 256 && cfg->block_n < 128) return say("CTA pairs (block_m 256) need block_n >= 128, got %d", cfg->block_n);
   if (cfg->block_n != 64 && cfg->block_n != 128 && cfg->block_n != 256)
     return say("block_n must be 64, 128 or 256, got %d", cfg->block_n);
   if (cfg->block_k != 64) return say("block_k must be 64 (one 128-byte swizzle row), got %d", cfg->block_k);
@@ -184,7 +186,7 @@ int check_cfg(int op, int out_dtype, const FoTileCfg* cfg, char* why, size_t why
     return say("stages out of range: %d", cfg->stages);
   if (cfg->group_m < 0) return say("group_m must be >= 0, got %d", cfg->group_m);
   if (cfg->max_ctas < 0) return say("max_ctas must be >= 0, got %d", cfg->max_ctas);
-  const int smem = fo::smem_bytes_for(cfg->block_n, cfg->stages);
+  const int smem = fo::smem_bytes_for(cfg->block_n, cfg->stages, cfg->block_m == 256);
   if (smem > 232448) return say("shared memory %d B exceeds the 227 KB per-block limit", smem);
   // TMEM: two fp32 accumulators of block_n columns each, <= 512 columns.
   if (2 * cfg->block_n > 512) return say("TMEM columns %d exceed 512", 2 * cfg->block_n);
@@ -291,7 +293,7 @@ int fo_set_wait_timeout_ns(uint64_t ns) {
 
 size_t fo_config_smem_bytes(int32_t op, int32_t out_dtype, const FoTileCfg* cfg) {
   if (check_cfg(op, out_dtype, cfg, nullptr, 0) != FO_OK) return 0;
-  return static_cast<size_t>(fo::smem_bytes_for(cfg->block_n, cfg->stages));
+  return static_cast<size_t>(fo::smem_bytes_for(cfg->block_n, cfg->stages, cfg->block_m == 256));
 }
 
 int fo_query_config_legal(int32_t op, int32_t out_dtype, const FoTileCfg* cfg, char* why,
@@ -310,6 +312,7 @@ size_t fo_gemm_workspace_size(const FoGemmDesc* d, const FoTileCfg* cfg) {
   if (d->M <= 0 || d->N <= 0) return 0;
   if (d->epilogue == FO_EPI_BIAS_LN) return ln_workspace(d->M, d->N, cfg->block_n);
   // Other epilogues: room for the split-K tail (optional; without it there is no split).
+  if (cfg->block_m == 256) return 0;  // CTA pairs run whole tiles only
   const int bn = cfg->block_n;
   const int tiles = static_cast<int>(((d->M + 127) / 128) * ((d->N + bn - 1) / bn));
   const int cap = cfg->max_ctas > 0 ? cfg->max_ctas : sm_count_or_default();
@@ -371,7 +374,8 @@ int fo_gemm(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
   p.M = static_cast<int>(d->M);
   p.N = static_cast<int>(d->N);
   p.K = static_cast<int>(d->K);
-  p.tiles_m = (p.M + 127) / 128;
+  const bool pair = cfg->block_m == 256;
+  p.tiles_m = (p.M + cfg->block_m - 1) / cfg->block_m;
   p.tiles_n = (p.N + bn - 1) / bn;
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.k_blocks = (p.K + 63) / 64;
@@ -389,22 +393,25 @@ int fo_gemm(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
   p.ldo = d->ldo;
   if (ln) {
     p.ln_stats = reinterpret_cast<float4*>(static_cast<char*>(d->workspace) +
-                                           round_up(static_cast<size_t>(p.tiles_m) * 4, 256));
+                                           round_up(static_cast<size_t>((p.M + 127) / 128) * 4, 256));
   }
   fill_common(p, di);
 
   if (p.K > 0) {
     if (int rc = make_tmap(&la.tmA, d->in_dtype, d->a, d->K, d->M, d->lda * ib, 64, 128, "A")) return rc;
     if (d->b_layout == FO_B_NK) {
-      if (int rc = make_tmap(&la.tmB, d->in_dtype, d->b, d->K, d->N, d->ldb * ib, 64, bn, "B")) return rc;
+      if (int rc = make_tmap(&la.tmB, d->in_dtype, d->b, d->K, d->N, d->ldb * ib, 64, pair ? bn / 2 : bn, "B"))
+        return rc;
     } else {
       if (int rc = make_tmap(&la.tmB, d->in_dtype, d->b, d->N, d->K, d->ldb * ib, 64, 64, "B")) return rc;
     }
   }
   if (int rc = make_tmap(&la.tmC, d->out_dtype, d->out, d->N, d->M, d->ldo * ob, 128 / ob, 32, "out")) return rc;
 
-  const int cap = cfg->max_ctas > 0 ? cfg->max_ctas : di.sms;
-  SplitPlan pl = plan_split(p.num_tiles, p.k_blocks, cap, !ln);
+  // Persistent grid: one CTA (or CTA pair) per SM (pair of SMs).
+  const int cap = pair ? (cfg->max_ctas > 0 ? cfg->max_ctas / 2 : di.sms / 2) : (cfg->max_ctas > 0 ? cfg->max_ctas : di.sms);
+  if (cap < 1) return fail(FO_EINVAL, "max_ctas too small for CTA pairs");
+  SplitPlan pl = plan_split(p.num_tiles, p.k_blocks, cap, !ln && !pair);
   const size_t split_need = split_workspace(pl, bn);
   if (split_need == 0 || d->workspace == nullptr || d->workspace_bytes < split_need || !aligned16(d->workspace))
     pl = plan_split(p.num_tiles, p.k_blocks, cap, false);  // no room for partials: whole tiles only
@@ -417,8 +424,9 @@ int fo_gemm(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
     p.split_ws = reinterpret_cast<float*>(static_cast<char*>(d->workspace) +
                                           round_up(static_cast<size_t>(pl.split_tiles) * 4 * sizeof(int), 256));
   }
-  la.grid = pl.grid;
-  la.smem = fo::smem_bytes_for(bn, cfg->stages);
+  la.grid = pair ? 2 * pl.grid : pl.grid;
+  la.pair = pair;
+  la.smem = fo::smem_bytes_for(bn, cfg->stages, pair);
   la.stream = static_cast<cudaStream_t>(stream);
   const int out_dt = d->out_dtype == FO_DT_F16 ? fo::DT_F16 : d->out_dtype == FO_DT_BF16 ? fo::DT_BF16 : fo::DT_F32;
   cudaError_t e = ln ? fo::launch_ln_family(bn, out_dt, la) : fo::launch_gemm_family(bn, act, out_dt, la);
@@ -468,9 +476,9 @@ int fo_conv2d(const FoConvDesc* d, const FoTileCfg* cfg, void* stream) {
   p.M = static_cast<int>(M64);
   p.N = d->f;
   p.K = static_cast<int>(K64);
-  p.tiles_m = (p.M + 127) / 128;
+  // CTA pairs need the TMA im2col producer; without it the conv runs as single CTAs.
+  bool pair = cfg->block_m == 256;
   p.tiles_n = (p.N + bn - 1) / bn;
-  p.num_tiles = p.tiles_m * p.tiles_n;
   p.c_blocks = (d->c + 63) / 64;
   p.k_blocks = d->kh * d->kw * p.c_blocks;
   p.group_m = cfg->group_m;
@@ -495,17 +503,23 @@ int fo_conv2d(const FoConvDesc* d, const FoTileCfg* cfg, void* stream) {
   p.dil = d->dil;
   fill_common(p, di);
   p.conv_tma = (d->stride <= 8 && !conv_gather_forced() && make_im2col_map(&la.tmA, d)) ? 1 : 0;
+  if (!p.conv_tma) pair = false;
+  const int tile_m = pair ? 256 : 128;
+  p.tiles_m = (p.M + tile_m - 1) / tile_m;
+  p.num_tiles = p.tiles_m * p.tiles_n;
   if (int rc = make_tmap(&la.tmB, d->in_dtype, d->wgt, d->f, K64, static_cast<uint64_t>(d->f) * 2, 64, 64, "weights"))
     return rc;
   if (int rc = make_tmap(&la.tmC, d->out_dtype, d->out, d->f, M64, static_cast<uint64_t>(d->f) * ob, 128 / ob, 32,
                          "out"))
     return rc;
-  const int cap = cfg->max_ctas > 0 ? cfg->max_ctas : di.sms;
-  la.grid = p.num_tiles < cap ? p.num_tiles : cap;
+  const int cap = pair ? (cfg->max_ctas > 0 ? cfg->max_ctas / 2 : di.sms / 2) : (cfg->max_ctas > 0 ? cfg->max_ctas : di.sms);
+  if (cap < 1) return fail(FO_EINVAL, "max_ctas too small for CTA pairs");
+  la.grid = (p.num_tiles < cap ? p.num_tiles : cap) * (pair ? 2 : 1);
+  la.pair = pair;
   p.num_units = p.dp_units = p.num_tiles;  // whole tiles
   p.split = 1;
   p.kb_per_part = p.k_blocks;
-  la.smem = fo::smem_bytes_for(bn, cfg->stages);
+  la.smem = fo::smem_bytes_for(bn, cfg->stages, pair);
   la.stream = static_cast<cudaStream_t>(stream);
   const int out_dt = d->out_dtype == FO_DT_F16 ? fo::DT_F16 : d->out_dtype == FO_DT_BF16 ? fo::DT_BF16 : fo::DT_F32;
   cudaError_t e = fo::launch_conv_family(bn, act, out_dt, la);

@@ -1,20 +1,28 @@
-// Instantiations of the plain / bias / activation GEMM kernels.
+// Instantiations of the plain / bias / activation GEMM kernels.  Compiled twice:
+// FO_PAIR = 0 (one CTA per 128-row tile) and FO_PAIR = 1 (CTA pairs, 256-row tiles).
 #include "fo_launch.cuh"
 
+#ifndef FO_PAIR
+#define FO_PAIR 0
+#endif
+
 namespace fo {
+namespace {
+
+constexpr bool kPair = FO_PAIR != 0;
 
 template <int BN, int ACT>
-static cudaError_t by_out(int out_dt, const LaunchArgs& a) {
+cudaError_t by_out(int out_dt, const LaunchArgs& a) {
   switch (out_dt) {
-    case DT_F16: return launch_tc<BN, ACT, DT_F16, false, false>(a);
-    case DT_BF16: return launch_tc<BN, ACT, DT_BF16, false, false>(a);
-    case DT_F32: return launch_tc<BN, ACT, DT_F32, false, false>(a);
+    case DT_F16: return launch_tc<BN, ACT, DT_F16, false, false, kPair>(a);
+    case DT_BF16: return launch_tc<BN, ACT, DT_BF16, false, false, kPair>(a);
+    case DT_F32: return launch_tc<BN, ACT, DT_F32, false, false, kPair>(a);
   }
   return cudaErrorInvalidValue;
 }
 
 template <int BN>
-static cudaError_t by_act(int act, int out_dt, const LaunchArgs& a) {
+cudaError_t by_act(int act, int out_dt, const LaunchArgs& a) {
   switch (act) {
     case ACT_NONE: return by_out<BN, ACT_NONE>(out_dt, a);
     case ACT_RELU: return by_out<BN, ACT_RELU>(out_dt, a);
@@ -24,7 +32,18 @@ static cudaError_t by_act(int act, int out_dt, const LaunchArgs& a) {
   return cudaErrorInvalidValue;
 }
 
-cudaError_t launch_gemm_family(int bn, int act, int out_dt, const LaunchArgs& a) {
+}  // namespace
+
+#if FO_PAIR
+cudaError_t launch_gemm_family_pair(int bn, int act, int out_dt, const LaunchArgs& a) {
+  switch (bn) {
+    case 128: return by_act<128>(act, out_dt, a);
+    case 256: return by_act<256>(act, out_dt, a);
+  }
+  return cudaErrorInvalidValue;
+}
+#else
+cudaError_t launch_gemm_family_single(int bn, int act, int out_dt, const LaunchArgs& a) {
   switch (bn) {
     case 64: return by_act<64>(act, out_dt, a);
     case 128: return by_act<128>(act, out_dt, a);
@@ -32,5 +51,10 @@ cudaError_t launch_gemm_family(int bn, int act, int out_dt, const LaunchArgs& a)
   }
   return cudaErrorInvalidValue;
 }
+
+cudaError_t launch_gemm_family(int bn, int act, int out_dt, const LaunchArgs& a) {
+  return a.pair ? launch_gemm_family_pair(bn, act, out_dt, a) : launch_gemm_family_single(bn, act, out_dt, a);
+}
+#endif
 
 }  // namespace fo

@@ -7,7 +7,12 @@ namespace fo {
 // GEMM + bias + slice statistics, then the stream-ordered normalisation pass.
 template <int BN, int OUT>
 static cudaError_t gemm_then_normalize(const LaunchArgs& a) {
-  cudaError_t e = launch_tc<BN, ACT_NONE, OUT, true, false>(a);
+  cudaError_t e;
+  if constexpr (BN >= 128) {
+    e = a.pair ? launch_tc<BN, ACT_NONE, OUT, true, false, true>(a) : launch_tc<BN, ACT_NONE, OUT, true, false, false>(a);
+  } else {
+    e = a.pair ? cudaErrorInvalidValue : launch_tc<BN, ACT_NONE, OUT, true, false, false>(a);
+  }
   if (e != cudaSuccess) return e;
   const int blocks = (a.p.M + 7) / 8;
   fo_ln_normalize_kernel<OUT><<<blocks, 256, 0, a.stream>>>(a.p, BN);

@@ -73,8 +73,9 @@ struct KParams {
 };
 
 __host__ __device__ constexpr int b_stage_bytes(int bn) { return bn * kBK * 2; }
-__host__ __device__ constexpr int smem_bytes_for(int bn, int stages) {
-  return 1024 + stages * (kAStageBytes + b_stage_bytes(bn)) + kEpiBytes + kMiscBytes;
+// pair: CTA-pair kernel (block_m 256), where each CTA holds half of the B tile.
+__host__ __device__ constexpr int smem_bytes_for(int bn, int stages, bool pair = false) {
+  return 1024 + stages * (kAStageBytes + b_stage_bytes(pair ? bn / 2 : bn)) + kEpiBytes + kMiscBytes;
 }
 
 __device__ __forceinline__ void record_error(const KParams& p, int code, int where) {
@@ -208,14 +209,20 @@ __device__ __forceinline__ void drain_loads(uint32_t bar_full, int stages, int i
   }
 }
 
-template <int BN, int ACT, int OUT_DT, bool LN, bool CONV>
+template <int BN, int ACT, int OUT_DT, bool LN, bool CONV, bool PAIR>
 __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
     fo_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const __grid_constant__ CUtensorMap tmC, const KParams p) {
   constexpr int kProducerWarps = CONV ? 4 : 1;
   constexpr int kMmaWarp = kProducerWarps;
   constexpr int kFirstEpiWarp = kProducerWarps + 1;
-  constexpr int kBStage = b_stage_bytes(BN);
+  // PAIR: a cluster of two CTAs computes one 256 x BN tile with tcgen05 cta_group::2;
+  // CTA r loads rows r*128.. of A and columns r*BN/2.. of B, holds rows r*128.. of the
+  // accumulator in its TMEM and stores them.  The leader (rank 0) issues the MMAs.
+  constexpr int kBHalf = PAIR ? BN / 2 : BN;  // B columns this CTA loads
+  constexpr int kTileM = PAIR ? 2 * kBM : kBM;
+  constexpr int kBStage = b_stage_bytes(kBHalf);
+  static_assert(!PAIR || BN >= 128, "CTA pairs need BN >= 128");
   constexpr int kOutBytes = OUT_DT == DT_F32 ? 4 : 2;
   constexpr int kCPC = 128 / kOutBytes;  // output columns per 128-byte chunk
   constexpr int kChunks = BN / kCPC;
@@ -243,6 +250,9 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0;
+  const int cid = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int ncl = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
@@ -251,15 +261,20 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(bar_tfull + 8 * a, 1);
-      mbar_init(bar_tempty + 8 * a, kEpiWarps);
+      mbar_init(bar_tempty + 8 * a, PAIR ? 2 * kEpiWarps : kEpiWarps);
     }
     mbar_init(bar_drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == kMmaWarp) {
-    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(smem_u32(tmem_slot), kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+      tmem_relinquish();
+    }
   }
   if (threadIdx.x == 32 * kFirstEpiWarp) {
     tma_prefetch_desc(&tmC);
@@ -270,6 +285,7 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // both CTAs' barriers exist before any remote use
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const uint64_t tmo = p.timeout_ns;
@@ -282,7 +298,7 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
         uint32_t ph = 0;
         int issued = 0;  // stage loads issued by this thread
         bool ok = true;
-        for (int u = blockIdx.x; u < p.num_units && ok; u += gridDim.x) {
+        for (int u = cid; u < p.num_units && ok; u += ncl) {
           const Unit un = unit_of(p, u);
           const int tm = un.tm, tn = un.tn;
           for (int kb = un.kb0; kb < un.kb1; ++kb) {
@@ -291,14 +307,30 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
               break;
             }
             const uint32_t fb = bar_full + 8 * s;
-            mbar_arrive_expect_tx(fb, kAStageBytes + kBStage);
-            tma_load_2d(sA + s * kAStageBytes, &tmA, fb, kb * kBK, tm * kBM);
-            if (p.b_mn) {
+            const int arow = tm * kTileM + static_cast<int>(rank) * kBM;
+            const int bcol = tn * BN + static_cast<int>(rank) * kBHalf;
+            if constexpr (PAIR) {
+              // Both CTAs' bytes complete on the leader's barrier; only the leader arrives.
+              const uint32_t fbl = mapa_shared(fb, 0);
+              if (rank == 0) mbar_arrive_expect_tx(fb, 2 * (kAStageBytes + kBStage));
+              tma_load_2d_pair(sA + s * kAStageBytes, &tmA, fbl, kb * kBK, arow);
+              if (p.b_mn) {
 #pragma unroll
-              for (int j = 0; j < BN / 64; ++j)
-                tma_load_2d(sB + s * kBStage + j * 64 * 128, &tmB, fb, tn * BN + j * 64, kb * kBK);
+                for (int j = 0; j < kBHalf / 64; ++j)
+                  tma_load_2d_pair(sB + s * kBStage + j * 64 * 128, &tmB, fbl, bcol + j * 64, kb * kBK);
+              } else {
+                tma_load_2d_pair(sB + s * kBStage, &tmB, fbl, kb * kBK, bcol);
+              }
             } else {
-              tma_load_2d(sB + s * kBStage, &tmB, fb, kb * kBK, tn * BN);
+              mbar_arrive_expect_tx(fb, kAStageBytes + kBStage);
+              tma_load_2d(sA + s * kAStageBytes, &tmA, fb, kb * kBK, arow);
+              if (p.b_mn) {
+#pragma unroll
+                for (int j = 0; j < BN / 64; ++j)
+                  tma_load_2d(sB + s * kBStage + j * 64 * 128, &tmB, fb, bcol + j * 64, kb * kBK);
+              } else {
+                tma_load_2d(sB + s * kBStage, &tmB, fb, kb * kBK, bcol);
+              }
             }
             ++issued;
             if (++s == stages) {
@@ -311,7 +343,9 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
           record_error(p, kStatusTimeout, 0x10);
           *abort_flag = 1;
         }
-        drain_loads(bar_full, stages, issued);
+        // A pair's loads complete on the leader's barriers: the leader drains both CTAs'
+        // loads, and the closing cluster barrier keeps the peer alive until then.
+        if (!PAIR || rank == 0) drain_loads(bar_full, stages, issued);
       }
     } else if (p.conv_tma) {
       // conv, TMA im2col: one thread loads each 128-pixel x 64-channel A tile of the
@@ -322,10 +356,10 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
         int issued = 0;
         bool ok = true;
         const int ohow = p.OH * p.OW;
-        for (int u = blockIdx.x; u < p.num_units && ok; u += gridDim.x) {
+        for (int u = cid; u < p.num_units && ok; u += ncl) {
           const Unit un = unit_of(p, u);
           const int tm = un.tm, tn = un.tn;
-          const int m0 = tm * kBM;
+          const int m0 = tm * kTileM + static_cast<int>(rank) * kBM;
           const int n_img = m0 / ohow;
           const int rem = m0 - n_img * ohow;
           const int oh = rem / p.OW;
@@ -342,12 +376,22 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
               break;
             }
             const uint32_t fb = bar_full + 8 * s;
-            mbar_arrive_expect_tx(fb, kAStageBytes + kBStage);
-            tma_load_im2col_4d(sA + s * kAStageBytes, &tmA, fb, cb * kBK, w0, h0, n_img,
-                               static_cast<uint16_t>(kw * p.dil), static_cast<uint16_t>(kh * p.dil));
+            const int bcol = tn * BN + static_cast<int>(rank) * kBHalf;
+            const uint16_t ow16 = static_cast<uint16_t>(kw * p.dil), oh16 = static_cast<uint16_t>(kh * p.dil);
+            if constexpr (PAIR) {
+              const uint32_t fbl = mapa_shared(fb, 0);
+              if (rank == 0) mbar_arrive_expect_tx(fb, 2 * (kAStageBytes + kBStage));
+              tma_load_im2col_4d_pair(sA + s * kAStageBytes, &tmA, fbl, cb * kBK, w0, h0, n_img, ow16, oh16);
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j)
-              tma_load_2d(sB + s * kBStage + j * 64 * 128, &tmB, fb, tn * BN + j * 64, tap * p.C + cb * kBK);
+              for (int j = 0; j < kBHalf / 64; ++j)
+                tma_load_2d_pair(sB + s * kBStage + j * 64 * 128, &tmB, fbl, bcol + j * 64, tap * p.C + cb * kBK);
+            } else {
+              mbar_arrive_expect_tx(fb, kAStageBytes + kBStage);
+              tma_load_im2col_4d(sA + s * kAStageBytes, &tmA, fb, cb * kBK, w0, h0, n_img, ow16, oh16);
+#pragma unroll
+              for (int j = 0; j < BN / 64; ++j)
+                tma_load_2d(sB + s * kBStage + j * 64 * 128, &tmB, fb, bcol + j * 64, tap * p.C + cb * kBK);
+            }
             ++issued;
             if (++s == stages) {
               s = 0;
@@ -359,7 +403,9 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
           record_error(p, kStatusTimeout, 0x12);
           *abort_flag = 1;
         }
-        drain_loads(bar_full, stages, issued);
+        // A pair's loads complete on the leader's barriers: the leader drains both CTAs'
+        // loads, and the closing cluster barrier keeps the peer alive until then.
+        if (!PAIR || rank == 0) drain_loads(bar_full, stages, issued);
       }
     } else {
       // conv gather: thread i of the warpgroup owns row i (one output pixel) of the A tile.
@@ -371,7 +417,7 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
       bool ok = true;
       const int ohow = p.OH * p.OW;
       const char* xb = reinterpret_cast<const char*>(p.x);
-      for (int u = blockIdx.x; u < p.num_units && ok; u += gridDim.x) {
+      for (int u = cid; u < p.num_units && ok; u += ncl) {
         const Unit un = unit_of(p, u);
         const int tm = un.tm, tn = un.tn;
         const int m = tm * kBM + i;
@@ -445,16 +491,21 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc = idesc_f16(p.ab_bf16, p.b_mn, BN);
+    if (lane == 0 && rank == 0) {
+      const uint32_t idesc = idesc_f16(p.ab_bf16, p.b_mn, BN, kTileM);
+      const uint64_t a_desc0 = sdesc_sw128(sA, 16, 1024);
+      const uint64_t b_desc0 = p.b_mn ? sdesc_sw128(sB, 64 * 128, 1024) : sdesc_sw128(sB, 16, 1024);
+      const uint32_t b_kstep = p.b_mn ? (2048 >> 4) : (32 >> 4);
       int s = 0;
       uint32_t ph = 0;
       int acc = 0;
       uint32_t acc_ph = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < p.num_units && ok; u += gridDim.x) {
+      for (int u = cid; u < p.num_units && ok; u += ncl) {
         const Unit un = unit_of(p, u);
-        if (!mbar_wait(bar_tempty + 8 * acc, acc_ph ^ 1, tmo, abort_flag)) {
+        const bool freed = PAIR ? mbar_wait_cluster(bar_tempty + 8 * acc, acc_ph ^ 1, tmo, abort_flag)
+                                : mbar_wait(bar_tempty + 8 * acc, acc_ph ^ 1, tmo, abort_flag);
+        if (!freed) {
           ok = false;
           break;
         }
@@ -466,23 +517,39 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = sA + s * kAStageBytes;
-          const uint32_t b0 = sB + s * kBStage;
+          // Descriptors of this stage; the K step is an add on the start-address field
+          // (+32 B for K-major rows, +2048 B = 16 rows for MN-major B).
+          const uint64_t ad0 = a_desc0 + static_cast<uint64_t>((s * kAStageBytes) >> 4);
+          const uint64_t bd0 = b_desc0 + static_cast<uint64_t>((s * kBStage) >> 4);
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
-            const uint64_t ad = sdesc_sw128(a0 + k * 32, 16, 1024);
-            const uint64_t bd = p.b_mn ? sdesc_sw128(b0 + k * 2048, 64 * 128, 1024)
-                                       : sdesc_sw128(b0 + k * 32, 16, 1024);
-            tc_mma_f16(d, ad, bd, idesc, (kb != un.kb0 || k != 0) ? 1u : 0u);
+            const uint64_t ad = ad0 + static_cast<uint64_t>(2 * k);
+            const uint64_t bd = bd0 + static_cast<uint64_t>(k * b_kstep);
+            const uint32_t accum = (kb != un.kb0 || k != 0) ? 1u : 0u;
+            if constexpr (PAIR) {
+              tc_mma_f16_pair(d, ad, bd, idesc, accum);
+            } else {
+              tc_mma_f16(d, ad, bd, idesc, accum);
+            }
           }
-          tc_commit(bar_empty + 8 * s);
+          if constexpr (PAIR) {  // free the stage in both CTAs
+            tc_commit_pair(mapa_shared(bar_empty + 8 * s, 0));
+            tc_commit_pair(mapa_shared(bar_empty + 8 * s, 1));
+          } else {
+            tc_commit(bar_empty + 8 * s);
+          }
           if (++s == stages) {
             s = 0;
             ph ^= 1;
           }
         }
         if (!ok) break;
-        tc_commit(bar_tfull + 8 * acc);
+        if constexpr (PAIR) {  // both halves of the accumulator are ready
+          tc_commit_pair(mapa_shared(bar_tfull + 8 * acc, 0));
+          tc_commit_pair(mapa_shared(bar_tfull + 8 * acc, 1));
+        } else {
+          tc_commit(bar_tfull + 8 * acc);
+        }
         acc ^= 1;
         if (acc == 0) acc_ph ^= 1;
       }
@@ -491,7 +558,11 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
         *abort_flag = 1;
       }
       // Drain: all issued MMAs complete before TMEM is released.
-      tc_commit(bar_drain);
+      if constexpr (PAIR) {
+        tc_commit_pair(mapa_shared(bar_drain, 0));
+      } else {
+        tc_commit(bar_drain);
+      }
       mbar_wait(bar_drain, 0, kDrainTimeoutNs, nullptr);
     }
   } else if (warp < kFirstEpiWarp + kEpiWarps) {
@@ -504,7 +575,7 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
     uint32_t acc_ph = 0;
     uint32_t nstore = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
+    for (int u = cid; u < p.num_units; u += ncl) {
       const Unit un = unit_of(p, u);
       const int tm = un.tm, tn = un.tn;
       const bool has_k = un.kb1 > un.kb0;
@@ -513,7 +584,7 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
         break;
       }
       tc_fence_after();
-      const int row0 = tm * kBM + quarter * 32;
+      const int row0 = tm * kTileM + static_cast<int>(rank) * kBM + quarter * 32;
       const int col0 = tn * BN;
       // Split tile: publish this part's fp32 partial ([column][128 rows], coalesced), then
       // the warp whose arrival completes its row quarter adds the other parts and runs
@@ -538,7 +609,13 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
         if (!last) {
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(bar_tempty + 8 * acc);
+          if (lane == 0) {
+            if constexpr (PAIR) {
+              mbar_arrive_cluster(mapa_shared(bar_tempty + 8 * acc, 0));
+            } else {
+              mbar_arrive(bar_tempty + 8 * acc);
+            }
+          }
           acc ^= 1;
           if (acc == 0) acc_ph ^= 1;
           continue;
@@ -578,7 +655,13 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
           // The accumulator buffer is free once every lane's loads of it have completed.
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(bar_tempty + 8 * acc);
+          if (lane == 0) {
+            if constexpr (PAIR) {
+              mbar_arrive_cluster(mapa_shared(bar_tempty + 8 * acc, 0));
+            } else {
+              mbar_arrive(bar_tempty + 8 * acc);
+            }
+          }
         }
         if (p.has_bias) {
 #pragma unroll
@@ -665,9 +748,14 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
 
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // no CTA leaves while its peer may still use it
   if (warp == kMmaWarp) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    if constexpr (PAIR) {
+      tmem_dealloc_pair(tmem_base, kTmemCols);
+    } else {
+      tmem_dealloc(tmem_base, kTmemCols);
+    }
   }
 }
 

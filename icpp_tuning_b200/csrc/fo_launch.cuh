@@ -12,14 +12,15 @@ namespace fo {
 struct LaunchArgs {
   CUtensorMap tmA, tmB, tmC;
   KParams p;
-  int grid;
+  int grid;  // CTAs (for CTA pairs: 2 x clusters)
   int smem;
   cudaStream_t stream;
+  bool pair;  // launch as clusters of two CTAs (block_m 256, tcgen05 cta_group::2)
 };
 
-template <int BN, int ACT, int OUT_DT, bool LN, bool CONV>
+template <int BN, int ACT, int OUT_DT, bool LN, bool CONV, bool PAIR>
 cudaError_t launch_tc(const LaunchArgs& a) {
-  auto kern = fo_tc_kernel<BN, ACT, OUT_DT, LN, CONV>;
+  auto kern = fo_tc_kernel<BN, ACT, OUT_DT, LN, CONV, PAIR>;
   // Opt in to the full 227 KB of dynamic shared memory once per device.
   static std::atomic<uint64_t> opted{0};
   int dev = 0;
@@ -31,12 +32,43 @@ cudaError_t launch_tc(const LaunchArgs& a) {
     opted.fetch_or(bit, std::memory_order_acq_rel);
   }
   constexpr int kThreads = CONV ? 288 : 192;
-  kern<<<a.grid, kThreads, a.smem, a.stream>>>(a.tmA, a.tmB, a.tmC, a.p);
-  return cudaGetLastError();
+  if constexpr (PAIR) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.grid, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = a.smem;
+    cfg.stream = a.stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    // A persistent grid larger than the number of co-resident pairs would leave a tail
+    // wave: clamp to what the GPU can hold at once (queried once per device).
+    static std::atomic<int> max_clusters[64];
+    int mc = max_clusters[dev & 63].load(std::memory_order_relaxed);
+    if (mc == 0) {
+      if (cudaOccupancyMaxActiveClusters(&mc, kern, &cfg) != cudaSuccess || mc <= 0) {
+        cudaGetLastError();
+        mc = -1;
+      }
+      max_clusters[dev & 63].store(mc, std::memory_order_relaxed);
+    }
+    if (mc > 0 && static_cast<int>(cfg.gridDim.x) > 2 * mc) cfg.gridDim.x = 2 * mc;
+    return cudaLaunchKernelEx(&cfg, kern, a.tmA, a.tmB, a.tmC, a.p);
+  } else {
+    kern<<<a.grid, kThreads, a.smem, a.stream>>>(a.tmA, a.tmB, a.tmC, a.p);
+    return cudaGetLastError();
+  }
 }
 
 // Returns cudaErrorInvalidValue for a combination this build does not instantiate.
+// The gemm family is compiled twice (fo_family_gemm.cu with FO_PAIR 0 and 1).
 cudaError_t launch_gemm_family(int bn, int act, int out_dt, const LaunchArgs& a);
+cudaError_t launch_gemm_family_single(int bn, int act, int out_dt, const LaunchArgs& a);
+cudaError_t launch_gemm_family_pair(int bn, int act, int out_dt, const LaunchArgs& a);
 cudaError_t launch_ln_family(int bn, int out_dt, const LaunchArgs& a);
 cudaError_t launch_conv_family(int bn, int act, int out_dt, const LaunchArgs& a);
 

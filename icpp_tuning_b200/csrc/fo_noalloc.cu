@@ -155,7 +155,8 @@ int run(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
   p.M = static_cast<int>(d->M);
   p.N = static_cast<int>(d->N);
   p.K = static_cast<int>(d->K);
-  p.tiles_m = (p.M + 127) / 128;
+  const bool pair = cfg->block_m == 256;
+  p.tiles_m = (p.M + cfg->block_m - 1) / cfg->block_m;
   p.tiles_n = (p.N + bn - 1) / bn;
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.k_blocks = (p.K + 63) / 64;
@@ -172,7 +173,7 @@ int run(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
   p.out = d->out;
   p.ldo = d->ldo;
   // Same layout as fo_gemm's workspace: a reserved 256-byte-aligned header, then the stats.
-  const size_t header_bytes = round_up(static_cast<size_t>(p.tiles_m) * 4, 256);
+  const size_t header_bytes = round_up(static_cast<size_t>((p.M + 127) / 128) * 4, 256);
   p.ln_stats = reinterpret_cast<float4*>(static_cast<char*>(scratch) + header_bytes);
   p.status = status;
   p.timeout_ns = 2000000000ull;
@@ -180,7 +181,7 @@ int run(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
   if (p.K > 0) {
     if (int rc = tmap(&la.tmA, d->in_dtype, d->a, d->K, d->M, d->lda * 2, 64, 128)) return rc;
     if (d->b_layout == FO_B_NK) {
-      if (int rc = tmap(&la.tmB, d->in_dtype, d->b, d->K, d->N, d->ldb * 2, 64, bn)) return rc;
+      if (int rc = tmap(&la.tmB, d->in_dtype, d->b, d->K, d->N, d->ldb * 2, 64, pair ? bn / 2 : bn)) return rc;
     } else {
       if (int rc = tmap(&la.tmB, d->in_dtype, d->b, d->N, d->K, d->ldb * 2, 64, 64)) return rc;
     }
@@ -188,12 +189,14 @@ int run(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
   if (int rc = tmap(&la.tmC, d->out_dtype, d->out, d->N, d->M, d->ldo * 2, 64, 32)) return rc;
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int cap = cfg->max_ctas > 0 ? cfg->max_ctas : sms;
-  la.grid = p.num_tiles < cap ? p.num_tiles : cap;
+  const int cap = pair ? (cfg->max_ctas > 0 ? cfg->max_ctas / 2 : sms / 2) : (cfg->max_ctas > 0 ? cfg->max_ctas : sms);
+  if (cap < 1) return say(FO_EINVAL, "max_ctas too small for CTA pairs");
+  la.grid = (p.num_tiles < cap ? p.num_tiles : cap) * (pair ? 2 : 1);
+  la.pair = pair;
   p.num_units = p.dp_units = p.num_tiles;  // whole tiles
   p.split = 1;
   p.kb_per_part = p.k_blocks;
-  la.smem = fo::smem_bytes_for(bn, cfg->stages);
+  la.smem = fo::smem_bytes_for(bn, cfg->stages, pair);
   la.stream = st;
   cudaError_t e = fo::launch_ln_family(bn, d->out_dtype == FO_DT_F16 ? fo::DT_F16 : fo::DT_BF16, la);
   if (e != cudaSuccess) {

@@ -24,12 +24,14 @@ SHAPES = [
 @pytest.mark.parametrize("conv", [False, True])
 def test_every_config_legal_for_the_library(conv):
     for raw in tcgen05_configs(conv=conv, stages=range(2, 9)):
-        cfg = N.tile_cfg(block_n=raw["block_N"], stages=raw["num_stages"], group_m=raw["group_m"])
+        cfg = N.tile_cfg(block_n=raw["block_N"], stages=raw["num_stages"], group_m=raw["group_m"],
+                         block_m=raw["block_M"])
         ok, why = N.config_legal(1 if conv else 0, N.FO_DT_BF16, cfg)
         assert ok, why
-        assert N.config_smem_bytes(1 if conv else 0, N.FO_DT_BF16, cfg) == smem_bytes(raw["block_N"], raw["num_stages"])
-        tc = TuneConfig(128, raw["block_N"], 64, raw["num_stages"], raw["thread_num"] // 32, kind="tcgen05")
-        assert tc.shared_mem_bytes == smem_bytes(raw["block_N"], raw["num_stages"])
+        want = smem_bytes(raw["block_N"], raw["num_stages"], raw["block_M"])
+        assert N.config_smem_bytes(1 if conv else 0, N.FO_DT_BF16, cfg) == want
+        tc = TuneConfig(raw["block_M"], raw["block_N"], 64, raw["num_stages"], raw["thread_num"] // 32, kind="tcgen05")
+        assert tc.shared_mem_bytes == want
         assert tc.is_valid_for_backend("tcgen05")
 
 
@@ -39,6 +41,10 @@ def test_library_rejects_illegal_configs():
         assert not ok and why in msg
     ok, msg = N.config_legal(0, N.FO_DT_BF16, N.tile_cfg(block_n=128, stages=4, block_m=64))
     assert not ok and "block_m" in msg
+    ok, msg = N.config_legal(0, N.FO_DT_BF16, N.tile_cfg(block_n=64, stages=4, block_m=256))
+    assert not ok and "block_n >= 128" in msg
+    ok, msg = N.config_legal(0, N.FO_DT_BF16, N.tile_cfg(block_n=256, stages=6, block_m=256))
+    assert ok, msg
     ok, msg = N.config_legal(1, N.FO_DT_BF16, N.tile_cfg(block_n=128, stages=2))
     assert not ok  # conv producer needs >= 3 stages
 
@@ -49,7 +55,7 @@ def test_baseline_shapes_select_legal(desc, shape):
     assert 0.0 < score <= 1.0
     op = 1 if "conv" in desc.name else 0
     ok, why = N.config_legal(op, N.FO_DT_BF16, N.tile_cfg(block_n=raw["block_N"], stages=raw["num_stages"],
-                                                          group_m=raw["group_m"]))
+                                                          group_m=raw["group_m"], block_m=raw["block_M"]))
     assert ok, why
     rk = rank_all(desc, hw=B200, detailed=True, **shape)
     assert rk[0]["score"] == score
@@ -65,7 +71,7 @@ def test_search_space_tcgen05_prunes_to_library_legal():
     assert space
     for c in space:
         ok, why = N.config_legal(0, N.FO_DT_BF16, N.tile_cfg(block_n=c.block_N, stages=c.num_stages,
-                                                              group_m=c.group_size_m))
+                                                              group_m=c.group_size_m, block_m=c.block_M))
         assert ok, why
     full = ss.generate_exhaustive_configs("matmul", "tcgen05")
     assert len(full) > len(space)  # some stage counts exceed 227 KB
