@@ -107,7 +107,8 @@ CUtensorMapDataType tma_dt(int dt) {
 // boxes of box_inner x box_outer elements.  Out-of-range elements load as zero and are
 // skipped by stores.
 int make_tmap(CUtensorMap* m, int dt, const void* base, uint64_t inner, uint64_t outer,
-              uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, const char* what) {
+              uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, const char* what,
+              CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   auto fn = encode_fn();
   if (fn == nullptr) return fail(FO_ECUDA, "cuTensorMapEncodeTiled is unavailable in the driver");
   cuuint64_t dims[2] = {inner, outer};
@@ -115,7 +116,7 @@ int make_tmap(CUtensorMap* m, int dt, const void* base, uint64_t inner, uint64_t
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(m, tma_dt(dt), 2, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(FO_EINVAL, "tensor map for %s rejected by the driver (CUresult %d; dims %llu x %llu, row %llu B)",
@@ -141,7 +142,7 @@ PFN_cuTensorMapEncodeIm2col_v12000 encode_im2col_fn() {
 // positions through the bounding box [-pad, dim - 1 + pad - (k - 1) * dil] of W, then
 // H, then N (stepping by the conv stride) and fetches 64 channels per position.  Returns
 // false when the driver rejects the geometry (the gather producer is used instead).
-bool make_im2col_map(CUtensorMap* m, const FoConvDesc* d) {
+bool make_im2col_map(CUtensorMap* m, const FoConvDesc* d, uint32_t pixels) {
   auto fn = encode_im2col_fn();
   if (fn == nullptr) return false;
   const int lw = -d->pad, lh = -d->pad;
@@ -155,7 +156,7 @@ bool make_im2col_map(CUtensorMap* m, const FoConvDesc* d) {
   int lower[2] = {lw, lh};
   int upper[2] = {uw, uh};
   cuuint32_t estr[4] = {1, static_cast<cuuint32_t>(d->stride), static_cast<cuuint32_t>(d->stride), 1};
-  CUresult r = fn(m, tma_dt(d->in_dtype), 4, const_cast<void*>(d->x), dims, strides, lower, upper, 64, 128, estr,
+  CUresult r = fn(m, tma_dt(d->in_dtype), 4, const_cast<void*>(d->x), dims, strides, lower, upper, 64, pixels, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
@@ -185,6 +186,9 @@ int check_cfg(int op, int out_dtype, const FoTileCfg* cfg, char* why, size_t why
   if (cfg->stages < min_stages || cfg->stages > fo::kMaxStages)
     return say("stages out of range: %d", cfg->stages);
   if (cfg->group_m < 0) return say("group_m must be >= 0, got %d", cfg->group_m);
+  if (cfg->swap_ab != 0 && cfg->swap_ab != 1) return say("swap_ab must be 0 or 1, got %d", cfg->swap_ab);
+  if (cfg->swap_ab && (op != 1 || cfg->block_m != 128 || cfg->block_n < 128))
+    return say("swap_ab is a conv2d mode with block_m 128 and block_n >= 128 (block_n %d)", cfg->block_n);
   if (cfg->max_ctas < 0) return say("max_ctas must be >= 0, got %d", cfg->max_ctas);
   const int smem = fo::smem_bytes_for(cfg->block_n, cfg->stages, cfg->block_m == 256);
   if (smem > 232448) return say("shared memory %d B exceeds the 227 KB per-block limit", smem);
@@ -478,7 +482,7 @@ int fo_conv2d(const FoConvDesc* d, const FoTileCfg* cfg, void* stream) {
   p.K = static_cast<int>(K64);
   // CTA pairs need the TMA im2col producer; without it the conv runs as single CTAs.
   bool pair = cfg->block_m == 256;
-  p.tiles_n = (p.N + bn - 1) / bn;
+  bool swap = cfg->swap_ab == 1;
   p.c_blocks = (d->c + 63) / 64;
   p.k_blocks = d->kh * d->kw * p.c_blocks;
   p.group_m = cfg->group_m;
@@ -502,20 +506,33 @@ int fo_conv2d(const FoConvDesc* d, const FoTileCfg* cfg, void* stream) {
   p.pad = d->pad;
   p.dil = d->dil;
   fill_common(p, di);
-  p.conv_tma = (d->stride <= 8 && !conv_gather_forced() && make_im2col_map(&la.tmA, d)) ? 1 : 0;
-  if (!p.conv_tma) pair = false;
-  const int tile_m = pair ? 256 : 128;
-  p.tiles_m = (p.M + tile_m - 1) / tile_m;
+  p.conv_tma = (d->stride <= 8 && !conv_gather_forced() && make_im2col_map(&la.tmA, d, swap ? bn : 128)) ? 1 : 0;
+  if (!p.conv_tma) pair = swap = false;  // both need the TMA im2col producer
+  if (swap) {
+    // M: output channels in blocks of 128; N: output pixels in blocks of block_n
+    p.tiles_m = (p.N + 127) / 128;
+    p.tiles_n = (p.M + bn - 1) / bn;
+  } else {
+    const int tile_m = pair ? 256 : 128;
+    p.tiles_m = (p.M + tile_m - 1) / tile_m;
+    p.tiles_n = (p.N + bn - 1) / bn;
+  }
   p.num_tiles = p.tiles_m * p.tiles_n;
   if (int rc = make_tmap(&la.tmB, d->in_dtype, d->wgt, d->f, K64, static_cast<uint64_t>(d->f) * 2, 64, 64, "weights"))
     return rc;
-  if (int rc = make_tmap(&la.tmC, d->out_dtype, d->out, d->f, M64, static_cast<uint64_t>(d->f) * ob, 128 / ob, 32,
-                         "out"))
+  if (swap) {  // 32 channels x 32 pixels per store, unswizzled
+    if (int rc = make_tmap(&la.tmC, d->out_dtype, d->out, d->f, M64, static_cast<uint64_t>(d->f) * ob, 32, 32, "out",
+                           CU_TENSOR_MAP_SWIZZLE_NONE))
+      return rc;
+  } else if (int rc = make_tmap(&la.tmC, d->out_dtype, d->out, d->f, M64, static_cast<uint64_t>(d->f) * ob, 128 / ob,
+                                32, "out")) {
     return rc;
+  }
   const int cap = pair ? (cfg->max_ctas > 0 ? cfg->max_ctas / 2 : di.sms / 2) : (cfg->max_ctas > 0 ? cfg->max_ctas : di.sms);
   if (cap < 1) return fail(FO_EINVAL, "max_ctas too small for CTA pairs");
   la.grid = (p.num_tiles < cap ? p.num_tiles : cap) * (pair ? 2 : 1);
   la.pair = pair;
+  la.swap = swap;
   p.num_units = p.dp_units = p.num_tiles;  // whole tiles
   p.split = 1;
   p.kb_per_part = p.k_blocks;

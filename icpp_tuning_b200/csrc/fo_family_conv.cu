@@ -14,11 +14,22 @@ static cudaError_t by_out_p(int out_dt, const LaunchArgs& a) {
 }
 
 template <int BN, int ACT>
+static cudaError_t by_out_swap(int out_dt, const LaunchArgs& a) {
+  switch (out_dt) {
+    case DT_F16: return launch_tc<BN, ACT, DT_F16, false, true, false, true>(a);
+    case DT_BF16: return launch_tc<BN, ACT, DT_BF16, false, true, false, true>(a);
+    case DT_F32: return launch_tc<BN, ACT, DT_F32, false, true, false, true>(a);
+  }
+  return cudaErrorInvalidValue;
+}
+
+template <int BN, int ACT>
 static cudaError_t by_out(int out_dt, const LaunchArgs& a) {
   if constexpr (BN >= 128) {
+    if (a.swap) return by_out_swap<BN, ACT>(out_dt, a);
     if (a.pair) return by_out_p<BN, ACT, true>(out_dt, a);
   } else {
-    if (a.pair) return cudaErrorInvalidValue;
+    if (a.pair || a.swap) return cudaErrorInvalidValue;
   }
   return by_out_p<BN, ACT, false>(out_dt, a);
 }

@@ -209,7 +209,7 @@ __device__ __forceinline__ void drain_loads(uint32_t bar_full, int stages, int i
   }
 }
 
-template <int BN, int ACT, int OUT_DT, bool LN, bool CONV, bool PAIR>
+template <int BN, int ACT, int OUT_DT, bool LN, bool CONV, bool PAIR, bool SWAP = false>
 __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
     fo_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const __grid_constant__ CUtensorMap tmC, const KParams p) {
@@ -223,6 +223,10 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
   constexpr int kTileM = PAIR ? 2 * kBM : kBM;
   constexpr int kBStage = b_stage_bytes(kBHalf);
   static_assert(!PAIR || BN >= 128, "CTA pairs need BN >= 128");
+  // SWAP (conv only): the MMA computes Y^T = W^T X^T, M = 128 output channels (A = weight
+  // block, MN-major), N = BN output pixels (B = im2col tile, K-major), so a conv with few
+  // channels still runs 128 x 256 MMAs; the epilogue transposes through shared memory.
+  static_assert(!SWAP || (CONV && !PAIR && !LN), "operand swap is a single-CTA conv mode");
   constexpr int kOutBytes = OUT_DT == DT_F32 ? 4 : 2;
   constexpr int kCPC = 128 / kOutBytes;  // output columns per 128-byte chunk
   constexpr int kChunks = BN / kCPC;
@@ -359,7 +363,7 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
         for (int u = cid; u < p.num_units && ok; u += ncl) {
           const Unit un = unit_of(p, u);
           const int tm = un.tm, tn = un.tn;
-          const int m0 = tm * kTileM + static_cast<int>(rank) * kBM;
+          const int m0 = SWAP ? tn * BN : tm * kTileM + static_cast<int>(rank) * kBM;
           const int n_img = m0 / ohow;
           const int rem = m0 - n_img * ohow;
           const int oh = rem / p.OW;
@@ -378,7 +382,13 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
             const uint32_t fb = bar_full + 8 * s;
             const int bcol = tn * BN + static_cast<int>(rank) * kBHalf;
             const uint16_t ow16 = static_cast<uint16_t>(kw * p.dil), oh16 = static_cast<uint16_t>(kh * p.dil);
-            if constexpr (PAIR) {
+            if constexpr (SWAP) {
+              mbar_arrive_expect_tx(fb, kAStageBytes + kBStage);
+#pragma unroll
+              for (int j = 0; j < 2; ++j)  // A: 128 channels x 64 K of the weights, MN-major
+                tma_load_2d(sA + s * kAStageBytes + j * 64 * 128, &tmB, fb, tm * kBM + j * 64, tap * p.C + cb * kBK);
+              tma_load_im2col_4d(sB + s * kBStage, &tmA, fb, cb * kBK, w0, h0, n_img, ow16, oh16);  // B: BN pixels
+            } else if constexpr (PAIR) {
               const uint32_t fbl = mapa_shared(fb, 0);
               if (rank == 0) mbar_arrive_expect_tx(fb, 2 * (kAStageBytes + kBStage));
               tma_load_im2col_4d_pair(sA + s * kAStageBytes, &tmA, fbl, cb * kBK, w0, h0, n_img, ow16, oh16);
@@ -492,10 +502,12 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0 && rank == 0) {
-      const uint32_t idesc = idesc_f16(p.ab_bf16, p.b_mn, BN, kTileM);
-      const uint64_t a_desc0 = sdesc_sw128(sA, 16, 1024);
-      const uint64_t b_desc0 = p.b_mn ? sdesc_sw128(sB, 64 * 128, 1024) : sdesc_sw128(sB, 16, 1024);
-      const uint32_t b_kstep = p.b_mn ? (2048 >> 4) : (32 >> 4);
+      const int b_mn = SWAP ? 0 : p.b_mn;
+      const uint32_t idesc = idesc_f16(p.ab_bf16, b_mn, BN, kTileM) | (SWAP ? (1u << 15) : 0u);  // [15]: A MN-major
+      const uint64_t a_desc0 = SWAP ? sdesc_sw128(sA, 64 * 128, 1024) : sdesc_sw128(sA, 16, 1024);
+      const uint32_t a_kstep = SWAP ? (2048 >> 4) : (32 >> 4);
+      const uint64_t b_desc0 = b_mn ? sdesc_sw128(sB, 64 * 128, 1024) : sdesc_sw128(sB, 16, 1024);
+      const uint32_t b_kstep = b_mn ? (2048 >> 4) : (32 >> 4);
       int s = 0;
       uint32_t ph = 0;
       int acc = 0;
@@ -523,7 +535,7 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
           const uint64_t bd0 = b_desc0 + static_cast<uint64_t>((s * kBStage) >> 4);
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
-            const uint64_t ad = ad0 + static_cast<uint64_t>(2 * k);
+            const uint64_t ad = ad0 + static_cast<uint64_t>(k * a_kstep);
             const uint64_t bd = bd0 + static_cast<uint64_t>(k * b_kstep);
             const uint32_t accum = (kb != un.kb0 || k != 0) ? 1u : 0u;
             if constexpr (PAIR) {
@@ -584,6 +596,51 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
         break;
       }
       tc_fence_after();
+      if constexpr (SWAP) {
+        // TMEM lane = output channel f, column = output pixel.  Each 32-pixel chunk is
+        // transposed through shared memory ([pixel][32 channels], unswizzled) and stored
+        // as a 32 x 32 block of the NHWC output.
+        const int f = tm * kBM + quarter * 32 + lane;
+        const float bf = (p.has_bias && f < p.N) ? load_vec(p.bias, p.vec_dtype, f) : 0.f;
+        constexpr int kRowB = 32 * kOutBytes;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tmem_base + lane_off + acc * BN + c * 32, r);
+          tc_wait_ld_regs(r);
+          if (c == BN / 32 - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_tempty + 8 * acc);
+          }
+          const uint32_t buf = buf0 + (nstore & 1) * kEpiBufBytes;
+          if (nstore >= 2) {
+            if (lane == 0) bulk_wait_read<1>();
+            __syncwarp();
+          }
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float val = apply_act<ACT>((has_k ? __uint_as_float(r[i]) : 0.f) + bf);
+            const uint32_t addr = buf + i * kRowB + lane * kOutBytes;
+            if constexpr (OUT_DT == DT_F32) {
+              asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(__float_as_uint(val)) : "memory");
+            } else {
+              const unsigned short h = static_cast<unsigned short>(pack2<OUT_DT>(val, 0.f) & 0xFFFFu);
+              asm volatile("st.shared.b16 [%0], %1;" ::"r"(addr), "h"(h) : "memory");
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, buf, tm * kBM + quarter * 32, tn * BN + c * 32);
+            bulk_commit();
+          }
+          ++nstore;
+        }
+        acc ^= 1;
+        if (acc == 0) acc_ph ^= 1;
+        continue;
+      }
       const int row0 = tm * kTileM + static_cast<int>(rank) * kBM + quarter * 32;
       const int col0 = tn * BN;
       // Split tile: publish this part's fp32 partial ([column][128 rows], coalesced), then

@@ -16,11 +16,12 @@ struct LaunchArgs {
   int smem;
   cudaStream_t stream;
   bool pair;  // launch as clusters of two CTAs (block_m 256, tcgen05 cta_group::2)
+  bool swap;  // conv: operand-swapped kernel (M = output channels, N = pixels)
 };
 
-template <int BN, int ACT, int OUT_DT, bool LN, bool CONV, bool PAIR>
+template <int BN, int ACT, int OUT_DT, bool LN, bool CONV, bool PAIR, bool SWAP = false>
 cudaError_t launch_tc(const LaunchArgs& a) {
-  auto kern = fo_tc_kernel<BN, ACT, OUT_DT, LN, CONV, PAIR>;
+  auto kern = fo_tc_kernel<BN, ACT, OUT_DT, LN, CONV, PAIR, SWAP>;
   // Opt in to the full 227 KB of dynamic shared memory once per device.
   static std::atomic<uint64_t> opted{0};
   int dev = 0;

@@ -76,7 +76,8 @@ def as_tile_cfg(cfg) -> N.FoTileCfg:
         return cfg
     return N.tile_cfg(block_n=int(cfg["block_N"]), stages=int(cfg["num_stages"]),
                       group_m=int(cfg.get("group_m", 0)), max_ctas=int(cfg.get("max_ctas", 0)),
-                      block_m=int(cfg.get("block_M", 128)), block_k=int(cfg.get("block_K", 64)))
+                      block_m=int(cfg.get("block_M", 128)), block_k=int(cfg.get("block_K", 64)),
+                      swap_ab=int(cfg.get("swap_ab", 0)))
 
 
 def workspace_bytes(M: int, N_: int, K: int, epilogue: str, cfg) -> int:

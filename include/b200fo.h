@@ -59,12 +59,14 @@ extern "C" {
  * by the warp-specialised design, so the free parameters are block_n, stages, group_m
  * and the grid size. */
 typedef struct FoTileCfg {
-  int32_t block_m;  /* 128                                                              */
+  int32_t block_m;  /* 128 (one CTA) or 256 (a CTA pair, tcgen05 cta_group::2)         */
   int32_t block_n;  /* 64, 128 or 256                                                   */
   int32_t block_k;  /* 64                                                               */
   int32_t stages;   /* shared-memory pipeline depth, 2..8 (bounded by 227 KB)          */
   int32_t group_m;  /* tile raster: 0 = row-major, g>0 = groups of g row blocks        */
   int32_t max_ctas; /* persistent grid size cap; 0 = one CTA per SM                     */
+  int32_t swap_ab;  /* conv2d only: 1 = compute Y^T = W^T X^T (M = 128 output channels,  */
+                    /* N = block_n output pixels) so few-channel convs use wide MMAs     */
 } FoTileCfg;
 
 /* One GEMM-family call.  A[M,K] row-major (row stride lda elements).  B per b_layout

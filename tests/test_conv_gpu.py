@@ -65,3 +65,20 @@ def test_config5_conv_full():
     ref = R.conv2d_bias_relu(x[sl], wt, bias, True, 1, 1, 1, out_dtype=torch.bfloat16)
     assert_close(y[sl], ref, TOL)
     status_clean()
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=str)
+@pytest.mark.parametrize("bn", [128, 256])
+@pytest.mark.parametrize("odt", [torch.bfloat16, torch.float32])
+def test_conv_swapped_operands(shape, bn, odt):
+    """swap_ab: Y^T = W^T X^T (M = output channels, N = pixels), transposing epilogue."""
+    n, h, w, c, f, k, s, p, d = shape
+    g = gen(22)
+    x = randn(g, n, h, w, c)
+    wt = randn(g, k, k, c, f, scale=(k * k * c) ** -0.5)
+    bias = randn(g, f, scale=0.1)
+    cfg = N.tile_cfg(bn, 4 if bn == 256 else 6, 0, swap_ab=1)
+    out = fused.conv2d_nhwc(*cuda(x, wt), bias=bias.cuda(), relu=True, stride=s, padding=p, dilation=d,
+                            out_dtype=odt, config=cfg)
+    assert_close(out, R.conv2d_bias_relu(x, wt, bias, True, s, p, d, out_dtype=odt), TOL)
+    status_clean()
