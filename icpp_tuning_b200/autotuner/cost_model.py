@@ -145,6 +145,7 @@ class TuneConfig:
     group_size_m: int = 8
     kind: str = "simt"
     max_ctas: int = 0
+    swap_ab: int = 0  # tcgen05 conv: tiles over (output channels, pixels) instead
 
     @property
     def threads(self) -> int:

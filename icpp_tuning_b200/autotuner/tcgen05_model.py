@@ -18,7 +18,7 @@ running this design (docs/cost_model.md of the reference describes the factor id
   eff_implicit_conv conv only: rate of the TMA im2col loads relative to tiled loads
   eff_epilogue      overlap of the epilogue (TMEM -> registers -> TMA store) with the
                     next tile's mainloop (two TMEM accumulators)
-  eff_reduction     LayerNorm only: the in-place normalisation pass of each row block
+  eff_reduction     LayerNorm only: the stream-ordered in-place normalisation pass
 
 score = product = (ideal tensor time) / (predicted time).  The constants in CONSTANTS
 are fitted to B200 measurements of these kernels.
@@ -35,13 +35,19 @@ CONSTANTS = {
     # measured on B200 (4096^3 bf16, same stages / raster): BN=256 1267, BN=128 836,
     # BN=64 462 TFLOP/s -- narrow tiles are bound by shared-memory operand traffic
     "mma_rate_bn": {256: 1.0, 128: 0.66, 64: 0.37},
-    # CTA pairs (block_M 256): each SM reads half of B, so narrow tiles lose less
-    "mma_rate_bn_pair": {256: 1.05, 128: 0.9},
+    # CTA pairs (block_M 256): each SM loads half of B (4096^3: BN=128 pairs 837, BN=256 pairs 1274)
+    "mma_rate_bn_pair": {256: 1.03, 128: 0.66},  # measured: pairs do not lift narrow tiles
     "hbm_efficiency": 0.8,  # achievable fraction of the HBM figure in the GPU spec
     "mem_overlap": 0.35,  # share of the shorter of (compute, HBM) time that does not overlap
-    "tma_latency_s": 1.2e-6,  # global -> shared latency a stage ring has to cover
+    # stages - 1 loads in flight must cover this latency (4096^3: 3 stages run at 0.9 of 4)
+    "tma_latency_s": 0.8e-6,
+    # achievable share of the nominal dense peak under the 1 kW power cap (cuBLAS bf16
+    # 8192^3 measured 1680 of 2250 TFLOP/s on this pool)
+    "tensor_rate_fraction": 0.75,
     "epi_bytes_per_s_sm": 120e9,  # epilogue store throughput of one SM (TMEM ld + TMA store)
-    "ln_bytes_per_s_sm": 90e9,  # normalisation pass read+write throughput of one SM
+    # LayerNorm normalisation pass (separate stream-ordered kernel), read + write bytes/s:
+    # 16384 x 4096 bf16 measured ~100 us on top of the GEMM
+    "ln_pass_bytes_per_s": 2.6e12,
     # TMA im2col loads (one 128-pixel x 64-channel box per filter tap) run at this share
     # of a tiled load's rate: measured 589 vs 836 TFLOP/s for BN=128 conv vs GEMM tiles
     "im2col_rate": 0.7,
@@ -55,7 +61,7 @@ def _cdiv(a: int, b: int) -> int:
 
 
 def _sm_rate(hw: GPUSpec) -> float:
-    return hw.peak_fp16_tflops * 1e12 / max(1, hw.num_sm)
+    return CONSTANTS["tensor_rate_fraction"] * hw.peak_fp16_tflops * 1e12 / max(1, hw.num_sm)
 
 
 def _traffic_bytes(op: OpSpec, c: TuneConfig, hw: GPUSpec, ctas: int) -> float:
@@ -91,7 +97,9 @@ def _model(op: OpSpec, c: TuneConfig, hw: GPUSpec) -> dict:
     ml = op.mainloop
     bm, bn, bk = c.block_M, c.block_N, c.block_K
     pair = bm == 256
-    tiles_m, tiles_n = _cdiv(op.M, bm), _cdiv(op.N, bn)
+    # swap_ab (conv): the tile grid runs over (output channels, pixels)
+    rows, cols = (op.N, op.M) if c.swap_ab else (op.M, op.N)
+    tiles_m, tiles_n = _cdiv(rows, bm), _cdiv(cols, bn)
     k_blocks = max(1, _cdiv(op.K, bk))
     tiles = tiles_m * tiles_n
     sms = hw.num_sm // 2 if pair else hw.num_sm  # persistent units: SMs or SM pairs
@@ -102,7 +110,7 @@ def _model(op: OpSpec, c: TuneConfig, hw: GPUSpec) -> dict:
 
     # -- mainloop: padded MMA work of one tile at the BN-dependent tensor rate
     e_bn = (K["mma_rate_bn_pair"] if pair else K["mma_rate_bn"]).get(bn, 0.6)
-    padding = (op.M * op.N * op.K) / float(tiles_m * bm * tiles_n * bn * k_blocks * bk)
+    padding = (rows * cols * op.K) / float(tiles_m * bm * tiles_n * bn * k_blocks * bk)
     t_kb = 2.0 * bm * bn * bk / (rate * e_bn)
     # -- pipeline: stages - 1 loads in flight while one stage is consumed
     e_pipe = min(1.0, (c.num_stages - 1) * t_kb / K["tma_latency_s"])
@@ -119,10 +127,7 @@ def _model(op: OpSpec, c: TuneConfig, hw: GPUSpec) -> dict:
     # -- LayerNorm: one normalisation pass (read + write) per 128-row block
     t_ln = 0.0
     if op.has_reduction_epilogue:
-        per_block = bm * op.N * ml.output_element_bytes * 2 / K["ln_bytes_per_s_sm"]
-        # a block's pass overlaps up to two tiles of the CTA's own mainloop
-        stall = max(0.0, per_block - 2 * t_tile_mma) + 0.25 * per_block
-        t_ln = stall * tiles_m / ctas
+        t_ln = 2.0 * op.M * op.N * ml.output_element_bytes / K["ln_pass_bytes_per_s"]
     t_work = waves * t_tile
     e_red = t_work / (t_work + t_ln)
     # -- parallel: SM-time used by the persistent grid, plus fixed cost

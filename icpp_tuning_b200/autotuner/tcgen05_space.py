@@ -46,6 +46,11 @@ def tcgen05_configs(block_ns: Sequence[int] = (64, 128, 256), group_ms: Sequence
                 for g in group_ms:
                     out.append({"block_M": bm, "block_N": bn, "block_K": 64, "num_stages": s,
                                 "thread_num": CONV_THREADS if conv else GEMM_THREADS, "group_m": g})
+    if conv:  # operand-swapped conv: 128 output channels x block_N pixels per tile
+        for bn in (128, 256):
+            for s in sorted({x for x in (stages or (3, 4)) if 3 <= x <= max_stages(bn)}):
+                out.append({"block_M": 128, "block_N": bn, "block_K": 64, "num_stages": s,
+                            "thread_num": CONV_THREADS, "group_m": 0, "swap_ab": 1})
     return out
 
 
@@ -56,4 +61,8 @@ class Tcgen05Descriptor(TileLangKernelBase):
         return TuneConfig(block_M=raw["block_M"], block_N=raw["block_N"], block_K=raw["block_K"],
                           num_stages=raw["num_stages"], num_warps=raw["thread_num"] // 32,
                           group_size_m=raw.get("group_m", 0), kind="tcgen05",
-                          max_ctas=raw.get("max_ctas", 0))
+                          max_ctas=raw.get("max_ctas", 0), swap_ab=raw.get("swap_ab", 0))
+
+    def format_config(self, raw: Dict[str, Any]) -> str:
+        base = super().format_config(raw)
+        return base + "_SW" if raw.get("swap_ab") else base
