@@ -209,16 +209,18 @@ def run_ours(args):
     per_launch_ms = dev_ms / args.steps
     achieved = flops / (per_launch_ms / 1e3) / 1e12
     traffic = None
-    prof = ROOT / "profiles" / "gemm_4096_bf16_traffic.json"
+    prof = ROOT / "profiles" / "gemm_4096_bf16.md"  # committed ncu summary of this kernel
     if prof.exists():
-        traffic = json.loads(prof.read_text()).get("dram_bytes_per_launch")
+        for line in prof.read_text().splitlines():
+            if line.startswith("dram_bytes_per_launch:"):
+                traffic = int(line.split(":", 1)[1])
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded randn, BASELINE configs[1] shapes)",
         "config": {"workload": WORKLOAD, "parallelism": f"M-shard x{ws} (weak: 4096 rows per GPU)",
-                   "tile": kern.config and "BM128_BN%d_BK64_S%d_G%d" % (kern.config["block_N"], kern.config["num_stages"],
-                                                                      kern.config.get("group_m", 0)),
+                   "tile": "BM%d_BN%d_BK64_S%d_G%d" % (kern.config["block_M"], kern.config["block_N"],
+                                                        kern.config["num_stages"], kern.config.get("group_m", 0)),
                    "l2": "flushed between timed steps (256 MiB write outside the events)"},
         "e2e": e2e,
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": UNIT,
