@@ -31,7 +31,7 @@ EXPORTED = (
     "fo_gemm", "fo_gemm_workspace_size", "fo_conv2d", "fo_query_config_legal",
     "fo_config_smem_bytes", "fo_device_status", "fo_set_wait_timeout_ns",
     "fo_selftest_wait_timeout", "fo_last_error", "fo_version", "fo_launch_count",
-    "fo_gemm_bias_layernorm_noalloc",
+    "fo_gemm_bias_layernorm_noalloc", "fo_conv2d_workspace_size",
 )
 
 
@@ -58,7 +58,8 @@ class FoConvDesc(ctypes.Structure):
                 ("x", ctypes.c_void_p), ("wgt", ctypes.c_void_p), ("bias", ctypes.c_void_p),
                 ("out", ctypes.c_void_p), ("in_dtype", ctypes.c_int32),
                 ("vec_dtype", ctypes.c_int32), ("out_dtype", ctypes.c_int32),
-                ("epilogue", ctypes.c_int32)]
+                ("epilogue", ctypes.c_int32), ("workspace", ctypes.c_void_p),
+                ("workspace_bytes", ctypes.c_size_t)]
 
 
 class FoError(RuntimeError):
@@ -83,6 +84,8 @@ def _declare(l: ctypes.CDLL) -> None:
     l.fo_gemm_workspace_size.restype = ctypes.c_size_t
     l.fo_conv2d.argtypes = [P(FoConvDesc), P(FoTileCfg), ctypes.c_void_p]
     l.fo_conv2d.restype = ctypes.c_int
+    l.fo_conv2d_workspace_size.argtypes = [P(FoConvDesc), P(FoTileCfg)]
+    l.fo_conv2d_workspace_size.restype = ctypes.c_size_t
     l.fo_query_config_legal.argtypes = [ctypes.c_int32, ctypes.c_int32, P(FoTileCfg),
                                         ctypes.c_char_p, ctypes.c_size_t]
     l.fo_query_config_legal.restype = ctypes.c_int

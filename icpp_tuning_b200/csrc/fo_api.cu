@@ -215,7 +215,8 @@ size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // Work split of a GEMM over `cap` persistent CTAs.  Whole tiles fill as many complete
 // waves as they can; the tiles of a last, less than half-full wave (or of a problem with
-// fewer tiles than CTAs) are split along K into up to 8 parts so every CTA has work.
+// fewer tiles than CTAs) are split along K into up to 8 parts of >= 8 k-blocks each so
+// every CTA has work.
 struct SplitPlan {
   int grid, num_units, dp_units, split, kb_per_part, split_tiles;
 };
@@ -229,6 +230,11 @@ SplitPlan plan_split(int tiles, int k_blocks, int cap, bool allow) {
   int split = cap / left;
   if (split > 8) split = 8;
   if (split > k_blocks) split = k_blocks;
+  if (split < 2) return pl;
+  // Each part must keep >= 8 k-blocks: shorter parts spend as long writing and reducing
+  // their fp32 partials as multiplying (measured on the 3x3x128 conv: 6 k-block parts
+  // made the call 10% slower).
+  if (split > k_blocks / 8) split = k_blocks / 8;
   if (split < 2) return pl;
   const int kbp = (k_blocks + split - 1) / split;
   split = (k_blocks + kbp - 1) / kbp;  // no empty parts
@@ -439,6 +445,34 @@ int fo_gemm(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
   return ok();
 }
 
+// Tile grid of a conv call: (tiles, k_blocks, single-CTA?) as fo_conv2d lays it out when
+// the TMA im2col path is available (the split tail needs whole-K producers per unit).
+static bool conv_grid(const FoConvDesc* d, const FoTileCfg* cfg, int* tiles, int* k_blocks) {
+  if (d == nullptr || cfg == nullptr || check_cfg(1, d->out_dtype, cfg, nullptr, 0) != FO_OK) return false;
+  if (d->n <= 0 || d->h <= 0 || d->w <= 0 || d->c <= 0 || d->f <= 0 || d->kh <= 0 || d->kw <= 0 || d->stride <= 0 ||
+      d->dil <= 0 || d->pad < 0)
+    return false;
+  const int oh = (d->h + 2 * d->pad - d->dil * (d->kh - 1) - 1) / d->stride + 1;
+  const int ow = (d->w + 2 * d->pad - d->dil * (d->kw - 1) - 1) / d->stride + 1;
+  if (oh <= 0 || ow <= 0) return false;
+  const int64_t M = static_cast<int64_t>(d->n) * oh * ow;
+  if (cfg->block_m == 256) return false;  // CTA pairs run whole tiles
+  const int bn = cfg->block_n;
+  if (cfg->swap_ab)
+    *tiles = static_cast<int>(((d->f + 127) / 128) * ((M + bn - 1) / bn));
+  else
+    *tiles = static_cast<int>(((M + 127) / 128) * ((d->f + bn - 1) / bn));
+  *k_blocks = d->kh * d->kw * ((d->c + 63) / 64);
+  return true;
+}
+
+extern "C" size_t fo_conv2d_workspace_size(const FoConvDesc* d, const FoTileCfg* cfg) {
+  int tiles = 0, kb = 0;
+  if (!conv_grid(d, cfg, &tiles, &kb)) return 0;
+  const int cap = cfg->max_ctas > 0 ? cfg->max_ctas : sm_count_or_default();
+  return split_workspace(plan_split(tiles, kb, cap, true), cfg->block_n);
+}
+
 int fo_conv2d(const FoConvDesc* d, const FoTileCfg* cfg, void* stream) {
   if (d == nullptr) return fail(FO_EINVAL, "null descriptor");
   char why[256];
@@ -530,12 +564,22 @@ int fo_conv2d(const FoConvDesc* d, const FoTileCfg* cfg, void* stream) {
   }
   const int cap = pair ? (cfg->max_ctas > 0 ? cfg->max_ctas / 2 : di.sms / 2) : (cfg->max_ctas > 0 ? cfg->max_ctas : di.sms);
   if (cap < 1) return fail(FO_EINVAL, "max_ctas too small for CTA pairs");
-  la.grid = (p.num_tiles < cap ? p.num_tiles : cap) * (pair ? 2 : 1);
   la.pair = pair;
   la.swap = swap;
-  p.num_units = p.dp_units = p.num_tiles;  // whole tiles
-  p.split = 1;
-  p.kb_per_part = p.k_blocks;
+  SplitPlan pl = plan_split(p.num_tiles, p.k_blocks, cap, !pair && p.conv_tma);
+  const size_t split_need = split_workspace(pl, bn);
+  if (split_need == 0 || d->workspace == nullptr || d->workspace_bytes < split_need || !aligned16(d->workspace))
+    pl = plan_split(p.num_tiles, p.k_blocks, cap, false);
+  p.num_units = pl.num_units;
+  p.dp_units = pl.dp_units;
+  p.split = pl.split;
+  p.kb_per_part = pl.kb_per_part;
+  if (pl.split > 1) {
+    p.split_cnt = static_cast<int*>(d->workspace);
+    p.split_ws = reinterpret_cast<float*>(static_cast<char*>(d->workspace) +
+                                          round_up(static_cast<size_t>(pl.split_tiles) * 4 * sizeof(int), 256));
+  }
+  la.grid = pl.grid * (pair ? 2 : 1);
   la.smem = fo::smem_bytes_for(bn, cfg->stages, pair);
   la.stream = static_cast<cudaStream_t>(stream);
   const int out_dt = d->out_dtype == FO_DT_F16 ? fo::DT_F16 : d->out_dtype == FO_DT_BF16 ? fo::DT_BF16 : fo::DT_F32;

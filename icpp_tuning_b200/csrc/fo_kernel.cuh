@@ -596,53 +596,6 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
         break;
       }
       tc_fence_after();
-      if constexpr (SWAP) {
-        // TMEM lane = output channel f, column = output pixel.  Each 32-pixel chunk is
-        // transposed through shared memory ([pixel][32 channels], unswizzled) and stored
-        // as a 32 x 32 block of the NHWC output.
-        const int f = tm * kBM + quarter * 32 + lane;
-        const float bf = (p.has_bias && f < p.N) ? load_vec(p.bias, p.vec_dtype, f) : 0.f;
-        constexpr int kRowB = 32 * kOutBytes;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tmem_base + lane_off + acc * BN + c * 32, r);
-          tc_wait_ld_regs(r);
-          if (c == BN / 32 - 1) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar_tempty + 8 * acc);
-          }
-          const uint32_t buf = buf0 + (nstore & 1) * kEpiBufBytes;
-          if (nstore >= 2) {
-            if (lane == 0) bulk_wait_read<1>();
-            __syncwarp();
-          }
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float val = apply_act<ACT>((has_k ? __uint_as_float(r[i]) : 0.f) + bf);
-            const uint32_t addr = buf + i * kRowB + lane * kOutBytes;
-            if constexpr (OUT_DT == DT_F32) {
-              asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(__float_as_uint(val)) : "memory");
-            } else {
-              const unsigned short h = static_cast<unsigned short>(pack2<OUT_DT>(val, 0.f) & 0xFFFFu);
-              asm volatile("st.shared.b16 [%0], %1;" ::"r"(addr), "h"(h) : "memory");
-            }
-          }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            tma_store_2d(&tmC, buf, tm * kBM + quarter * 32, tn * BN + c * 32);
-            bulk_commit();
-          }
-          ++nstore;
-        }
-        acc ^= 1;
-        if (acc == 0) acc_ph ^= 1;
-        continue;
-      }
-      const int row0 = tm * kTileM + static_cast<int>(rank) * kBM + quarter * 32;
-      const int col0 = tn * BN;
       // Split tile: publish this part's fp32 partial ([column][128 rows], coalesced), then
       // the warp whose arrival completes its row quarter adds the other parts and runs
       // the epilogue; the other warps release the accumulator and move on.
@@ -682,6 +635,65 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
       }
       float st_cnt = 0.f, st_mean = 0.f, st_m2 = 0.f;
       float shift = 0.f;  // LayerNorm: the tile is stored centred on its first chunk's mean
+      if constexpr (SWAP) {
+        // TMEM lane = output channel f, column = output pixel.  Each 32-pixel chunk is
+        // transposed through shared memory ([pixel][32 channels], unswizzled) and stored
+        // as a 32 x 32 block of the NHWC output.
+        const int f = tm * kBM + quarter * 32 + lane;
+        const float bf = (p.has_bias && f < p.N) ? load_vec(p.bias, p.vec_dtype, f) : 0.f;
+        constexpr int kRowB = 32 * kOutBytes;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tmem_base + lane_off + acc * BN + c * 32, r);
+          tc_wait_ld_regs(r);
+          if (c == BN / 32 - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_tempty + 8 * acc);
+          }
+          const uint32_t buf = buf0 + (nstore & 1) * kEpiBufBytes;
+          if (nstore >= 2) {
+            if (lane == 0) bulk_wait_read<1>();
+            __syncwarp();
+          }
+#pragma unroll
+          float acc_v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc_v[i] = has_k ? __uint_as_float(r[i]) : 0.f;
+          if (split_tile != nullptr) {
+            for (int q = 0; q < p.split; ++q) {
+              if (q == un.part) continue;
+              const float* other = split_tile + static_cast<long long>(q) * BN * 128 + quarter * 32 + lane;
+#pragma unroll
+              for (int i = 0; i < 32; ++i) acc_v[i] += __ldcg(other + (c * 32 + i) * 128);
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float val = apply_act<ACT>(acc_v[i] + bf);
+            const uint32_t addr = buf + i * kRowB + lane * kOutBytes;
+            if constexpr (OUT_DT == DT_F32) {
+              asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(__float_as_uint(val)) : "memory");
+            } else {
+              const unsigned short h = static_cast<unsigned short>(pack2<OUT_DT>(val, 0.f) & 0xFFFFu);
+              asm volatile("st.shared.b16 [%0], %1;" ::"r"(addr), "h"(h) : "memory");
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, buf, tm * kBM + quarter * 32, tn * BN + c * 32);
+            bulk_commit();
+          }
+          ++nstore;
+        }
+        acc ^= 1;
+        if (acc == 0) acc_ph ^= 1;
+        continue;
+      }
+      const int row0 = tm * kTileM + static_cast<int>(rank) * kBM + quarter * 32;
+      const int col0 = tn * BN;
 #pragma unroll 1
       for (int c = 0; c < kChunks; ++c) {
         const int cbase = col0 + c * kCPC;

@@ -145,12 +145,33 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, b_layout: str = "kn", epilogue: st
     return out
 
 
+def _conv_desc(n, h, wd, c, f, kh, kw, stride, padding, dilation, out_dtype=N.FO_DT_BF16) -> N.FoConvDesc:
+    d = N.FoConvDesc()
+    d.n, d.h, d.w, d.c, d.f, d.kh, d.kw = n, h, wd, c, f, kh, kw
+    d.stride, d.pad, d.dil = stride, padding, dilation
+    d.in_dtype = d.out_dtype = out_dtype
+    return d
+
+
+def conv_workspace_bytes(n, h, w, c, f, kh, kw, stride=1, padding=1, dilation=1, config=None) -> int:
+    """Optional zero-filled workspace that lets fo_conv2d split a partial last wave along K."""
+    cfg = as_tile_cfg(config) if config is not None else default_conv_config(f)
+    d = _conv_desc(n, h, w, c, f, kh, kw, stride, padding, dilation)
+    return int(N.lib().fo_conv2d_workspace_size(ctypes.byref(d), ctypes.byref(cfg)))
+
+
+def default_conv_config(f: int) -> N.FoTileCfg:
+    """Operand-swapped 128-channel x 256-pixel tiles (the measured best for few channels)."""
+    return N.tile_cfg(block_n=256, stages=4, group_m=0, swap_ab=1)
+
+
 def conv2d_nhwc(x: torch.Tensor, w: torch.Tensor, *, bias: Optional[torch.Tensor] = None,
                 relu: bool = False, stride: int = 1, padding: int = 1, dilation: int = 1,
                 out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
-                config=None, stream=None) -> torch.Tensor:
-    """out[n,oh,ow,f] = act(conv(x[n,h,w,c], w[kh,kw,c,f]) + bias[f]), implicit GEMM."""
-    dev = _require_cuda(x, w, bias, out)
+                workspace: Optional[torch.Tensor] = None, config=None, stream=None) -> torch.Tensor:
+    """out[n,oh,ow,f] = act(conv(x[n,h,w,c], w[kh,kw,c,f]) + bias[f]), implicit GEMM.
+    `workspace` (optional, zero-filled, conv_workspace_bytes) enables the split-K tail."""
+    dev = _require_cuda(x, w, bias, out, workspace)
     if x.dim() != 4 or w.dim() != 4 or not x.is_contiguous() or not w.is_contiguous():
         raise ValueError("x must be contiguous NHWC [n,h,w,c] and w contiguous [kh,kw,c,f]")
     if x.dtype != w.dtype or x.dtype not in (torch.float16, torch.bfloat16):
@@ -176,11 +197,9 @@ def conv2d_nhwc(x: torch.Tensor, w: torch.Tensor, *, bias: Optional[torch.Tensor
     d.in_dtype, d.out_dtype = dtype_code(x.dtype), dtype_code(out.dtype)
     d.vec_dtype = dtype_code(bias.dtype) if bias is not None else N.FO_DT_F32
     d.epilogue = epi
-    if config is None:
-        bn = 128 if f > 64 else 64
-        cfg = N.tile_cfg(block_n=bn, stages=6 if bn == 128 else 8, group_m=0)
-    else:
-        cfg = as_tile_cfg(config)
+    cfg = as_tile_cfg(config) if config is not None else default_conv_config(f)
+    if workspace is not None:
+        d.workspace, d.workspace_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
     with torch.cuda.device(dev):
         N.check(N.lib().fo_conv2d(ctypes.byref(d), ctypes.byref(cfg), _stream(dev, stream)))
     return out

@@ -107,6 +107,8 @@ typedef struct FoConvDesc {
   int32_t vec_dtype;
   int32_t out_dtype;
   int32_t epilogue;
+  void* workspace;        /* optional, zero-filled: fp32 partials of the split-K tail */
+  size_t workspace_bytes; /* (fo_conv2d_workspace_size); NULL / 0 = no split          */
 } FoConvDesc;
 
 /* Replaces: the callable from tilelang.compile(...) for gemm / gemm_bias_act /
@@ -124,6 +126,10 @@ size_t fo_gemm_workspace_size(const FoGemmDesc* desc, const FoTileCfg* cfg);
 /* Replaces: build_conv2d_kernel(...)(X, W, Y) (kernel/tilelang/conv/conv2d.py:282-290,
  * conv2d_relu.py:146-155).  Writes into desc->out. */
 int fo_conv2d(const FoConvDesc* desc, const FoTileCfg* cfg, void* stream);
+
+/* Bytes of optional workspace fo_conv2d uses to split the tiles of a partial last wave
+ * along K (zero-filled before first use, left zeroed); 0 when no split applies. */
+size_t fo_conv2d_workspace_size(const FoConvDesc* desc, const FoTileCfg* cfg);
 
 /* Legality of a tile config for an op (0 = gemm family, 1 = conv2d) and output dtype:
  * shared memory <= 227 KB, TMEM columns <= 512, tcgen05 shape rules.  Returns FO_OK or

@@ -82,3 +82,25 @@ def test_conv_swapped_operands(shape, bn, odt):
                             out_dtype=odt, config=cfg)
     assert_close(out, R.conv2d_bias_relu(x, wt, bias, True, s, p, d, out_dtype=odt), TOL)
     status_clean()
+
+
+@pytest.mark.parametrize("swap", [0, 1])
+def test_conv_split_tail(swap):
+    """A partial last wave split along K (workspace given) matches the whole-tile result."""
+    n, h, w, c, f = 56, 28, 28, 256, 128  # a partial last wave for both tilings, K = 36 k-blocks
+    g = gen(23)
+    x = randn(g, n, h, w, c)
+    wt = randn(g, 3, 3, c, f, scale=(9 * c) ** -0.5)
+    bias = randn(g, f, scale=0.1)
+    cfg = N.tile_cfg(256 if swap else 128, 4, 0, swap_ab=swap)
+    nbytes = fused.conv_workspace_bytes(n, h, w, c, f, 3, 3, config=cfg)
+    assert nbytes > 0
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    xd, wd_, bd = cuda(x, wt, bias)
+    whole = fused.conv2d_nhwc(xd, wd_, bias=bd, relu=True, config=cfg)
+    for _ in range(2):
+        split = fused.conv2d_nhwc(xd, wd_, bias=bd, relu=True, workspace=ws, config=cfg)
+        torch.testing.assert_close(split.float(), whole.float(), atol=1e-2, rtol=1e-2)
+    assert_close(split[:4], R.conv2d_bias_relu(x[:4], wt, bias, True, 1, 1, 1, out_dtype=torch.bfloat16), TOL)
+    assert int(ws[:256].view(torch.int32).abs().sum()) == 0
+    status_clean()
