@@ -52,6 +52,7 @@ CONSTANTS = {
     # of a tiled load's rate: measured 589 vs 836 TFLOP/s for BN=128 conv vs GEMM tiles
     "im2col_rate": 0.7,
     "fixed_s": 6.0e-6,  # launch + TMEM alloc + pipeline fill + last epilogue
+    "split_overhead_s": 3.0e-6,  # partial write -> fence -> atomic -> reduce chain
     "l2_fraction": 0.6,  # share of L2 that holds one wave's operand working set
 }
 
@@ -62,6 +63,22 @@ def _cdiv(a: int, b: int) -> int:
 
 def _sm_rate(hw: GPUSpec) -> float:
     return CONSTANTS["tensor_rate_fraction"] * hw.peak_fp16_tflops * 1e12 / max(1, hw.num_sm)
+
+
+def split_plan(tiles: int, k_blocks: int, cap: int):
+    """Mirror of the C ABI's split-K tail planner (fo_api.cu plan_split): returns
+    (full_units, left_tiles, split).  Parts keep >= 16 k-blocks; only a last wave less than
+    half full (or a problem with fewer tiles than CTAs) is split, into at most 8 parts."""
+    full = tiles // cap if tiles >= cap else 0
+    left = tiles - full * cap
+    if left == 0 or 2 * left > cap or k_blocks < 2:
+        return full * cap, left, 1
+    split = min(cap // left, 8, k_blocks // 16)
+    if split < 2:
+        return full * cap, left, 1
+    kbp = -(-k_blocks // split)
+    split = -(-k_blocks // kbp)
+    return full * cap, left, max(1, split)
 
 
 def _traffic_bytes(op: OpSpec, c: TuneConfig, hw: GPUSpec, ctas: int) -> float:
@@ -128,7 +145,13 @@ def _model(op: OpSpec, c: TuneConfig, hw: GPUSpec) -> dict:
     t_ln = 0.0
     if op.has_reduction_epilogue:
         t_ln = 2.0 * op.M * op.N * ml.output_element_bytes / K["ln_pass_bytes_per_s"]
+    # split-K tail (single-CTA GEMM / conv with a workspace): the last, less than half-full
+    # wave is split along K, so it costs 1/split of a wave plus the partials' reduction
     t_work = waves * t_tile
+    if not pair and not op.has_reduction_epilogue:
+        dp_units, left, split = split_plan(tiles, k_blocks, ctas)
+        if split > 1:
+            t_work = (dp_units // ctas) * t_tile + -(-left * split // ctas) * t_tile / split + K["split_overhead_s"]
     e_red = t_work / (t_work + t_ln)
     # -- parallel: SM-time used by the persistent grid, plus fixed cost
     quant = tiles / float(waves * sms)
@@ -139,16 +162,19 @@ def _model(op: OpSpec, c: TuneConfig, hw: GPUSpec) -> dict:
     t_mem = traffic / (hw.mem_bandwidth_gbps * 1e9 * K["hbm_efficiency"])
     t_tot = max(t_comp, t_mem) + K["mem_overlap"] * min(t_comp, t_mem)
     e_mem = t_comp / t_tot
-    e_main = padding * e_bn
+    e_main = min(1.0, padding * e_bn)
+    t_pred = t_tot
+    # score = ideal time (all SMs at the achievable tensor rate) / predicted time; the
+    # wave / launch / split share is the residual factor, so the seven multiply to it.
+    t_ideal = ml.mainloop_flops / (_sm_rate(hw) * hw.num_sm)
+    score = min(1.0, t_ideal / t_pred)
+    others = e_main * e_mem * e_pipe * e_conv * e_epi * e_red
+    e_par = score / others if others > 0 else 0.0
     factors = {
         "eff_mainloop": e_main, "eff_memory": e_mem, "eff_parallel": e_par,
         "eff_pipeline": e_pipe, "eff_implicit_conv": e_conv, "eff_epilogue": e_epi,
         "eff_reduction": e_red,
     }
-    score = 1.0
-    for v in factors.values():
-        score *= v
-    t_pred = t_tot
     return {
         "score": score, **factors,
         "projection": {

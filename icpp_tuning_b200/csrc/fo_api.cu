@@ -215,7 +215,7 @@ size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // Work split of a GEMM over `cap` persistent CTAs.  Whole tiles fill as many complete
 // waves as they can; the tiles of a last, less than half-full wave (or of a problem with
-// fewer tiles than CTAs) are split along K into up to 8 parts of >= 8 k-blocks each so
+// fewer tiles than CTAs) are split along K into up to 8 parts of >= 16 k-blocks each so
 // every CTA has work.
 struct SplitPlan {
   int grid, num_units, dp_units, split, kb_per_part, split_tiles;
@@ -231,10 +231,11 @@ SplitPlan plan_split(int tiles, int k_blocks, int cap, bool allow) {
   if (split > 8) split = 8;
   if (split > k_blocks) split = k_blocks;
   if (split < 2) return pl;
-  // Each part must keep >= 8 k-blocks: shorter parts spend as long writing and reducing
-  // their fp32 partials as multiplying (measured on the 3x3x128 conv: 6 k-block parts
-  // made the call 10% slower).
-  if (split > k_blocks / 8) split = k_blocks / 8;
+  // Each part must keep >= 16 k-blocks: shorter parts spend about as long writing and
+  // reducing their fp32 partials (a write -> fence -> atomic -> read chain of ~2-3 us) as
+  // multiplying (measured: 1024^3 with 8-k-block parts and a 3x3x128 conv with 9 got
+  // slower; 4096^3 with 32-k-block parts went from 107 to 103 us).
+  if (split > k_blocks / 16) split = k_blocks / 16;
   if (split < 2) return pl;
   const int kbp = (k_blocks + split - 1) / split;
   split = (k_blocks + kbp - 1) / kbp;  // no empty parts
