@@ -153,7 +153,7 @@ def test_config3_gemm_bias_gelu_mlp():
 @pytest.mark.parametrize("M,Nn,K,bn,layout", [
     (126, 2304, 2048, 64, "kn"),      # 36 tiles on 148 SMs: split 4 ways along K
     (4096, 4096, 4096, 256, "nk"),    # 512 tiles: the 68-tile last wave split 2 ways
-    (300, 520, 1080, 128, "kn"),      # K of 17 k-blocks: uneven parts
+    (300, 520, 2056, 128, "kn"),      # K of 33 k-blocks: uneven parts (17 + 16)
 ])
 def test_split_k_tail(M, Nn, K, bn, layout):
     a, b, bias = _inputs(9, M, Nn, K, torch.bfloat16, layout)
