@@ -858,36 +858,38 @@ __global__ void __launch_bounds__(256) fo_ln_normalize_kernel(const KParams p, i
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * 8 + warp;
   if (row >= p.M) return;
-  float cnt = 0.f, mean = 0.f, m2 = 0.f;
-  for (int j = lane; j < p.tiles_n; j += 32) {
-    const float4 pm = __ldcg(p.ln_stats + static_cast<long long>(j) * p.M + row);
-    chan_merge(cnt, mean, m2, static_cast<float>(min(bn, p.N - j * bn)), pm.x, pm.y);
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float c2 = __shfl_xor_sync(0xffffffffu, cnt, o);
-    const float m2b = __shfl_xor_sync(0xffffffffu, m2, o);
-    const float mb = __shfl_xor_sync(0xffffffffu, mean, o);
-    chan_merge(cnt, mean, m2, c2, mb, m2b);
-  }
-  const float rs = rsqrtf(m2 / static_cast<float>(p.N) + p.eps);
   unsigned short* rowp = reinterpret_cast<unsigned short*>(p.out) + static_cast<long long>(row) * p.ldo;
   const int slabs = (p.N + 255) / 256;
   for (int s0 = 0; s0 < slabs; s0 += 8) {
+    // Issue this batch's row loads first so they overlap the statistics merge.
     uint4 y[8];
-    float off[8];
+    float sh[8];
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const int col = (s0 + u) * 256 + lane * 8;
       if (s0 + u < slabs && col < p.N) {
         y[u] = __ldcg(reinterpret_cast<const uint4*>(rowp + col));
-        off[u] = __ldcg(p.ln_stats + static_cast<long long>(col / bn) * p.M + row).z - mean;
+        sh[u] = __ldcg(p.ln_stats + static_cast<long long>(col / bn) * p.M + row).z;
       }
     }
+    float cnt = 0.f, mean = 0.f, m2 = 0.f;
+    for (int j = lane; j < p.tiles_n; j += 32) {
+      const float4 pm = __ldcg(p.ln_stats + static_cast<long long>(j) * p.M + row);
+      chan_merge(cnt, mean, m2, static_cast<float>(min(bn, p.N - j * bn)), pm.x, pm.y);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float c2 = __shfl_xor_sync(0xffffffffu, cnt, o);
+      const float m2b = __shfl_xor_sync(0xffffffffu, m2, o);
+      const float mb = __shfl_xor_sync(0xffffffffu, mean, o);
+      chan_merge(cnt, mean, m2, c2, mb, m2b);
+    }
+    const float rs = rsqrtf(m2 / static_cast<float>(p.N) + p.eps);
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const int col = (s0 + u) * 256 + lane * 8;
       if (s0 + u < slabs && col < p.N) {
+        const float off = sh[u] - mean;
         float g[8], b[8];
         load_vec8(p.gamma, p.vec_dtype, col, g);
         load_vec8(p.beta, p.vec_dtype, col, b);
@@ -895,8 +897,8 @@ __global__ void __launch_bounds__(256) fo_ln_normalize_kernel(const KParams p, i
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float2 f = unpack2<OUT_DT>(w[e]);
-          w[e] = pack2<OUT_DT>(fmaf((f.x + off[u]) * rs, g[2 * e], b[2 * e]),
-                               fmaf((f.y + off[u]) * rs, g[2 * e + 1], b[2 * e + 1]));
+          w[e] = pack2<OUT_DT>(fmaf((f.x + off) * rs, g[2 * e], b[2 * e]),
+                               fmaf((f.y + off) * rs, g[2 * e + 1], b[2 * e + 1]));
         }
         __stcg(reinterpret_cast<uint4*>(rowp + col), make_uint4(w[0], w[1], w[2], w[3]));
       }
