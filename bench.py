@@ -134,6 +134,51 @@ def _inputs(seed: int, rank: int):
     return a, bt
 
 
+def e2e_pipelined(kern, a_h, bt_h, out_like, dev, steps: int, dist) -> float:
+    """Mean ms per step of `steps` host-to-host calls of kern (see run_ours), max over ranks."""
+    a_p, bt_p = a_h.pin_memory(), bt_h.pin_memory()
+    outs_p = [torch.empty_like(out_like, device="cpu").pin_memory() for _ in range(2)]
+    a_d = [torch.empty_like(a_p, device=dev) for _ in range(2)]
+    bt_d = [torch.empty_like(bt_p, device=dev) for _ in range(2)]
+    out_d = [torch.empty_like(out_like) for _ in range(2)]
+    s_in, s_mm, s_out = (torch.cuda.Stream(dev) for _ in range(3))
+    ev = lambda: torch.cuda.Event()  # noqa: E731
+    in_done = [ev(), ev()]
+    mm_done = [ev(), ev()]
+    out_done = [ev(), ev()]
+
+    def run(n):
+        for i in range(n):
+            k = i & 1
+            with torch.cuda.stream(s_in):
+                s_in.wait_event(mm_done[k]) if i >= 2 else None  # buffer k's last reader finished
+                a_d[k].copy_(a_p, non_blocking=True)
+                bt_d[k].copy_(bt_p, non_blocking=True)
+                in_done[k].record(s_in)
+            with torch.cuda.stream(s_mm):
+                s_mm.wait_event(in_done[k])
+                if i >= 2:
+                    s_mm.wait_event(out_done[k])  # out_d[k] downloaded
+                kern(a_d[k], bt_d[k], out=out_d[k])
+                mm_done[k].record(s_mm)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(mm_done[k])
+                outs_p[k].copy_(out_d[k], non_blocking=True)
+                out_done[k].record(s_out)
+
+    run(4)
+    torch.cuda.synchronize(dev)
+    _barrier(dist)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s_in)
+    run(steps)
+    s_in.wait_stream(s_out)
+    e1.record(s_in)
+    torch.cuda.synchronize(dev)
+    _barrier(dist)
+    return _max_over_ranks(e0.elapsed_time(e1) / steps, dist)
+
+
 def run_ours(args):
     from icpp_tuning_b200 import _native as N
     from icpp_tuning_b200.autotuner.gpu_spec import get_gpu_spec
@@ -179,27 +224,14 @@ def run_ours(args):
         if rank == 0:
             print(json.dumps({"profile_run": True, "ms_per_step": dev_ms / args.steps, "launches": launches}))
         return
-    # end to end through the public callable with host buffers
-    a_p, bt_p = a_h.pin_memory(), bt_h.pin_memory()
-    out_p = torch.empty(M0, N0, dtype=torch.bfloat16).pin_memory()
-    a_d, bt_d = torch.empty_like(a), torch.empty_like(bt)
-    e2e_steps = max(3, min(args.steps, 50))
-    for _ in range(2):
-        a_d.copy_(a_p, non_blocking=True), bt_d.copy_(bt_p, non_blocking=True)
-        out_p.copy_(kern(a_d, bt_d, out=out), non_blocking=True)
-    _barrier(dist)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(e2e_steps):
-        a_d.copy_(a_p, non_blocking=True)
-        bt_d.copy_(bt_p, non_blocking=True)
-        out_p.copy_(kern(a_d, bt_d, out=out), non_blocking=True)
-    e1.record(stream)
-    _barrier(dist)
-    e2e_ms = _max_over_ranks(e0.elapsed_time(e1) / e2e_steps, dist)
+    # End to end through the public callable with host buffers.  Every step copies its
+    # inputs from pinned host memory and reads its result back inside the timed region;
+    # steps are pipelined over three streams (copy-in, compute, copy-out) with two device
+    # buffer sets, so step i+1's upload overlaps step i's multiply and download.
+    e2e_ms = e2e_pipelined(kern, a_h, bt_h, out, dev, max(3, min(args.steps, 50)), dist)
     e2e = {"value": round(flops * ws / (e2e_ms / 1e3) / 1e12, 2), "unit": UNIT,
-           "h2d_bytes_per_step": a_p.numel() * 2 + bt_p.numel() * 2, "d2h_bytes_per_step": out_p.numel() * 2,
-           "ms_per_step": round(e2e_ms, 4)}
+           "h2d_bytes_per_step": a_h.numel() * 2 + bt_h.numel() * 2, "d2h_bytes_per_step": out.numel() * 2,
+           "ms_per_step": round(e2e_ms, 4), "pipelined": "h2d / compute / d2h on three streams, 2 buffer sets"}
 
     if rank != 0:
         if dist is not None:
