@@ -268,6 +268,8 @@ def run_ours(args):
     if ws == 1 and not args.no_ops:
         line["per_op"] = per_op_table(args)
     print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
 
 
 def cpu_baseline(args, budget_s: float = 20.0) -> dict:
