@@ -23,7 +23,7 @@ FO_ETIMEOUT = -5
 FO_DT_F16, FO_DT_BF16, FO_DT_F32 = 0, 1, 2
 FO_B_KN, FO_B_NK = 0, 1
 (FO_EPI_NONE, FO_EPI_BIAS, FO_EPI_BIAS_RELU, FO_EPI_BIAS_GELU_TANH, FO_EPI_BIAS_GELU_ERF,
- FO_EPI_BIAS_LN, FO_EPI_RELU) = range(7)
+ FO_EPI_BIAS_LN, FO_EPI_RELU, FO_EPI_BIAS_RESIDUAL_LN) = range(8)
 FO_NOALLOC_LN_SCRATCH_BYTES = 8 << 20
 
 # Every symbol include/b200fo.h declares; tests check the library exports all of them.
@@ -49,7 +49,8 @@ class FoGemmDesc(ctypes.Structure):
                 ("in_dtype", ctypes.c_int32), ("vec_dtype", ctypes.c_int32),
                 ("out_dtype", ctypes.c_int32), ("b_layout", ctypes.c_int32),
                 ("epilogue", ctypes.c_int32), ("eps", ctypes.c_float),
-                ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t)]
+                ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
+                ("residual", ctypes.c_void_p), ("ldr", ctypes.c_int64)]
 
 
 class FoConvDesc(ctypes.Structure):

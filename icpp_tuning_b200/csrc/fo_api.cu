@@ -207,6 +207,7 @@ int act_of(int epi, int* has_bias) {
     case FO_EPI_BIAS_GELU_ERF: *has_bias = 1; return fo::ACT_GELU_ERF;
     case FO_EPI_BIAS_LN: *has_bias = 1; return fo::ACT_NONE;
     case FO_EPI_RELU: *has_bias = 0; return fo::ACT_RELU;
+    case FO_EPI_BIAS_RESIDUAL_LN: *has_bias = 1; return fo::ACT_NONE;
   }
   return -1;
 }
@@ -346,6 +347,7 @@ int fo_gemm(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
   const int act = act_of(d->epilogue, &has_bias);
   if (act < 0) return fail(FO_EINVAL, "bad epilogue %d", d->epilogue);
   const bool ln = d->epilogue == FO_EPI_BIAS_LN;
+  const bool rln = d->epilogue == FO_EPI_BIAS_RESIDUAL_LN;
   if (has_bias && (d->bias == nullptr || !valid_dt(d->vec_dtype)))
     return fail(FO_EINVAL, "epilogue %d needs a bias vector and a valid vec_dtype", d->epilogue);
   if (d->M == 0 || d->N == 0) return ok();  // empty output: nothing to launch
@@ -364,6 +366,16 @@ int fo_gemm(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
     if (d->ldb < bmin || (d->ldb * ib) % 16 != 0)
       return fail(FO_EINVAL, "ldb=%lld must be >= %lld and a multiple of 8 elements", (long long)d->ldb,
                   (long long)bmin);
+  }
+  if (rln) {
+    if (d->out_dtype == FO_DT_F32) return fail(FO_EINVAL, "LayerNorm output must be f16 or bf16");
+    if (d->gamma == nullptr || d->beta == nullptr || !aligned16(d->gamma) || !aligned16(d->beta))
+      return fail(FO_EINVAL, "LayerNorm needs 16-byte aligned gamma and beta");
+    if (d->N % 8 != 0 || d->N > 4096)
+      return fail(FO_EINVAL, "residual LayerNorm needs N %% 8 == 0 and N <= 4096, got N=%lld", (long long)d->N);
+    if (d->residual == nullptr || !aligned16(d->residual) || d->ldr < d->N || (d->ldr * ob) % 16 != 0)
+      return fail(FO_EINVAL, "residual must be a 16-byte aligned [M, N] tensor of the output dtype with ldr >= N");
+    if (!(d->eps >= 0.0f)) return fail(FO_EINVAL, "eps must be >= 0");
   }
   if (ln) {
     if (d->out_dtype == FO_DT_F32) return fail(FO_EINVAL, "LayerNorm output must be f16 or bf16");
@@ -402,6 +414,8 @@ int fo_gemm(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
   p.eps = d->eps;
   p.out = d->out;
   p.ldo = d->ldo;
+  p.residual = d->residual;
+  p.ldr = d->ldr;
   if (ln) {
     p.ln_stats = reinterpret_cast<float4*>(static_cast<char*>(d->workspace) +
                                            round_up(static_cast<size_t>((p.M + 127) / 128) * 4, 256));
@@ -440,9 +454,11 @@ int fo_gemm(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
   la.smem = fo::smem_bytes_for(bn, cfg->stages, pair);
   la.stream = static_cast<cudaStream_t>(stream);
   const int out_dt = d->out_dtype == FO_DT_F16 ? fo::DT_F16 : d->out_dtype == FO_DT_BF16 ? fo::DT_BF16 : fo::DT_F32;
-  cudaError_t e = ln ? fo::launch_ln_family(bn, out_dt, la) : fo::launch_gemm_family(bn, act, out_dt, la);
+  cudaError_t e = ln ? fo::launch_ln_family(bn, out_dt, la)
+                 : rln ? fo::launch_residual_ln(bn, out_dt, la)
+                       : fo::launch_gemm_family(bn, act, out_dt, la);
   if (e != cudaSuccess) return fail(FO_ECUDA, "kernel launch failed: %s", cudaGetErrorString(e));
-  g_launches.fetch_add(ln ? 2 : 1);  // LayerNorm: GEMM kernel + normalisation kernel
+  g_launches.fetch_add(ln || rln ? 2 : 1);  // LayerNorm: GEMM kernel + row kernel
   return ok();
 }
 

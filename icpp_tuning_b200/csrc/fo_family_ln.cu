@@ -37,4 +37,24 @@ cudaError_t launch_ln_family(int bn, int out_dt, const LaunchArgs& a) {
   return cudaErrorInvalidValue;
 }
 
+// GEMM + bias (16-bit) through the plain family, then the residual LayerNorm row pass.
+cudaError_t launch_residual_ln(int bn, int out_dt, const LaunchArgs& a) {
+  cudaError_t e = launch_gemm_family(bn, ACT_NONE, out_dt, a);
+  if (e != cudaSuccess) return e;
+  const int blocks = (a.p.M + 7) / 8;
+  const int slabs = (a.p.N + 255) / 256;
+  if (out_dt != DT_F16 && out_dt != DT_BF16) return cudaErrorInvalidValue;
+  const bool h = out_dt == DT_F16;
+  if (slabs <= 4)
+    h ? fo_ln_residual_kernel<DT_F16, 4><<<blocks, 256, 0, a.stream>>>(a.p)
+      : fo_ln_residual_kernel<DT_BF16, 4><<<blocks, 256, 0, a.stream>>>(a.p);
+  else if (slabs <= 8)
+    h ? fo_ln_residual_kernel<DT_F16, 8><<<blocks, 256, 0, a.stream>>>(a.p)
+      : fo_ln_residual_kernel<DT_BF16, 8><<<blocks, 256, 0, a.stream>>>(a.p);
+  else
+    h ? fo_ln_residual_kernel<DT_F16, 16><<<blocks, 256, 0, a.stream>>>(a.p)
+      : fo_ln_residual_kernel<DT_BF16, 16><<<blocks, 256, 0, a.stream>>>(a.p);
+  return cudaGetLastError();
+}
+
 }  // namespace fo

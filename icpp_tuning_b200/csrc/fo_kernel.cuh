@@ -57,6 +57,8 @@ struct KParams {
   int vec_dtype;
   float eps;
   float4* ln_stats;  // [tiles_n][M] (mean, M2, shift, 0) of each row over one N tile
+  const void* residual;  // residual LayerNorm: [M, N] rows added before normalising
+  long long ldr;
   void* out;
   long long ldo;
   int* status;  // [0] = code, [1] = where, [2] = block
@@ -902,6 +904,81 @@ __global__ void __launch_bounds__(256) fo_ln_normalize_kernel(const KParams p, i
         }
         __stcg(reinterpret_cast<uint4*>(rowp + col), make_uint4(w[0], w[1], w[2], w[3]));
       }
+    }
+  }
+}
+
+// Residual LayerNorm pass (evaluation/end2end.py:76-79, :84-87 of the reference):
+// out = LN(out + residual) * gamma + beta, one warp per row.  `out` holds the 16-bit
+// GEMM + bias result, as the reference's fp16 matmul does; each lane keeps its 8-column
+// slices of the row and of the residual packed in registers (N <= 4096), so the mean
+// and variance are exact two-pass fp32 statistics of x = out + residual.
+template <int OUT_DT, int kMaxSlabs>  // kMaxSlabs x 256 columns (<= 16)
+__global__ void __launch_bounds__(256) fo_ln_residual_kernel(const KParams p) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + warp;
+  if (row >= p.M) return;
+  unsigned short* rowp = reinterpret_cast<unsigned short*>(p.out) + static_cast<long long>(row) * p.ldo;
+  const unsigned short* resp = reinterpret_cast<const unsigned short*>(p.residual) + static_cast<long long>(row) * p.ldr;
+  const int slabs = (p.N + 255) / 256;
+  uint4 y[kMaxSlabs], r[kMaxSlabs];
+#pragma unroll
+  for (int u = 0; u < kMaxSlabs; ++u) {
+    const int col = u * 256 + lane * 8;
+    if (u < slabs && col < p.N) {
+      y[u] = __ldcg(reinterpret_cast<const uint4*>(rowp + col));
+      r[u] = __ldg(reinterpret_cast<const uint4*>(resp + col));
+    }
+  }
+  auto xval = [&](int u, float (&x)[8]) {
+    const uint32_t wy[4] = {y[u].x, y[u].y, y[u].z, y[u].w}, wr[4] = {r[u].x, r[u].y, r[u].z, r[u].w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 a = unpack2<OUT_DT>(wy[e]), b = unpack2<OUT_DT>(wr[e]);
+      x[2 * e] = a.x + b.x;
+      x[2 * e + 1] = a.y + b.y;
+    }
+  };
+  float sum = 0.f;
+#pragma unroll
+  for (int u = 0; u < kMaxSlabs; ++u) {
+    if (u < slabs && u * 256 + lane * 8 < p.N) {
+      float x[8];
+      xval(u, x);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) sum += x[e];
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float mean = sum / static_cast<float>(p.N);
+  float q = 0.f;
+#pragma unroll
+  for (int u = 0; u < kMaxSlabs; ++u) {
+    if (u < slabs && u * 256 + lane * 8 < p.N) {
+      float x[8];
+      xval(u, x);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) q += (x[e] - mean) * (x[e] - mean);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+  const float rs = rsqrtf(q / static_cast<float>(p.N) + p.eps);
+#pragma unroll
+  for (int u = 0; u < kMaxSlabs; ++u) {
+    const int col = u * 256 + lane * 8;
+    if (u < slabs && col < p.N) {
+      float x[8], g[8], b[8];
+      xval(u, x);
+      load_vec8(p.gamma, p.vec_dtype, col, g);
+      load_vec8(p.beta, p.vec_dtype, col, b);
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        w[e] = pack2<OUT_DT>(fmaf((x[2 * e] - mean) * rs, g[2 * e], b[2 * e]),
+                             fmaf((x[2 * e + 1] - mean) * rs, g[2 * e + 1], b[2 * e + 1]));
+      __stcg(reinterpret_cast<uint4*>(rowp + col), make_uint4(w[0], w[1], w[2], w[3]));
     }
   }
 }

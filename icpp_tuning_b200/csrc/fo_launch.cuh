@@ -71,6 +71,7 @@ cudaError_t launch_gemm_family(int bn, int act, int out_dt, const LaunchArgs& a)
 cudaError_t launch_gemm_family_single(int bn, int act, int out_dt, const LaunchArgs& a);
 cudaError_t launch_gemm_family_pair(int bn, int act, int out_dt, const LaunchArgs& a);
 cudaError_t launch_ln_family(int bn, int out_dt, const LaunchArgs& a);
+cudaError_t launch_residual_ln(int bn, int out_dt, const LaunchArgs& a);
 cudaError_t launch_conv_family(int bn, int act, int out_dt, const LaunchArgs& a);
 
 // Sets the message fo_last_error returns on the calling thread (defined in fo_api.cu).

@@ -19,6 +19,7 @@ EPILOGUES = {
     "none": N.FO_EPI_NONE, "bias": N.FO_EPI_BIAS, "bias_relu": N.FO_EPI_BIAS_RELU,
     "bias_gelu_tanh": N.FO_EPI_BIAS_GELU_TANH, "bias_gelu_erf": N.FO_EPI_BIAS_GELU_ERF,
     "bias_layernorm": N.FO_EPI_BIAS_LN, "relu": N.FO_EPI_RELU,
+    "bias_residual_layernorm": N.FO_EPI_BIAS_RESIDUAL_LN,
 }
 
 
@@ -97,7 +98,8 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, b_layout: str = "kn", epilogue: st
          bias: Optional[torch.Tensor] = None, gamma: Optional[torch.Tensor] = None,
          beta: Optional[torch.Tensor] = None, eps: float = 1e-5,
          out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
-         workspace: Optional[torch.Tensor] = None, config=None, stream=None) -> torch.Tensor:
+         workspace: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None,
+         config=None, stream=None) -> torch.Tensor:
     """out = epilogue(a @ B) with fp32 accumulation.
 
     a: [M, K]; b: [K, N] when b_layout == "kn" (reference layout), [N, K] when "nk".
@@ -105,8 +107,10 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, b_layout: str = "kn", epilogue: st
     ln_workspace_bytes(M, N, config) bytes for the per-row slice statistics.  The other
     epilogues accept an optional zero-filled workspace of workspace_bytes(...) bytes that
     lets the kernel split the tiles of a partial last wave along K.
+    "bias_residual_layernorm" computes LN(a @ B + bias + residual) with the GEMM result
+    rounded to the output dtype before the residual add (the fp16 model-layer semantics).
     """
-    dev = _require_cuda(a, b, bias, gamma, beta, out, workspace)
+    dev = _require_cuda(a, b, bias, gamma, beta, out, workspace, residual)
     if b_layout not in ("kn", "nk"):
         raise ValueError("b_layout must be 'kn' or 'nk'")
     if a.dtype != b.dtype or a.dtype not in (torch.float16, torch.bfloat16):
@@ -140,6 +144,10 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, b_layout: str = "kn", epilogue: st
     d.eps = float(eps)
     if workspace is not None:
         d.workspace, d.workspace_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
+    if residual is not None:
+        if tuple(residual.shape) != (M, Nn) or residual.dtype != out.dtype:
+            raise ValueError(f"residual must be [{M},{Nn}] of the output dtype")
+        d.residual, d.ldr = residual.data_ptr(), _rows(residual, "residual")
     with torch.cuda.device(dev):
         N.check(N.lib().fo_gemm(ctypes.byref(d), ctypes.byref(cfg), _stream(dev, stream)))
     return out

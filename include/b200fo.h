@@ -51,6 +51,8 @@ extern "C" {
 #define FO_EPI_BIAS_GELU_ERF 4  /* C = gelu_erf(A.B + bias)         (end2end.py:83)        */
 #define FO_EPI_BIAS_LN 5        /* C = LN_N(A.B + bias)*gamma+beta  (gemm_bias_layernorm.py:93-164) */
 #define FO_EPI_RELU 6           /* C = relu(A.B), no bias           (conv2d_relu.py:133-139) */
+#define FO_EPI_BIAS_RESIDUAL_LN 7 /* C = LN_N(A.B + bias + residual)*gamma+beta, A.B + bias rounded to
+                                     the output dtype first       (end2end.py:76-79, :84-87) */
 
 /* Tile configuration chosen by the autotuner (icpp_tuning_b200.autotuner).  The
  * reference's TuneConfig is (block_M, block_N, block_K, num_stages, num_warps)
@@ -92,6 +94,8 @@ typedef struct FoGemmDesc {
   float eps;         /* LayerNorm epsilon (reference default 1e-5)                      */
   void* workspace;
   size_t workspace_bytes;
+  const void* residual; /* FO_EPI_BIAS_RESIDUAL_LN: [M, N] of out_dtype, row stride ldr */
+  int64_t ldr;
 } FoGemmDesc;
 
 /* NHWC conv2d as implicit GEMM (reference kernel/tilelang/conv/conv2d.py:208-279):
