@@ -190,6 +190,8 @@ int check_cfg(int op, int out_dtype, const FoTileCfg* cfg, char* why, size_t why
   if (cfg->swap_ab && (op != 1 || cfg->block_m != 128 || cfg->block_n < 128))
     return say("swap_ab is a conv2d mode with block_m 128 and block_n >= 128 (block_n %d)", cfg->block_n);
   if (cfg->max_ctas < 0) return say("max_ctas must be >= 0, got %d", cfg->max_ctas);
+  if (cfg->split_k < 0 || cfg->split_k > 16) return say("split_k must be 0 (automatic) .. 16, got %d", cfg->split_k);
+  if (cfg->split_k > 1 && cfg->block_m == 256) return say("CTA pairs (block_m 256) run whole tiles: split_k %d", cfg->split_k);
   const int smem = fo::smem_bytes_for(cfg->block_n, cfg->stages, cfg->block_m == 256);
   if (smem > 232448) return say("shared memory %d B exceeds the 227 KB per-block limit", smem);
   // TMEM: two fp32 accumulators of block_n columns each, <= 512 columns.
@@ -217,26 +219,34 @@ size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 // Work split of a GEMM over `cap` persistent CTAs.  Whole tiles fill as many complete
 // waves as they can; the tiles of a last, less than half-full wave (or of a problem with
 // fewer tiles than CTAs) are split along K into up to 8 parts of >= 16 k-blocks each so
-// every CTA has work.
+// every CTA has work (`forced` 0).  forced = 1 never splits; forced = s >= 2 splits the
+// tiles of the last partial wave into s parts of any length (the autotuner's choice for
+// small, latency-bound problems, where spreading the loads over more SMs pays).
 struct SplitPlan {
   int grid, num_units, dp_units, split, kb_per_part, split_tiles;
 };
 
-SplitPlan plan_split(int tiles, int k_blocks, int cap, bool allow) {
+SplitPlan plan_split(int tiles, int k_blocks, int cap, bool allow, int forced = 0) {
   SplitPlan pl{tiles < cap ? tiles : cap, tiles, tiles, 1, k_blocks, 0};
-  if (!allow || k_blocks < 2 || tiles <= 0) return pl;
+  if (!allow || forced == 1 || k_blocks < 2 || tiles <= 0) return pl;
   const int full = tiles >= cap ? tiles / cap : 0;
   const int left = tiles - full * cap;
-  if (left == 0 || 2 * left > cap) return pl;
-  int split = cap / left;
-  if (split > 8) split = 8;
-  if (split > k_blocks) split = k_blocks;
-  if (split < 2) return pl;
-  // Each part must keep >= 16 k-blocks: shorter parts spend about as long writing and
-  // reducing their fp32 partials (a write -> fence -> atomic -> read chain of ~2-3 us) as
-  // multiplying (measured: 1024^3 with 8-k-block parts and a 3x3x128 conv with 9 got
-  // slower; 4096^3 with 32-k-block parts went from 107 to 103 us).
-  if (split > k_blocks / 16) split = k_blocks / 16;
+  if (left == 0) return pl;
+  int split;
+  if (forced >= 2) {
+    split = forced < k_blocks ? forced : k_blocks;
+  } else {
+    if (2 * left > cap) return pl;
+    split = cap / left;
+    if (split > 8) split = 8;
+    if (split > k_blocks) split = k_blocks;
+    if (split < 2) return pl;
+    // Each part must keep >= 16 k-blocks: shorter parts spend about as long writing and
+    // reducing their fp32 partials (a write -> fence -> atomic -> read chain of ~2-3 us) as
+    // multiplying (measured: 1024^3 with 8-k-block parts and a 3x3x128 conv with 9 got
+    // slower; 4096^3 with 32-k-block parts went from 107 to 103 us).
+    if (split > k_blocks / 16) split = k_blocks / 16;
+  }
   if (split < 2) return pl;
   const int kbp = (k_blocks + split - 1) / split;
   split = (k_blocks + kbp - 1) / kbp;  // no empty parts
@@ -328,7 +338,7 @@ size_t fo_gemm_workspace_size(const FoGemmDesc* d, const FoTileCfg* cfg) {
   const int bn = cfg->block_n;
   const int tiles = static_cast<int>(((d->M + 127) / 128) * ((d->N + bn - 1) / bn));
   const int cap = cfg->max_ctas > 0 ? cfg->max_ctas : sm_count_or_default();
-  return split_workspace(plan_split(tiles, static_cast<int>((d->K + 63) / 64), cap, true), bn);
+  return split_workspace(plan_split(tiles, static_cast<int>((d->K + 63) / 64), cap, true, cfg->split_k), bn);
 }
 
 int fo_gemm(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
@@ -436,7 +446,7 @@ int fo_gemm(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
   // Persistent grid: one CTA (or CTA pair) per SM (pair of SMs).
   const int cap = pair ? (cfg->max_ctas > 0 ? cfg->max_ctas / 2 : di.sms / 2) : (cfg->max_ctas > 0 ? cfg->max_ctas : di.sms);
   if (cap < 1) return fail(FO_EINVAL, "max_ctas too small for CTA pairs");
-  SplitPlan pl = plan_split(p.num_tiles, p.k_blocks, cap, !ln && !pair);
+  SplitPlan pl = plan_split(p.num_tiles, p.k_blocks, cap, !ln && !pair, cfg->split_k);
   const size_t split_need = split_workspace(pl, bn);
   if (split_need == 0 || d->workspace == nullptr || d->workspace_bytes < split_need || !aligned16(d->workspace))
     pl = plan_split(p.num_tiles, p.k_blocks, cap, false);  // no room for partials: whole tiles only
@@ -487,7 +497,7 @@ extern "C" size_t fo_conv2d_workspace_size(const FoConvDesc* d, const FoTileCfg*
   int tiles = 0, kb = 0;
   if (!conv_grid(d, cfg, &tiles, &kb)) return 0;
   const int cap = cfg->max_ctas > 0 ? cfg->max_ctas : sm_count_or_default();
-  return split_workspace(plan_split(tiles, kb, cap, true), cfg->block_n);
+  return split_workspace(plan_split(tiles, kb, cap, true, cfg->split_k), cfg->block_n);
 }
 
 int fo_conv2d(const FoConvDesc* d, const FoTileCfg* cfg, void* stream) {
@@ -583,7 +593,7 @@ int fo_conv2d(const FoConvDesc* d, const FoTileCfg* cfg, void* stream) {
   if (cap < 1) return fail(FO_EINVAL, "max_ctas too small for CTA pairs");
   la.pair = pair;
   la.swap = swap;
-  SplitPlan pl = plan_split(p.num_tiles, p.k_blocks, cap, !pair && p.conv_tma);
+  SplitPlan pl = plan_split(p.num_tiles, p.k_blocks, cap, !pair && p.conv_tma, cfg->split_k);
   const size_t split_need = split_workspace(pl, bn);
   if (split_need == 0 || d->workspace == nullptr || d->workspace_bytes < split_need || !aligned16(d->workspace))
     pl = plan_split(p.num_tiles, p.k_blocks, cap, false);

@@ -15,8 +15,9 @@
 //               blocks in 128B-swizzled shared memory and write them with TMA stores.
 //               For LayerNorm each thread owns one output row, so exact per-row
 //               (mean, M2) of the fp32 tile slice is a register reduction; the slice
-//               is stored centred on a shift and fo_ln_normalize_kernel (next on the
-//               stream) merges the slices' statistics (Chan et al.) and normalises.
+//               is stored centred on a shift and a row pass (next on the stream:
+//               fo_ln_rows_kernel or fo_ln_normalize_kernel) merges the slices'
+//               statistics (Chan et al.) and normalises.
 // Every wait is bounded (mbar_wait); a wait that runs out records FO_ETIMEOUT in the
 // device status word, raises a CTA-local abort flag, drains its in-flight copies and
 // returns.
@@ -571,6 +572,9 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
         record_error(p, kStatusTimeout, 0x20);
         *abort_flag = 1;
       }
+      // This CTA issues no more MMAs: a dependent row pass may begin launching (it waits
+      // for the whole grid to finish before it reads any output).
+      griddep_launch_dependents();
       // Drain: all issued MMAs complete before TMEM is released.
       if constexpr (PAIR) {
         tc_commit_pair(mapa_shared(bar_drain, 0));
@@ -803,8 +807,8 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
       if (acc == 0) acc_ph ^= 1;
 
       if constexpr (LN) {
-        // Per-tile row statistics; fo_ln_normalize_kernel (launched next on the same
-        // stream) merges them and normalises every row in place.
+        // Per-tile row statistics; the row pass (launched next on the same stream)
+        // merges them and normalises every row in place.
         const int row = row0 + lane;
         if (row < p.M) p.ln_stats[static_cast<long long>(tn) * p.M + row] = make_float4(st_mean, st_m2, shift, 0.f);
       }
@@ -859,6 +863,7 @@ template <int OUT_DT>
 __global__ void __launch_bounds__(256) fo_ln_normalize_kernel(const KParams p, int bn) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * 8 + warp;
+  griddep_wait();
   if (row >= p.M) return;
   unsigned short* rowp = reinterpret_cast<unsigned short*>(p.out) + static_cast<long long>(row) * p.ldo;
   const int slabs = (p.N + 255) / 256;
@@ -908,79 +913,254 @@ __global__ void __launch_bounds__(256) fo_ln_normalize_kernel(const KParams p, i
   }
 }
 
-// Residual LayerNorm pass (evaluation/end2end.py:76-79, :84-87 of the reference):
-// out = LN(out + residual) * gamma + beta, one warp per row.  `out` holds the 16-bit
-// GEMM + bias result, as the reference's fp16 matmul does; each lane keeps its 8-column
-// slices of the row and of the residual packed in registers (N <= 4096), so the mean
-// and variance are exact two-pass fp32 statistics of x = out + residual.
-template <int OUT_DT, int kMaxSlabs>  // kMaxSlabs x 256 columns (<= 16)
-__global__ void __launch_bounds__(256) fo_ln_residual_kernel(const KParams p) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.x * 8 + warp;
-  if (row >= p.M) return;
-  unsigned short* rowp = reinterpret_cast<unsigned short*>(p.out) + static_cast<long long>(row) * p.ldo;
-  const unsigned short* resp = reinterpret_cast<const unsigned short*>(p.residual) + static_cast<long long>(row) * p.ldr;
-  const int slabs = (p.N + 255) / 256;
-  uint4 y[kMaxSlabs], r[kMaxSlabs];
+// Row pass of both LayerNorm epilogues for N <= 1024 * kChunks: one 128-thread block per
+// row, each thread owning kChunks 8-element groups (columns chunk * 1024 + tid * 8), so
+// every load of the row is issued at once and the pass costs about one memory round trip
+// plus two block reductions.  gamma, beta and the residual do not depend on the GEMM and
+// are read before griddep_wait(), overlapping the GEMM's tail when the launch is
+// programmatic.
+//   RESID false (FO_EPI_BIAS_LN): the stored row is centred per BN slice; the slices'
+//     (mean, M2, shift) statistics are merged (Chan et al.) into the row's mean / rstd.
+//   RESID true (FO_EPI_BIAS_RESIDUAL_LN): x = stored (A.B + bias, rounded) + residual,
+//     rounded to the 16-bit output type as the reference's fp16 tensor add does; mean
+//     and variance are two-pass block reductions over the registers.
+// Its registers limit it to ~4 blocks per SM, so it is the small-M pass (every row of a
+// small problem resident at once); large M goes to the warp-per-row kernels.
+template <int OUT_DT, bool RESID, int kChunks>
+__global__ void __launch_bounds__(128) fo_ln_rows_kernel(const KParams p, int bn) {
+  __shared__ float red[3][4];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const long long row = blockIdx.x;
+  unsigned short* rowp = reinterpret_cast<unsigned short*>(p.out) + row * p.ldo;
+  float g[kChunks][8], b[kChunks][8];
+  uint4 r[RESID ? kChunks : 1];
 #pragma unroll
-  for (int u = 0; u < kMaxSlabs; ++u) {
-    const int col = u * 256 + lane * 8;
-    if (u < slabs && col < p.N) {
-      y[u] = __ldcg(reinterpret_cast<const uint4*>(rowp + col));
-      r[u] = __ldg(reinterpret_cast<const uint4*>(resp + col));
+  for (int c = 0; c < kChunks; ++c) {
+    const int col = c * 1024 + tid * 8;
+    if (col < p.N) {
+      load_vec8(p.gamma, p.vec_dtype, col, g[c]);
+      load_vec8(p.beta, p.vec_dtype, col, b[c]);
+      if constexpr (RESID)
+        r[c] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const unsigned short*>(p.residual) +
+                                                   row * p.ldr + col));
     }
   }
-  auto xval = [&](int u, float (&x)[8]) {
-    const uint32_t wy[4] = {y[u].x, y[u].y, y[u].z, y[u].w}, wr[4] = {r[u].x, r[u].y, r[u].z, r[u].w};
+  griddep_wait();
+  uint4 y[kChunks];
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    const int col = c * 1024 + tid * 8;
+    if (col < p.N) y[c] = __ldcg(reinterpret_cast<const uint4*>(rowp + col));
+  }
+  // x values of chunk c, in fp32
+  auto xval = [&](int c, float (&x)[8]) {
+    const uint32_t wy[4] = {y[c].x, y[c].y, y[c].z, y[c].w};
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const float2 a = unpack2<OUT_DT>(wy[e]), b = unpack2<OUT_DT>(wr[e]);
-      x[2 * e] = a.x + b.x;
-      x[2 * e + 1] = a.y + b.y;
+      const float2 a = unpack2<OUT_DT>(wy[e]);
+      x[2 * e] = a.x;
+      x[2 * e + 1] = a.y;
+    }
+    if constexpr (RESID) {  // x = round16(y + residual), the reference's 16-bit add
+      const uint32_t wr[4] = {r[c].x, r[c].y, r[c].z, r[c].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 a = unpack2<OUT_DT>(wr[e]);
+        const float2 q = unpack2<OUT_DT>(pack2<OUT_DT>(x[2 * e] + a.x, x[2 * e + 1] + a.y));
+        x[2 * e] = q.x;
+        x[2 * e + 1] = q.y;
+      }
     }
   };
-  float sum = 0.f;
+  float mean, rs;
+  float sh[kChunks];  // per-chunk shift to add back (LN: slice shift - mean; residual: -mean)
+  if constexpr (RESID) {
+    float sum = 0.f;
 #pragma unroll
-  for (int u = 0; u < kMaxSlabs; ++u) {
-    if (u < slabs && u * 256 + lane * 8 < p.N) {
-      float x[8];
-      xval(u, x);
+    for (int c = 0; c < kChunks; ++c) {
+      if (c * 1024 + tid * 8 < p.N) {
+        float x[8];
+        xval(c, x);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) sum += x[e];
+        for (int e = 0; e < 8; ++e) sum += x[e];
+      }
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) red[0][warp] = sum;
+    __syncthreads();
+    mean = (red[0][0] + red[0][1] + red[0][2] + red[0][3]) / static_cast<float>(p.N);
+    float q = 0.f;
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) {
+      if (c * 1024 + tid * 8 < p.N) {
+        float x[8];
+        xval(c, x);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) q += (x[e] - mean) * (x[e] - mean);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+    if (lane == 0) red[1][warp] = q;
+    __syncthreads();
+    rs = rsqrtf((red[1][0] + red[1][1] + red[1][2] + red[1][3]) / static_cast<float>(p.N) + p.eps);
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) sh[c] = -mean;
+  } else {
+    // slice statistics: thread j < tiles_n reads slice j's; each chunk's shift
+    float cnt = 0.f, m = 0.f, m2 = 0.f;
+    for (int j = tid; j < p.tiles_n; j += 128) {
+      const float4 pm = __ldcg(p.ln_stats + static_cast<long long>(j) * p.M + row);
+      chan_merge(cnt, m, m2, static_cast<float>(min(bn, p.N - j * bn)), pm.x, pm.y);
+    }
+    float shift[kChunks];
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) {
+      const int col = c * 1024 + tid * 8;
+      shift[c] = col < p.N ? __ldcg(p.ln_stats + static_cast<long long>(col / bn) * p.M + row).z : 0.f;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float c2 = __shfl_xor_sync(0xffffffffu, cnt, o);
+      const float mb = __shfl_xor_sync(0xffffffffu, m, o);
+      const float m2b = __shfl_xor_sync(0xffffffffu, m2, o);
+      chan_merge(cnt, m, m2, c2, mb, m2b);
+    }
+    if (lane == 0) {
+      red[0][warp] = cnt;
+      red[1][warp] = m;
+      red[2][warp] = m2;
+    }
+    __syncthreads();
+    cnt = red[0][0];
+    m = red[1][0];
+    m2 = red[2][0];
+#pragma unroll
+    for (int w = 1; w < 4; ++w) chan_merge(cnt, m, m2, red[0][w], red[1][w], red[2][w]);
+    mean = m;
+    rs = rsqrtf(m2 / static_cast<float>(p.N) + p.eps);
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) sh[c] = shift[c] - mean;
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-  const float mean = sum / static_cast<float>(p.N);
-  float q = 0.f;
-#pragma unroll
-  for (int u = 0; u < kMaxSlabs; ++u) {
-    if (u < slabs && u * 256 + lane * 8 < p.N) {
+  for (int c = 0; c < kChunks; ++c) {
+    const int col = c * 1024 + tid * 8;
+    if (col < p.N) {
       float x[8];
-      xval(u, x);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) q += (x[e] - mean) * (x[e] - mean);
-    }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
-  const float rs = rsqrtf(q / static_cast<float>(p.N) + p.eps);
-#pragma unroll
-  for (int u = 0; u < kMaxSlabs; ++u) {
-    const int col = u * 256 + lane * 8;
-    if (u < slabs && col < p.N) {
-      float x[8], g[8], b[8];
-      xval(u, x);
-      load_vec8(p.gamma, p.vec_dtype, col, g);
-      load_vec8(p.beta, p.vec_dtype, col, b);
+      xval(c, x);
       uint32_t w[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e)
-        w[e] = pack2<OUT_DT>(fmaf((x[2 * e] - mean) * rs, g[2 * e], b[2 * e]),
-                             fmaf((x[2 * e + 1] - mean) * rs, g[2 * e + 1], b[2 * e + 1]));
+        w[e] = pack2<OUT_DT>(fmaf((x[2 * e] + sh[c]) * rs, g[c][2 * e], b[c][2 * e]),
+                             fmaf((x[2 * e + 1] + sh[c]) * rs, g[c][2 * e + 1], b[c][2 * e + 1]));
+      __stcg(reinterpret_cast<uint4*>(rowp + col), make_uint4(w[0], w[1], w[2], w[3]));
+    }
+  }
+}
+
+// Bandwidth-oriented row pass (large M, N <= 256 * kSlabs): one warp per row, the whole
+// row loaded by one batch of 16-byte loads per lane (columns u * 256 + lane * 8), the
+// statistics merged with shuffles only (no block barrier), gamma / beta read per slab
+// at the end (they stay in L1 across the block's rows).  Same arithmetic as
+// fo_ln_rows_kernel.
+template <int OUT_DT, bool RESID, int kSlabs>
+__global__ void __launch_bounds__(256) fo_ln_warp_rows_kernel(const KParams p, int bn) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long row = static_cast<long long>(blockIdx.x) * 8 + warp;
+  griddep_wait();
+  if (row >= p.M) return;
+  unsigned short* rowp = reinterpret_cast<unsigned short*>(p.out) + row * p.ldo;
+  uint4 y[kSlabs];
+#pragma unroll
+  for (int u = 0; u < kSlabs; ++u) {
+    const int col = u * 256 + lane * 8;
+    if (col < p.N) y[u] = __ldcg(reinterpret_cast<const uint4*>(rowp + col));
+  }
+  float mean, rs;
+  float sh[kSlabs];
+  if constexpr (RESID) {
+    const unsigned short* resp = reinterpret_cast<const unsigned short*>(p.residual) + row * p.ldr;
+    float sum = 0.f;
+#pragma unroll
+    for (int u = 0; u < kSlabs; ++u) {
+      const int col = u * 256 + lane * 8;
+      if (col < p.N) {
+        const uint4 r = __ldg(reinterpret_cast<const uint4*>(resp + col));
+        uint32_t wy[4] = {y[u].x, y[u].y, y[u].z, y[u].w};
+        const uint32_t wr[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {  // x = round16(y + residual), the reference's 16-bit add
+          const float2 a = unpack2<OUT_DT>(wy[e]), b = unpack2<OUT_DT>(wr[e]);
+          wy[e] = pack2<OUT_DT>(a.x + b.x, a.y + b.y);
+          const float2 q = unpack2<OUT_DT>(wy[e]);
+          sum += q.x + q.y;
+        }
+        y[u] = make_uint4(wy[0], wy[1], wy[2], wy[3]);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    mean = sum / static_cast<float>(p.N);
+    float q2 = 0.f;
+#pragma unroll
+    for (int u = 0; u < kSlabs; ++u) {
+      if (u * 256 + lane * 8 < p.N) {
+        const uint32_t wy[4] = {y[u].x, y[u].y, y[u].z, y[u].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 a = unpack2<OUT_DT>(wy[e]);
+          q2 += (a.x - mean) * (a.x - mean) + (a.y - mean) * (a.y - mean);
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) q2 += __shfl_xor_sync(0xffffffffu, q2, o);
+    rs = rsqrtf(q2 / static_cast<float>(p.N) + p.eps);
+#pragma unroll
+    for (int u = 0; u < kSlabs; ++u) sh[u] = -mean;
+  } else {
+    float shift[kSlabs];
+#pragma unroll
+    for (int u = 0; u < kSlabs; ++u) {
+      const int col = u * 256 + lane * 8;
+      shift[u] = col < p.N ? __ldcg(p.ln_stats + static_cast<long long>(col / bn) * p.M + row).z : 0.f;
+    }
+    float cnt = 0.f, m = 0.f, m2 = 0.f;
+    for (int j = lane; j < p.tiles_n; j += 32) {
+      const float4 pm = __ldcg(p.ln_stats + static_cast<long long>(j) * p.M + row);
+      chan_merge(cnt, m, m2, static_cast<float>(min(bn, p.N - j * bn)), pm.x, pm.y);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float c2 = __shfl_xor_sync(0xffffffffu, cnt, o);
+      const float mb = __shfl_xor_sync(0xffffffffu, m, o);
+      const float m2b = __shfl_xor_sync(0xffffffffu, m2, o);
+      chan_merge(cnt, m, m2, c2, mb, m2b);
+    }
+    mean = m;
+    rs = rsqrtf(m2 / static_cast<float>(p.N) + p.eps);
+#pragma unroll
+    for (int u = 0; u < kSlabs; ++u) sh[u] = shift[u] - mean;
+  }
+#pragma unroll
+  for (int u = 0; u < kSlabs; ++u) {
+    const int col = u * 256 + lane * 8;
+    if (col < p.N) {
+      float g[8], b[8];
+      load_vec8(p.gamma, p.vec_dtype, col, g);
+      load_vec8(p.beta, p.vec_dtype, col, b);
+      uint32_t w[4] = {y[u].x, y[u].y, y[u].z, y[u].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = unpack2<OUT_DT>(w[e]);
+        w[e] = pack2<OUT_DT>(fmaf((f.x + sh[u]) * rs, g[2 * e], b[2 * e]),
+                             fmaf((f.y + sh[u]) * rs, g[2 * e + 1], b[2 * e + 1]));
+      }
       __stcg(reinterpret_cast<uint4*>(rowp + col), make_uint4(w[0], w[1], w[2], w[3]));
     }
   }
 }
 
 }  // namespace fo
+

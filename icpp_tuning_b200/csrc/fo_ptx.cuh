@@ -242,6 +242,13 @@ __device__ __forceinline__ void tc_mma_f16_pair(uint32_t d_tmem, uint64_t adesc,
 }
 // Arrives once on the barrier at cluster address `bar` (either CTA of the pair) when
 // every pair MMA this thread issued before has completed.
+// Programmatic dependent launch: a kernel launched after this one with the
+// programmatic-stream-serialization attribute may start once every CTA of this grid has
+// signalled (or exited); it must call griddep_wait() before reading what this grid wrote.
+// Both are no-ops for launches without dependents / without the attribute.
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ void tc_commit_pair(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
                : "memory");

@@ -69,6 +69,9 @@ typedef struct FoTileCfg {
   int32_t max_ctas; /* persistent grid size cap; 0 = one CTA per SM                     */
   int32_t swap_ab;  /* conv2d only: 1 = compute Y^T = W^T X^T (M = 128 output channels,  */
                     /* N = block_n output pixels) so few-channel convs use wide MMAs     */
+  int32_t split_k;  /* K split of the tiles that do not fill a whole wave of CTAs:        */
+                    /* 0 = automatic (parts of >= 16 k-blocks when under half a wave),    */
+                    /* 1 = never, s = 2..16 = s parts (needs the split workspace)         */
 } FoTileCfg;
 
 /* One GEMM-family call.  A[M,K] row-major (row stride lda elements).  B per b_layout

@@ -14,7 +14,8 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("M,N,K,dt", [(300, 768, 768, torch.float16), (257, 1024, 4096, torch.bfloat16),
-                                      (128, 4096, 512, torch.float16)])
+                                      (128, 4096, 512, torch.float16), (3000, 2304, 256, torch.float16),
+                                      (1500, 4096, 128, torch.bfloat16), (2049, 512, 192, torch.float16)])
 def test_residual_layernorm_epilogue(M, N, K, dt):
     g = gen(40)
     a, b = randn(g, M, K, dtype=dt, scale=0.5), randn(g, K, N, dtype=dt, scale=K ** -0.5)
@@ -23,7 +24,7 @@ def test_residual_layernorm_epilogue(M, N, K, dt):
     a, b, bias, res, gamma, beta = (t.cuda() for t in (a, b, bias, res, gamma, beta))
     out = fused.gemm(a, b, epilogue="bias_residual_layernorm", bias=bias, gamma=gamma, beta=beta, residual=res)
     y = (a.float() @ b.float() + bias.float()).to(dt)  # the GEMM result rounded first
-    ref = F.layer_norm(y.float() + res.float(), (N,), gamma.float(), beta.float(), 1e-5)
+    ref = F.layer_norm((y + res).float(), (N,), gamma.float(), beta.float(), 1e-5)  # 16-bit add, end2end.py:78
     torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=2e-2)
 
 

@@ -37,6 +37,23 @@ def test_ln_ragged(bn, odt):
     status_clean()
 
 
+@pytest.mark.parametrize("M,Nn,bn", [(2000, 1000, 64), (1100, 2304, 256), (3000, 4096, 128), (100, 5000, 256),
+                                     (1500, 6144, 128), (1, 768, 64)])
+def test_ln_row_pass_variants(M, Nn, bn):
+    """Each row-pass kernel: block per row (M <= 1024), warp per row (larger M), and the
+    batched pass for N > 4096; ragged N against the slab / chunk widths."""
+    K = 128
+    x, w, bias, gamma, beta = _inputs(13, M, Nn, K)
+    cfg = N.tile_cfg(bn, {256: 4, 128: 6, 64: 8}[bn], 0)
+    ws = torch.empty(fused.ln_workspace_bytes(M, Nn, cfg), dtype=torch.uint8, device="cuda")
+    out = fused.gemm(*cuda(x, w), b_layout="nk", epilogue="bias_layernorm", bias=bias.cuda(), gamma=gamma.cuda(),
+                     beta=beta.cuda(), workspace=ws, out_dtype=torch.bfloat16, config=cfg)
+    rows = torch.arange(0, M, max(1, M // 64))
+    ref = R.gemm_bias_layernorm(x[rows], w, bias, gamma, beta, b_layout="nk", out_dtype=torch.bfloat16)
+    assert_close(out[rows.cuda()], ref, TOL_LN)
+    status_clean()
+
+
 def test_ln_large_mean_offset():
     """Rows whose mean is far from zero: the centred (Chan) statistics stay accurate
     where E[x^2] - E[x]^2 (the reference LN kernel, gemm_bias_layernorm.py:143) loses bits."""
