@@ -52,7 +52,8 @@ CONSTANTS = {
     # of a tiled load's rate: measured 589 vs 836 TFLOP/s for BN=128 conv vs GEMM tiles
     "im2col_rate": 0.7,
     "fixed_s": 6.0e-6,  # launch + TMEM alloc + pipeline fill + last epilogue
-    "split_overhead_s": 3.0e-6,  # partial write -> fence -> atomic -> reduce chain
+    "split_overhead_s": 3.0e-6,
+    "l2_resident_fraction": 0.4,  # share of L2 an operand can hold across waves (two dies)  # partial write -> fence -> atomic -> reduce chain
     "l2_fraction": 0.6,  # share of L2 that holds one wave's operand working set
 }
 
@@ -96,7 +97,18 @@ def _traffic_bytes(op: OpSpec, c: TuneConfig, hw: GPUSpec, ctas: int) -> float:
     l2 = hw.l2_cache_size * CONSTANTS["l2_fraction"]
     if a_total + b_total <= l2:
         return a_total + b_total + out
-    # Operands larger than L2: each wave re-reads the blocks it touches.
+    # Operands larger than L2.  One operand that fits the resident share of L2 is read
+    # once.  Otherwise a grouped raster keeps the group's A row blocks resident while B
+    # streams past once per group (measured on 8192 x 16384 x 4096: group 16 > 8 > 32,
+    # whose 64 MB of A rows no longer stay resident); without that, each wave re-reads
+    # the blocks it touches.
+    resident = hw.l2_cache_size * CONSTANTS["l2_resident_fraction"]
+    if b_total <= resident or a_total <= resident:
+        return a_total + b_total + out
+    if c.group_size_m > 0 and ml.kind != "implicit_gemm_conv":
+        rows_g = min(tiles_m, c.group_size_m)
+        if rows_g * a_row <= resident:
+            return a_total + _cdiv(tiles_m, rows_g) * b_total + out
     g = c.group_size_m if c.group_size_m > 0 else 1
     if c.group_size_m > 0:
         rows_per_wave = min(tiles_m, g)
@@ -145,10 +157,11 @@ def _model(op: OpSpec, c: TuneConfig, hw: GPUSpec) -> dict:
     t_ln = 0.0
     if op.has_reduction_epilogue:
         t_ln = 2.0 * op.M * op.N * ml.output_element_bytes / K["ln_pass_bytes_per_s"]
-    # split-K tail (single-CTA GEMM / conv with a workspace): the last, less than half-full
-    # wave is split along K, so it costs 1/split of a wave plus the partials' reduction
+    # split-K tail (GEMM, CTA pairs included, and single-CTA conv, with a workspace): the
+    # last, less than half-full wave is split along K, so it costs 1/split of a wave plus
+    # the partials' reduction
     t_work = waves * t_tile
-    if not pair and not op.has_reduction_epilogue:
+    if not op.has_reduction_epilogue and not (pair and ml.kind == "implicit_gemm_conv"):
         dp_units, left, split = split_plan(tiles, k_blocks, ctas)
         if split > 1:
             t_work = (dp_units // ctas) * t_tile + -(-left * split // ctas) * t_tile / split + K["split_overhead_s"]

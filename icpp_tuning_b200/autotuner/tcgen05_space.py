@@ -32,7 +32,7 @@ def max_stages(block_n: int, block_m: int = 128) -> int:
     return s
 
 
-def tcgen05_configs(block_ns: Sequence[int] = (64, 128, 256), group_ms: Sequence[int] = (0, 8, 16),
+def tcgen05_configs(block_ns: Sequence[int] = (64, 128, 256), group_ms: Sequence[int] = (8, 16, 0),
                     conv: bool = False, stages: Sequence[int] = (),
                     block_ms: Sequence[int] = (128, 256)) -> List[Dict[str, Any]]:
     out = []
@@ -41,14 +41,16 @@ def tcgen05_configs(block_ns: Sequence[int] = (64, 128, 256), group_ms: Sequence
             if bm == 256 and bn < 128:
                 continue
             top = max_stages(bn, bm)
-            st = sorted({s for s in (stages or (3, 4, top)) if (3 if conv else 2) <= s <= top})
+            # deepest pipeline first: rank_all keeps generation order among equal scores,
+            # and measured ties (S5 / S6 pairs) never favour the shallower ring
+            st = sorted({s for s in (stages or (3, 4, top)) if (3 if conv else 2) <= s <= top}, reverse=True)
             for s in st:
                 for g in group_ms:
                     out.append({"block_M": bm, "block_N": bn, "block_K": 64, "num_stages": s,
                                 "thread_num": CONV_THREADS if conv else GEMM_THREADS, "group_m": g})
     if conv:  # operand-swapped conv: 128 output channels x block_N pixels per tile
         for bn in (128, 256):
-            for s in sorted({x for x in (stages or (3, 4)) if 3 <= x <= max_stages(bn)}):
+            for s in sorted({x for x in (stages or (3, 4)) if 3 <= x <= max_stages(bn)}, reverse=True):
                 out.append({"block_M": 128, "block_N": bn, "block_K": 64, "num_stages": s,
                             "thread_num": CONV_THREADS, "group_m": 0, "swap_ab": 1})
     return out

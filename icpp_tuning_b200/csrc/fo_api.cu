@@ -191,7 +191,6 @@ int check_cfg(int op, int out_dtype, const FoTileCfg* cfg, char* why, size_t why
     return say("swap_ab is a conv2d mode with block_m 128 and block_n >= 128 (block_n %d)", cfg->block_n);
   if (cfg->max_ctas < 0) return say("max_ctas must be >= 0, got %d", cfg->max_ctas);
   if (cfg->split_k < 0 || cfg->split_k > 16) return say("split_k must be 0 (automatic) .. 16, got %d", cfg->split_k);
-  if (cfg->split_k > 1 && cfg->block_m == 256) return say("CTA pairs (block_m 256) run whole tiles: split_k %d", cfg->split_k);
   const int smem = fo::smem_bytes_for(cfg->block_n, cfg->stages, cfg->block_m == 256);
   if (smem > 232448) return say("shared memory %d B exceeds the 227 KB per-block limit", smem);
   // TMEM: two fp32 accumulators of block_n columns each, <= 512 columns.
@@ -260,10 +259,16 @@ SplitPlan plan_split(int tiles, int k_blocks, int cap, bool allow, int forced = 
   return pl;
 }
 
-size_t split_workspace(const SplitPlan& pl, int bn) {
+// Counters then fp32 partials, per 128-row slot of each split tile (`halves` slots per
+// tile: 2 for CTA pairs).
+size_t split_counter_bytes(const SplitPlan& pl, int halves) {
+  return round_up(static_cast<size_t>(pl.split_tiles) * halves * 4 * sizeof(int), 256);
+}
+
+size_t split_workspace(const SplitPlan& pl, int bn, int halves = 1) {
   if (pl.split < 2) return 0;
-  return round_up(static_cast<size_t>(pl.split_tiles) * 4 * sizeof(int), 256) +
-         static_cast<size_t>(pl.split_tiles) * pl.split * 128 * bn * sizeof(float);
+  return split_counter_bytes(pl, halves) +
+         static_cast<size_t>(pl.split_tiles) * halves * pl.split * 128 * bn * sizeof(float);
 }
 
 int sm_count_or_default() {
@@ -334,11 +339,11 @@ size_t fo_gemm_workspace_size(const FoGemmDesc* d, const FoTileCfg* cfg) {
   if (d->M <= 0 || d->N <= 0) return 0;
   if (d->epilogue == FO_EPI_BIAS_LN) return ln_workspace(d->M, d->N, cfg->block_n);
   // Other epilogues: room for the split-K tail (optional; without it there is no split).
-  if (cfg->block_m == 256) return 0;  // CTA pairs run whole tiles only
-  const int bn = cfg->block_n;
-  const int tiles = static_cast<int>(((d->M + 127) / 128) * ((d->N + bn - 1) / bn));
-  const int cap = cfg->max_ctas > 0 ? cfg->max_ctas : sm_count_or_default();
-  return split_workspace(plan_split(tiles, static_cast<int>((d->K + 63) / 64), cap, true, cfg->split_k), bn);
+  const int bn = cfg->block_n, bm = cfg->block_m, halves = bm / 128;
+  const int tiles = static_cast<int>(((d->M + bm - 1) / bm) * ((d->N + bn - 1) / bn));
+  const int sms = cfg->max_ctas > 0 ? cfg->max_ctas : sm_count_or_default();
+  return split_workspace(plan_split(tiles, static_cast<int>((d->K + 63) / 64), sms / halves, true, cfg->split_k), bn,
+                         halves);
 }
 
 int fo_gemm(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
@@ -446,8 +451,8 @@ int fo_gemm(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
   // Persistent grid: one CTA (or CTA pair) per SM (pair of SMs).
   const int cap = pair ? (cfg->max_ctas > 0 ? cfg->max_ctas / 2 : di.sms / 2) : (cfg->max_ctas > 0 ? cfg->max_ctas : di.sms);
   if (cap < 1) return fail(FO_EINVAL, "max_ctas too small for CTA pairs");
-  SplitPlan pl = plan_split(p.num_tiles, p.k_blocks, cap, !ln && !pair, cfg->split_k);
-  const size_t split_need = split_workspace(pl, bn);
+  SplitPlan pl = plan_split(p.num_tiles, p.k_blocks, cap, !ln, cfg->split_k);
+  const size_t split_need = split_workspace(pl, bn, pair ? 2 : 1);
   if (split_need == 0 || d->workspace == nullptr || d->workspace_bytes < split_need || !aligned16(d->workspace))
     pl = plan_split(p.num_tiles, p.k_blocks, cap, false);  // no room for partials: whole tiles only
   p.num_units = pl.num_units;
@@ -456,8 +461,7 @@ int fo_gemm(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
   p.kb_per_part = pl.kb_per_part;
   if (pl.split > 1) {
     p.split_cnt = static_cast<int*>(d->workspace);
-    p.split_ws = reinterpret_cast<float*>(static_cast<char*>(d->workspace) +
-                                          round_up(static_cast<size_t>(pl.split_tiles) * 4 * sizeof(int), 256));
+    p.split_ws = reinterpret_cast<float*>(static_cast<char*>(d->workspace) + split_counter_bytes(pl, pair ? 2 : 1));
   }
   la.grid = pair ? 2 * pl.grid : pl.grid;
   la.pair = pair;

@@ -71,8 +71,9 @@ struct KParams {
   // work units: units [0, dp_units) are whole tiles; the remaining tiles are split along K
   // into `split` parts of kb_per_part k-blocks, reduced through split_ws / split_cnt.
   int num_units, dp_units, split, kb_per_part;
-  float* split_ws;  // [split tile][part][BN columns][128 rows] fp32 partial accumulators
-  int* split_cnt;   // [split tile][4 row quarters] arrival counters, self-resetting
+  float* split_ws;  // [split slot][part][BN columns][128 rows] fp32 partial accumulators
+  int* split_cnt;   // [split slot][4 row quarters] arrival counters, self-resetting
+                    // (a slot is a split tile's 128 rows: two per tile for CTA pairs)
 };
 
 __host__ __device__ constexpr int b_stage_bytes(int bn) { return bn * kBK * 2; }
@@ -606,8 +607,10 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
       // the warp whose arrival completes its row quarter adds the other parts and runs
       // the epilogue; the other warps release the accumulator and move on.
       float* split_tile = nullptr;
+      // split slot of this CTA's 128 rows (a CTA pair's tile has two)
+      const int sti = PAIR ? un.st * 2 + static_cast<int>(rank) : un.st;
       if (un.st >= 0) {
-        split_tile = p.split_ws + static_cast<long long>(un.st) * p.split * BN * 128;
+        split_tile = p.split_ws + static_cast<long long>(sti) * p.split * BN * 128;
         float* mine = split_tile + static_cast<long long>(un.part) * BN * 128 + quarter * 32 + lane;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
@@ -620,7 +623,7 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
         __threadfence();
         __syncwarp();
         int last = 0;
-        if (lane == 0) last = atomicAdd(p.split_cnt + un.st * 4 + quarter, 1) == p.split - 1;
+        if (lane == 0) last = atomicAdd(p.split_cnt + sti * 4 + quarter, 1) == p.split - 1;
         last = __shfl_sync(0xffffffffu, last, 0);
         if (!last) {
           tc_fence_before();
@@ -637,7 +640,7 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
           continue;
         }
         __threadfence();
-        if (lane == 0) p.split_cnt[un.st * 4 + quarter] = 0;
+        if (lane == 0) p.split_cnt[sti * 4 + quarter] = 0;
       }
       float st_cnt = 0.f, st_mean = 0.f, st_m2 = 0.f;
       float shift = 0.f;  // LayerNorm: the tile is stored centred on its first chunk's mean

@@ -29,6 +29,25 @@ def test_pair_gemm(bn, layout, M, Nn, K):
     status_clean()
 
 
+@pytest.mark.parametrize("M,Nn,K,max_ctas,split_k", [(512, 512, 2048, 0, 0), (1280, 512, 1000, 8, 3),
+                                                    (300, 1304, 520, 0, 4), (2304, 2304, 4096, 0, 0)])
+def test_pair_split_tail(M, Nn, K, max_ctas, split_k):
+    """Pairs whose last partial wave is split along K (each CTA of a pair reduces its own
+    128 rows); repeated calls check the self-resetting arrival counters."""
+    g = gen(35)
+    a, b = randn(g, M, K, scale=K ** -0.25), randn(g, Nn, K, scale=K ** -0.25)
+    cfg = N.tile_cfg(block_n=256, stages=6, group_m=8, max_ctas=max_ctas, block_m=256, split_k=split_k)
+    nbytes = fused.workspace_bytes(M, Nn, K, "none", cfg)
+    assert nbytes > 0
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    ref = R.gemm(a, b, "nk", upcast=True)
+    for _ in range(3):
+        out = fused.gemm(*cuda(a, b), b_layout="nk", out_dtype=torch.float32, workspace=ws, config=cfg)
+        assert_close(out, ref, dict(atol=1e-4, rtol=1e-4))
+    assert int(ws[:32].view(torch.int32).abs().sum()) == 0  # first split tile's counters left zeroed
+    status_clean()
+
+
 @pytest.mark.parametrize("act", ["relu", "gelu_tanh"])
 def test_pair_bias_act_f16(act):
     g = gen(32)
