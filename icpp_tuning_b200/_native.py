@@ -23,7 +23,7 @@ FO_ETIMEOUT = -5
 FO_DT_F16, FO_DT_BF16, FO_DT_F32 = 0, 1, 2
 FO_B_KN, FO_B_NK = 0, 1
 (FO_EPI_NONE, FO_EPI_BIAS, FO_EPI_BIAS_RELU, FO_EPI_BIAS_GELU_TANH, FO_EPI_BIAS_GELU_ERF,
- FO_EPI_BIAS_LN, FO_EPI_RELU, FO_EPI_BIAS_RESIDUAL_LN) = range(8)
+ FO_EPI_BIAS_LN, FO_EPI_RELU, FO_EPI_BIAS_RESIDUAL_LN, FO_EPI_BN, FO_EPI_BN_RELU, FO_EPI_BN_ADD_RELU) = range(11)
 FO_NOALLOC_LN_SCRATCH_BYTES = 8 << 20
 
 # Every symbol include/b200fo.h declares; tests check the library exports all of them.
@@ -61,7 +61,9 @@ class FoConvDesc(ctypes.Structure):
                 ("out", ctypes.c_void_p), ("in_dtype", ctypes.c_int32),
                 ("vec_dtype", ctypes.c_int32), ("out_dtype", ctypes.c_int32),
                 ("epilogue", ctypes.c_int32), ("workspace", ctypes.c_void_p),
-                ("workspace_bytes", ctypes.c_size_t)]
+                ("workspace_bytes", ctypes.c_size_t), ("bn_gamma", ctypes.c_void_p),
+                ("bn_beta", ctypes.c_void_p), ("bn_mean", ctypes.c_void_p), ("bn_var", ctypes.c_void_p),
+                ("bn_eps", ctypes.c_float), ("residual", ctypes.c_void_p)]
 
 
 class FoError(RuntimeError):

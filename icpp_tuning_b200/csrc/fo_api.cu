@@ -209,6 +209,9 @@ int act_of(int epi, int* has_bias) {
     case FO_EPI_BIAS_LN: *has_bias = 1; return fo::ACT_NONE;
     case FO_EPI_RELU: *has_bias = 0; return fo::ACT_RELU;
     case FO_EPI_BIAS_RESIDUAL_LN: *has_bias = 1; return fo::ACT_NONE;
+    case FO_EPI_BN: *has_bias = 0; return fo::ACT_NONE;
+    case FO_EPI_BN_RELU: *has_bias = 0; return fo::ACT_RELU;
+    case FO_EPI_BN_ADD_RELU: *has_bias = 0; return fo::ACT_RELU;
   }
   return -1;
 }
@@ -360,7 +363,8 @@ int fo_gemm(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
   if (d->b_layout != FO_B_KN && d->b_layout != FO_B_NK) return fail(FO_EINVAL, "bad b_layout %d", d->b_layout);
   int has_bias = 0;
   const int act = act_of(d->epilogue, &has_bias);
-  if (act < 0) return fail(FO_EINVAL, "bad epilogue %d", d->epilogue);
+  if (act < 0 || d->epilogue == FO_EPI_BN || d->epilogue == FO_EPI_BN_RELU || d->epilogue == FO_EPI_BN_ADD_RELU)
+    return fail(FO_EINVAL, "bad gemm epilogue %d", d->epilogue);
   const bool ln = d->epilogue == FO_EPI_BIAS_LN;
   const bool rln = d->epilogue == FO_EPI_BIAS_RESIDUAL_LN;
   if (has_bias && (d->bias == nullptr || !valid_dt(d->vec_dtype)))
@@ -516,10 +520,23 @@ int fo_conv2d(const FoConvDesc* d, const FoTileCfg* cfg, void* stream) {
   if (!valid_dt(d->out_dtype)) return fail(FO_EINVAL, "bad out_dtype %d", d->out_dtype);
   int has_bias = 0;
   const int act = act_of(d->epilogue, &has_bias);
-  if (act != fo::ACT_NONE && act != fo::ACT_RELU)
-    return fail(FO_EINVAL, "conv2d epilogue must be NONE, BIAS, RELU or BIAS_RELU");
+  const bool bn_epi = d->epilogue == FO_EPI_BN || d->epilogue == FO_EPI_BN_RELU || d->epilogue == FO_EPI_BN_ADD_RELU;
+  if (act < 0 || (act != fo::ACT_NONE && act != fo::ACT_RELU) || d->epilogue == FO_EPI_BIAS_LN ||
+      d->epilogue == FO_EPI_BIAS_RESIDUAL_LN)
+    return fail(FO_EINVAL, "conv2d epilogue must be NONE, BIAS, RELU, BIAS_RELU, BN, BN_RELU or BN_ADD_RELU");
   if (has_bias && (d->bias == nullptr || !valid_dt(d->vec_dtype)))
     return fail(FO_EINVAL, "conv2d bias epilogue needs a bias vector and a valid vec_dtype");
+  if (bn_epi) {
+    if (d->bn_gamma == nullptr || d->bn_beta == nullptr || d->bn_mean == nullptr || d->bn_var == nullptr ||
+        !valid_dt(d->vec_dtype))
+      return fail(FO_EINVAL, "BatchNorm epilogues need bn_gamma, bn_beta, bn_mean, bn_var and a valid vec_dtype");
+    if (!(d->bn_eps >= 0.0f)) return fail(FO_EINVAL, "bn_eps must be >= 0");
+  }
+  if (d->epilogue == FO_EPI_BN_ADD_RELU) {
+    if (d->out_dtype == FO_DT_F32) return fail(FO_EINVAL, "BN_ADD_RELU needs an f16 or bf16 output and residual");
+    if (d->residual == nullptr || !aligned16(d->residual))
+      return fail(FO_EINVAL, "BN_ADD_RELU needs a 16-byte aligned residual [n, oh, ow, f] of the output dtype");
+  }
   const int oh = (d->h + 2 * d->pad - d->dil * (d->kh - 1) - 1) / d->stride + 1;
   const int ow = (d->w + 2 * d->pad - d->dil * (d->kw - 1) - 1) / d->stride + 1;
   if (oh <= 0 || ow <= 0) return fail(FO_EINVAL, "conv output is empty (oh=%d ow=%d)", oh, ow);
@@ -557,6 +574,18 @@ int fo_conv2d(const FoConvDesc* d, const FoTileCfg* cfg, void* stream) {
   p.has_bias = has_bias;
   p.bias = d->bias;
   p.vec_dtype = d->vec_dtype;
+  if (bn_epi) {
+    p.bn_mode = d->epilogue == FO_EPI_BN_ADD_RELU ? 2 : 1;  // the reference clamps var there only
+    p.bn_eps = d->bn_eps;
+    p.bn_gamma = d->bn_gamma;
+    p.bn_beta = d->bn_beta;
+    p.bn_mean = d->bn_mean;
+    p.bn_var = d->bn_var;
+  }
+  if (d->epilogue == FO_EPI_BN_ADD_RELU) {
+    p.add_src = d->residual;
+    p.ld_add = d->f;
+  }
   p.out = d->out;
   p.ldo = d->f;
   p.x = d->x;

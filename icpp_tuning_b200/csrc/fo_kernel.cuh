@@ -71,6 +71,14 @@ struct KParams {
   // work units: units [0, dp_units) are whole tiles; the remaining tiles are split along K
   // into `split` parts of kb_per_part k-blocks, reduced through split_ws / split_cnt.
   int num_units, dp_units, split, kb_per_part;
+  // conv BatchNorm epilogues (inference form): per output channel f, with acc rounded to
+  // the input dtype first, y = (acc - mean[f]) * rsqrt(var[f] + bn_eps) * gamma[f] + beta[f], var clamped at 0
+  // when bn_mode == 2; then + add_src[pixel][f] when add_src is set; then ACT.
+  int bn_mode;  // 0 none, 1 BN, 2 BN with var clamped at 0
+  float bn_eps;
+  const void *bn_gamma, *bn_beta, *bn_mean, *bn_var;  // vec_dtype
+  const void* add_src;  // [M pixels, N] of the output dtype, row stride ld_add (or null)
+  long long ld_add;
   float* split_ws;  // [split slot][part][BN columns][128 rows] fp32 partial accumulators
   int* split_cnt;   // [split slot][4 row quarters] arrival counters, self-resetting
                     // (a slot is a split tile's 128 rows: two per tile for CTA pairs)
@@ -87,6 +95,28 @@ __device__ __forceinline__ void record_error(const KParams& p, int code, int whe
     p.status[1] = where;
     p.status[2] = static_cast<int>(blockIdx.x);
   }
+}
+
+__device__ __forceinline__ float load_vec(const void* ptr, int dt, int i);
+
+// Per-channel affine of the epilogue: y = acc * scale + shift.  Bias: (1, bias[f]);
+// BatchNorm: scale = gamma * rsqrt(var + eps), shift = beta - mean * scale (var clamped
+// at 0 for bn_mode 2, as the reference's conv_bn_add_relu does).
+__device__ __forceinline__ float2 channel_affine(const KParams& p, int f) {
+  if (f >= p.N) return make_float2(1.f, 0.f);
+  if (p.bn_mode) {
+    float var = load_vec(p.bn_var, p.vec_dtype, f);
+    if (p.bn_mode == 2) var = fmaxf(var, 0.f);
+    const float sc = load_vec(p.bn_gamma, p.vec_dtype, f) * rsqrtf(var + p.bn_eps);
+    return make_float2(sc, fmaf(-load_vec(p.bn_mean, p.vec_dtype, f), sc, load_vec(p.bn_beta, p.vec_dtype, f)));
+  }
+  return make_float2(1.f, p.has_bias ? load_vec(p.bias, p.vec_dtype, f) : 0.f);
+}
+
+// The conv result rounded to the input dtype, as the reference's BatchNorm operators see
+// it (their fp16 F.conv2d / fp16 out_shared tile) before applying the BatchNorm.
+__device__ __forceinline__ float round_in(float v, int ab_bf16) {
+  return ab_bf16 ? __bfloat162float(__float2bfloat16_rn(v)) : __half2float(__float2half_rn(v));
 }
 
 __device__ __forceinline__ float load_vec(const void* ptr, int dt, int i) {
@@ -649,7 +679,10 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
         // transposed through shared memory ([pixel][32 channels], unswizzled) and stored
         // as a 32 x 32 block of the NHWC output.
         const int f = tm * kBM + quarter * 32 + lane;
-        const float bf = (p.has_bias && f < p.N) ? load_vec(p.bias, p.vec_dtype, f) : 0.f;
+        const float2 aff = channel_affine(p, f);
+        const unsigned short* add_col = OUT_DT != DT_F32 && p.add_src != nullptr && f < p.N
+                                            ? reinterpret_cast<const unsigned short*>(p.add_src) + f
+                                            : nullptr;
         constexpr int kRowB = 32 * kOutBytes;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
@@ -678,9 +711,24 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
               for (int i = 0; i < 32; ++i) acc_v[i] += __ldcg(other + (c * 32 + i) * 128);
             }
           }
+          if (add_col != nullptr) {  // residual of the BN-add-ReLU epilogue: pixel rows
+            const int px0 = tn * BN + c * 32;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float a = px0 + i < p.M ? load_vec(add_col + static_cast<long long>(px0 + i) * p.ld_add, OUT_DT, 0)
+                                            : 0.f;
+              acc_v[i] = fmaf(round_in(acc_v[i], p.ab_bf16), aff.x, aff.y) + a;
+            }
+          } else if (p.bn_mode) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc_v[i] = fmaf(round_in(acc_v[i], p.ab_bf16), aff.x, aff.y);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc_v[i] = fmaf(acc_v[i], aff.x, aff.y);
+          }
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            const float val = apply_act<ACT>(acc_v[i] + bf);
+            const float val = apply_act<ACT>(acc_v[i]);
             const uint32_t addr = buf + i * kRowB + lane * kOutBytes;
             if constexpr (OUT_DT == DT_F32) {
               asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(__float_as_uint(val)) : "memory");
@@ -741,13 +789,46 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
             }
           }
         }
-        if (p.has_bias) {
+        if (p.bn_mode) {  // lane i folds column i's BatchNorm; shuffles broadcast it
+#pragma unroll
+          for (int h = 0; h < kCPC / 32; ++h) {
+            const float2 aff = channel_affine(p, cbase + h * 32 + lane);
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              v[h * 32 + i] = fmaf(round_in(v[h * 32 + i], p.ab_bf16), __shfl_sync(0xffffffffu, aff.x, i),
+                                   __shfl_sync(0xffffffffu, aff.y, i));
+          }
+        } else if (p.has_bias) {
 #pragma unroll
           for (int h = 0; h < kCPC / 32; ++h) {
             const int n = cbase + h * 32 + lane;
             const float bl = n < p.N ? load_vec(p.bias, p.vec_dtype, n) : 0.f;
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[h * 32 + i] += __shfl_sync(0xffffffffu, bl, i);
+          }
+        }
+        if constexpr (CONV && OUT_DT != DT_F32) {
+          // residual of the BN-add-ReLU epilogue: this lane's output row, kCPC columns
+          const int row = row0 + lane;
+          if (p.add_src != nullptr && row < p.M) {
+            const unsigned short* ar = reinterpret_cast<const unsigned short*>(p.add_src) + row * p.ld_add + cbase;
+            if (cbase + kCPC <= p.N) {
+#pragma unroll
+              for (int j = 0; j < kCPC / 8; ++j) {
+                const uint4 q = __ldg(reinterpret_cast<const uint4*>(ar) + j);
+                const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float2 f2 = unpack2<OUT_DT>(w[e]);
+                  v[8 * j + 2 * e] += f2.x;
+                  v[8 * j + 2 * e + 1] += f2.y;
+                }
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < kCPC; ++i)
+                if (cbase + i < p.N) v[i] += load_vec(ar, OUT_DT, i);
+            }
           }
         }
 #pragma unroll

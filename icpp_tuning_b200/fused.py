@@ -176,10 +176,17 @@ def default_conv_config(f: int) -> N.FoTileCfg:
 def conv2d_nhwc(x: torch.Tensor, w: torch.Tensor, *, bias: Optional[torch.Tensor] = None,
                 relu: bool = False, stride: int = 1, padding: int = 1, dilation: int = 1,
                 out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
-                workspace: Optional[torch.Tensor] = None, config=None, stream=None) -> torch.Tensor:
+                workspace: Optional[torch.Tensor] = None, config=None, stream=None,
+                bn: Optional[tuple] = None, bn_eps: float = 1e-5,
+                residual: Optional[torch.Tensor] = None) -> torch.Tensor:
     """out[n,oh,ow,f] = act(conv(x[n,h,w,c], w[kh,kw,c,f]) + bias[f]), implicit GEMM.
-    `workspace` (optional, zero-filled, conv_workspace_bytes) enables the split-K tail."""
-    dev = _require_cuda(x, w, bias, out, workspace)
+    `workspace` (optional, zero-filled, conv_workspace_bytes) enables the split-K tail.
+
+    BatchNorm epilogues (inference form, reference conv2d_bn / conv2d_bn_relu /
+    conv_bn_add_relu): bn = (gamma, beta, mean, var), [f] vectors of one dtype, replaces
+    bias: out = act(bn(conv) [+ residual]); `residual` ([n,oh,ow,f], the output dtype)
+    needs relu=True and clamps var at 0, as conv_bn_add_relu does."""
+    dev = _require_cuda(x, w, bias, out, workspace, residual, *(bn or ()))
     if x.dim() != 4 or w.dim() != 4 or not x.is_contiguous() or not w.is_contiguous():
         raise ValueError("x must be contiguous NHWC [n,h,w,c] and w contiguous [kh,kw,c,f]")
     if x.dtype != w.dtype or x.dtype not in (torch.float16, torch.bfloat16):
@@ -195,8 +202,27 @@ def conv2d_nhwc(x: torch.Tensor, w: torch.Tensor, *, bias: Optional[torch.Tensor
     if tuple(out.shape) != (n, oh, ow, f) or not out.is_contiguous():
         raise ValueError(f"out must be contiguous [{n},{oh},{ow},{f}]")
     bias = _vec(bias, f, "bias")
-    epi = {(False, False): N.FO_EPI_NONE, (True, False): N.FO_EPI_BIAS,
-           (False, True): N.FO_EPI_RELU, (True, True): N.FO_EPI_BIAS_RELU}[(bias is not None, relu)]
+    if bn is not None:
+        if bias is not None:
+            raise ValueError("bn replaces bias: pass one of them")
+        if len(bn) != 4:
+            raise ValueError("bn must be (gamma, beta, mean, var)")
+        bn = tuple(_vec(v, f, name) for v, name in zip(bn, ("gamma", "beta", "mean", "var")))
+        if len({v.dtype for v in bn}) != 1:
+            raise ValueError("gamma, beta, mean and var must share one dtype")
+        if residual is not None:
+            if not relu:
+                raise ValueError("the residual epilogue is BN + add + ReLU: pass relu=True")
+            if tuple(residual.shape) != (n, oh, ow, f) or residual.dtype != out.dtype or not residual.is_contiguous():
+                raise ValueError(f"residual must be a contiguous [{n},{oh},{ow},{f}] tensor of {out.dtype}")
+            epi = N.FO_EPI_BN_ADD_RELU
+        else:
+            epi = N.FO_EPI_BN_RELU if relu else N.FO_EPI_BN
+    elif residual is not None:
+        raise ValueError("a residual needs the BatchNorm epilogue (bn=...)")
+    else:
+        epi = {(False, False): N.FO_EPI_NONE, (True, False): N.FO_EPI_BIAS,
+               (False, True): N.FO_EPI_RELU, (True, True): N.FO_EPI_BIAS_RELU}[(bias is not None, relu)]
     d = N.FoConvDesc()
     d.n, d.h, d.w, d.c, d.f, d.kh, d.kw = n, h, wd, c, f, kh, kw
     d.stride, d.pad, d.dil = stride, padding, dilation
@@ -204,6 +230,11 @@ def conv2d_nhwc(x: torch.Tensor, w: torch.Tensor, *, bias: Optional[torch.Tensor
     d.bias = bias.data_ptr() if bias is not None else None
     d.in_dtype, d.out_dtype = dtype_code(x.dtype), dtype_code(out.dtype)
     d.vec_dtype = dtype_code(bias.dtype) if bias is not None else N.FO_DT_F32
+    if bn is not None:
+        d.bn_gamma, d.bn_beta, d.bn_mean, d.bn_var = (v.data_ptr() for v in bn)
+        d.bn_eps = bn_eps
+        d.vec_dtype = dtype_code(bn[0].dtype)
+        d.residual = residual.data_ptr() if residual is not None else None
     d.epilogue = epi
     cfg = as_tile_cfg(config) if config is not None else default_conv_config(f)
     if workspace is not None:

@@ -53,6 +53,12 @@ extern "C" {
 #define FO_EPI_RELU 6           /* C = relu(A.B), no bias           (conv2d_relu.py:133-139) */
 #define FO_EPI_BIAS_RESIDUAL_LN 7 /* C = LN_N(A.B + bias + residual)*gamma+beta, A.B + bias rounded to
                                      the output dtype first       (end2end.py:76-79, :84-87) */
+/* conv2d only, BatchNorm in inference form with per-channel vectors of vec_dtype:
+ * bn(y) = (y - mean) * rsqrt(var + bn_eps) * gamma + beta */
+#define FO_EPI_BN 8          /* Y = bn(conv)                     (conv2d_bn.py:29-45)        */
+#define FO_EPI_BN_RELU 9     /* Y = relu(bn(conv))               (conv2d_bn_relu.py:123-137) */
+#define FO_EPI_BN_ADD_RELU 10 /* Y = relu(bn(conv) + residual), var clamped at 0
+                                                                 (conv_bn_add_relu.py:29-46) */
 
 /* Tile configuration chosen by the autotuner (icpp_tuning_b200.autotuner).  The
  * reference's TuneConfig is (block_M, block_N, block_K, num_stages, num_warps)
@@ -103,7 +109,9 @@ typedef struct FoGemmDesc {
 
 /* NHWC conv2d as implicit GEMM (reference kernel/tilelang/conv/conv2d.py:208-279):
  * x[n,h,w,c], w[kh,kw,c,f] (the reference's weight layout, conv2d.py:224), out[n,oh,ow,f].
- * GEMM view: M = n*oh*ow, N = f, K = kh*kw*c.  Epilogues: NONE, BIAS, RELU, BIAS_RELU. */
+ * GEMM view: M = n*oh*ow, N = f, K = kh*kw*c.  Epilogues: NONE, BIAS, RELU, BIAS_RELU,
+ * BN, BN_RELU, BN_ADD_RELU (BatchNorm vectors bn_* of vec_dtype; the residual of
+ * BN_ADD_RELU is an [n, oh, ow, f] tensor of the 16-bit output dtype). */
 typedef struct FoConvDesc {
   int32_t n, h, w, c, f, kh, kw, stride, pad, dil;
   const void* x;
@@ -116,6 +124,12 @@ typedef struct FoConvDesc {
   int32_t epilogue;
   void* workspace;        /* optional, zero-filled: fp32 partials of the split-K tail */
   size_t workspace_bytes; /* (fo_conv2d_workspace_size); NULL / 0 = no split          */
+  const void* bn_gamma;   /* BatchNorm epilogues: [f] vectors of vec_dtype            */
+  const void* bn_beta;
+  const void* bn_mean;
+  const void* bn_var;
+  float bn_eps;           /* reference defaults: 1e-3 (BN), 1e-5 (BN_RELU, BN_ADD_RELU) */
+  const void* residual;   /* BN_ADD_RELU: [n, oh, ow, f] of out_dtype                  */
 } FoConvDesc;
 
 /* Replaces: the callable from tilelang.compile(...) for gemm / gemm_bias_act /

@@ -102,6 +102,25 @@ def conv2d_bias_relu(X, W, bias=None, relu: bool = True, stride: int = 1, paddin
     return y.permute(0, 2, 3, 1).to(out_dtype)
 
 
+def conv2d_bn(X, W, gamma, beta, mean, var, eps: float = 1e-5, relu: bool = False, residual=None,
+              clamp_var: bool = False, stride: int = 1, padding: int = 1, dilation: int = 1,
+              out_dtype: torch.dtype = torch.float16, upcast: bool = False) -> torch.Tensor:
+    """Conv + BatchNorm (inference form) [+ residual] [+ ReLU], the reference's
+    conv2d_bn.py:29-45 (eps 1e-3 there), conv2d_bn_relu.py:123-137 and
+    conv_bn_add_relu.py:29-46 (var clamped at 0, residual added before the ReLU): the
+    conv in the input dtype, .to(fp32), (y - mean) * rsqrt(var + eps) * gamma + beta."""
+    y = _conv_nchw(X, W, stride, padding, dilation, upcast).to(torch.float32)
+    g, b, m, v = (_cpu(t).float().view(1, -1, 1, 1) for t in (gamma, beta, mean, var))
+    if clamp_var:
+        v = torch.clamp(v, min=0.0)
+    y = (y - m) * torch.rsqrt(v + eps) * g + b
+    if residual is not None:
+        y = y + _cpu(residual).permute(0, 3, 1, 2).float()
+    if relu:
+        y = torch.relu(y)
+    return y.permute(0, 2, 3, 1).to(out_dtype)
+
+
 def conv_flops(n: int, c: int, oh: int, ow: int, f: int, kh: int, kw: int) -> int:
     """2 * N * OH * OW * F * C * KH * KW (conv2d.py:71-72)."""
     return 2 * n * oh * ow * f * c * kh * kw

@@ -59,6 +59,10 @@ def _call(d, cfg=None):
     (dict(out=(1 << 20) + 8), "16-byte"),
     (dict(M=-1), "negative"),
     (dict(epilogue=N.FO_EPI_BIAS_LN, bias=1 << 20), "gamma"),
+    (dict(epilogue=N.FO_EPI_BN_RELU), "gemm epilogue"),  # BatchNorm epilogues are conv-only
+    (dict(epilogue=N.FO_EPI_BIAS_RESIDUAL_LN, bias=1 << 20, gamma=1 << 20, beta=1 << 20), "residual"),
+    (dict(epilogue=N.FO_EPI_BIAS_RESIDUAL_LN, bias=1 << 20, gamma=1 << 20, beta=1 << 20, residual=1 << 20, ldr=256,
+          N=5000, ldo=5000), "N <= 4096"),
 ])
 def test_gemm_rejects(kw, msg):
     rc = _call(_desc(**kw))
@@ -105,6 +109,51 @@ def test_conv_rejects():
     d.epilogue = N.FO_EPI_RELU
     assert N.lib().fo_conv2d(ctypes.byref(d), ctypes.byref(cfg), None) == N.FO_EINVAL
     assert "C % 8" in N.last_error()
+
+
+def _conv_desc(**kw):
+    d = N.FoConvDesc()
+    for k, v in dict(n=1, h=8, w=8, c=16, f=64, kh=3, kw=3, stride=1, pad=1, dil=1).items():
+        setattr(d, k, v)
+    d.x = d.wgt = d.out = 1 << 20
+    d.in_dtype = d.out_dtype = d.vec_dtype = N.FO_DT_BF16
+    for k, v in kw.items():
+        setattr(d, k, v)
+    return d
+
+
+@pytest.mark.parametrize("kw,msg", [
+    (dict(epilogue=N.FO_EPI_BN), "bn_gamma"),
+    (dict(epilogue=N.FO_EPI_BN_RELU, bn_gamma=1 << 20, bn_beta=1 << 20, bn_mean=1 << 20), "bn_var"),
+    (dict(epilogue=N.FO_EPI_BN, bn_gamma=1 << 20, bn_beta=1 << 20, bn_mean=1 << 20, bn_var=1 << 20, bn_eps=-1.0),
+     "bn_eps"),
+    (dict(epilogue=N.FO_EPI_BN_ADD_RELU, bn_gamma=1 << 20, bn_beta=1 << 20, bn_mean=1 << 20, bn_var=1 << 20),
+     "residual"),
+    (dict(epilogue=N.FO_EPI_BN_ADD_RELU, bn_gamma=1 << 20, bn_beta=1 << 20, bn_mean=1 << 20, bn_var=1 << 20,
+          residual=(1 << 20) + 2), "residual"),
+    (dict(epilogue=N.FO_EPI_BN_ADD_RELU, bn_gamma=1 << 20, bn_beta=1 << 20, bn_mean=1 << 20, bn_var=1 << 20,
+          residual=1 << 20, out_dtype=N.FO_DT_F32), "f16 or bf16"),
+    (dict(epilogue=N.FO_EPI_BIAS_LN), "epilogue"),
+])
+def test_conv_batchnorm_rejects(kw, msg):
+    d = _conv_desc(**kw)
+    assert N.lib().fo_conv2d(ctypes.byref(d), ctypes.byref(N.tile_cfg(128, 4, 0)), None) == N.FO_EINVAL
+    assert msg in N.last_error()
+
+
+def test_split_k_field():
+    ok, why = N.config_legal(0, N.FO_DT_BF16, N.tile_cfg(256, 4, 8, split_k=17))
+    assert not ok and "split_k" in why
+    assert N.config_legal(0, N.FO_DT_BF16, N.tile_cfg(256, 6, 8, block_m=256, split_k=4))[0]
+    d = _desc(M=1000, N=1024, K=4096)
+    auto = N.lib().fo_gemm_workspace_size(ctypes.byref(d), ctypes.byref(N.tile_cfg(256, 4, 8)))
+    never = N.lib().fo_gemm_workspace_size(ctypes.byref(d), ctypes.byref(N.tile_cfg(256, 4, 8, split_k=1)))
+    four = N.lib().fo_gemm_workspace_size(ctypes.byref(d), ctypes.byref(N.tile_cfg(256, 4, 8, split_k=4)))
+    # 32 tiles < 148 SMs: the automatic plan splits each into 4 parts of 16 k-blocks;
+    # 4 counters per tile (512 B), then 4 fp32 partial tiles per tile
+    assert never == 0 and auto == four == 512 + 32 * 4 * 128 * 256 * 4
+    pair = N.lib().fo_gemm_workspace_size(ctypes.byref(d), ctypes.byref(N.tile_cfg(256, 6, 8, block_m=256)))
+    assert pair == 512 + 16 * 2 * 4 * 128 * 256 * 4  # 16 pair tiles, 2 halves (slots) each, 4 parts
 
 
 def test_timeout_setting():
