@@ -52,8 +52,12 @@ CONSTANTS = {
     # of a tiled load's rate: measured 589 vs 836 TFLOP/s for BN=128 conv vs GEMM tiles
     "im2col_rate": 0.7,
     "fixed_s": 6.0e-6,  # launch + TMEM alloc + pipeline fill + last epilogue
-    "split_overhead_s": 3.0e-6,
-    "l2_resident_fraction": 0.4,  # share of L2 an operand can hold across waves (two dies)  # partial write -> fence -> atomic -> reduce chain
+    "split_overhead_s": 2.0e-6,  # partial write -> fence -> atomic -> reduce chain
+    # the last-arriving CTA reads each other part's fp32 partial (128 x bn x 4 B) at this rate
+    "split_read_bytes_per_s": 30e9,
+    # one k-block of a 128 x 256 tile on one SM under the power cap (4096^3: 101 us / 3.46 waves / 64)
+    "split_t_kb256_s": 0.45e-6,
+    "l2_resident_fraction": 0.4,  # share of L2 an operand can hold across waves (two dies)
     "l2_fraction": 0.6,  # share of L2 that holds one wave's operand working set
 }
 
@@ -66,15 +70,33 @@ def _sm_rate(hw: GPUSpec) -> float:
     return CONSTANTS["tensor_rate_fraction"] * hw.peak_fp16_tflops * 1e12 / max(1, hw.num_sm)
 
 
-def split_plan(tiles: int, k_blocks: int, cap: int):
+def best_split(k_blocks: int, max_split: int, bn: int, conv: bool = False) -> int:
+    """Mirror of fo_api.cu best_split: the part count minimising k-blocks-per-part x t_kb
+    + (parts - 1) x partial read + chain."""
+    K = CONSTANTS
+    rate = 1.0 if bn >= 256 else 0.66 if bn >= 128 else 0.37
+    t_kb = K["split_t_kb256_s"] * (bn / 256.0) / rate / (K["im2col_rate"] if conv else 1.0)
+    part_s = bn * 512.0 / K["split_read_bytes_per_s"]
+    best, best_t = 1, k_blocks * t_kb
+    for s in range(2, max_split + 1):
+        kbp = -(-k_blocks // s)
+        parts = -(-k_blocks // kbp)
+        t = kbp * t_kb + (parts - 1) * part_s + K["split_overhead_s"]
+        if t < best_t:
+            best, best_t = s, t
+    return best
+
+
+def split_plan(tiles: int, k_blocks: int, cap: int, bn: int = 256, conv: bool = False):
     """Mirror of the C ABI's split-K tail planner (fo_api.cu plan_split): returns
-    (full_units, left_tiles, split).  Parts keep >= 16 k-blocks; only a last wave less than
-    half full (or a problem with fewer tiles than CTAs) is split, into at most 8 parts."""
+    (full_units, left_tiles, split).  Only a last wave less than half full (or a problem
+    with fewer tiles than CTAs) is split, into the cost-minimising part count (<= 8, and
+    <= the idle CTAs per tile)."""
     full = tiles // cap if tiles >= cap else 0
     left = tiles - full * cap
     if left == 0 or 2 * left > cap or k_blocks < 2:
         return full * cap, left, 1
-    split = min(cap // left, 8, k_blocks // 16)
+    split = best_split(k_blocks, min(cap // left, 8, k_blocks), bn, conv)
     if split < 2:
         return full * cap, left, 1
     kbp = -(-k_blocks // split)
@@ -162,9 +184,12 @@ def _model(op: OpSpec, c: TuneConfig, hw: GPUSpec) -> dict:
     # the partials' reduction
     t_work = waves * t_tile
     if not op.has_reduction_epilogue and not (pair and ml.kind == "implicit_gemm_conv"):
-        dp_units, left, split = split_plan(tiles, k_blocks, ctas)
+        # the planner sees the whole persistent grid (cap), not just the busy CTAs
+        conv = ml.kind == "implicit_gemm_conv"
+        dp_units, left, split = split_plan(tiles, k_blocks, cap, bn, conv)
         if split > 1:
-            t_work = (dp_units // ctas) * t_tile + -(-left * split // ctas) * t_tile / split + K["split_overhead_s"]
+            t_work = (dp_units // cap) * t_tile + -(-left * split // cap) * t_tile / split \
+                + K["split_overhead_s"] + (split - 1) * bn * 512.0 / K["split_read_bytes_per_s"]
     e_red = t_work / (t_work + t_ln)
     # -- parallel: SM-time used by the persistent grid, plus fixed cost
     quant = tiles / float(waves * sms)

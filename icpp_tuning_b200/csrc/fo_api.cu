@@ -220,15 +220,38 @@ size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // Work split of a GEMM over `cap` persistent CTAs.  Whole tiles fill as many complete
 // waves as they can; the tiles of a last, less than half-full wave (or of a problem with
-// fewer tiles than CTAs) are split along K into up to 8 parts of >= 16 k-blocks each so
-// every CTA has work (`forced` 0).  forced = 1 never splits; forced = s >= 2 splits the
-// tiles of the last partial wave into s parts of any length (the autotuner's choice for
-// small, latency-bound problems, where spreading the loads over more SMs pays).
+// fewer tiles than CTAs) are split along K (`forced` 0) into the number of parts that
+// minimises the measured cost of a split tile on B200:
+//   parts x k-blocks-per-part x t_kb  +  (parts - 1) x bn x 512 B / 30 GB/s  +  2 us,
+// where t_kb is one k-block of a 128 x bn tile (0.45 us x bn/256 / tensor rate of bn:
+// 1, 0.66, 0.37 for 256, 128, 64; conv's im2col producer at 0.7 of that), the second
+// term the last-arriving CTA reading the other parts' fp32 partials (about 30 GB/s per
+// SM), the third the write -> fence -> atomic chain.  The parts must fit the idle CTAs
+// (left x parts <= cap), at most 8.  forced = 1 never splits; forced = s >= 2 splits the
+// last partial wave into s parts regardless of cost.
 struct SplitPlan {
   int grid, num_units, dp_units, split, kb_per_part, split_tiles;
 };
 
-SplitPlan plan_split(int tiles, int k_blocks, int cap, bool allow, int forced = 0) {
+int best_split(int k_blocks, int max_split, int bn, bool conv) {
+  const double rate = bn >= 256 ? 1.0 : bn >= 128 ? 0.66 : 0.37;
+  const double t_kb = 0.45e-6 * (bn / 256.0) / rate / (conv ? 0.7 : 1.0);
+  const double part_s = bn * 512.0 / 30e9;
+  int best = 1;
+  double best_t = k_blocks * t_kb;
+  for (int s = 2; s <= max_split; ++s) {
+    const int kbp = (k_blocks + s - 1) / s;
+    const int parts = (k_blocks + kbp - 1) / kbp;
+    const double t = kbp * t_kb + (parts - 1) * part_s + 2e-6;
+    if (t < best_t) {
+      best_t = t;
+      best = s;
+    }
+  }
+  return best;
+}
+
+SplitPlan plan_split(int tiles, int k_blocks, int cap, bool allow, int forced = 0, int bn = 256, bool conv = false) {
   SplitPlan pl{tiles < cap ? tiles : cap, tiles, tiles, 1, k_blocks, 0};
   if (!allow || forced == 1 || k_blocks < 2 || tiles <= 0) return pl;
   const int full = tiles >= cap ? tiles / cap : 0;
@@ -239,15 +262,10 @@ SplitPlan plan_split(int tiles, int k_blocks, int cap, bool allow, int forced = 
     split = forced < k_blocks ? forced : k_blocks;
   } else {
     if (2 * left > cap) return pl;
-    split = cap / left;
-    if (split > 8) split = 8;
-    if (split > k_blocks) split = k_blocks;
-    if (split < 2) return pl;
-    // Each part must keep >= 16 k-blocks: shorter parts spend about as long writing and
-    // reducing their fp32 partials (a write -> fence -> atomic -> read chain of ~2-3 us) as
-    // multiplying (measured: 1024^3 with 8-k-block parts and a 3x3x128 conv with 9 got
-    // slower; 4096^3 with 32-k-block parts went from 107 to 103 us).
-    if (split > k_blocks / 16) split = k_blocks / 16;
+    int max_split = cap / left;
+    if (max_split > 8) max_split = 8;
+    if (max_split > k_blocks) max_split = k_blocks;
+    split = best_split(k_blocks, max_split, bn, conv);
   }
   if (split < 2) return pl;
   const int kbp = (k_blocks + split - 1) / split;
@@ -345,7 +363,7 @@ size_t fo_gemm_workspace_size(const FoGemmDesc* d, const FoTileCfg* cfg) {
   const int bn = cfg->block_n, bm = cfg->block_m, halves = bm / 128;
   const int tiles = static_cast<int>(((d->M + bm - 1) / bm) * ((d->N + bn - 1) / bn));
   const int sms = cfg->max_ctas > 0 ? cfg->max_ctas : sm_count_or_default();
-  return split_workspace(plan_split(tiles, static_cast<int>((d->K + 63) / 64), sms / halves, true, cfg->split_k), bn,
+  return split_workspace(plan_split(tiles, static_cast<int>((d->K + 63) / 64), sms / halves, true, cfg->split_k, bn), bn,
                          halves);
 }
 
@@ -455,7 +473,7 @@ int fo_gemm(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
   // Persistent grid: one CTA (or CTA pair) per SM (pair of SMs).
   const int cap = pair ? (cfg->max_ctas > 0 ? cfg->max_ctas / 2 : di.sms / 2) : (cfg->max_ctas > 0 ? cfg->max_ctas : di.sms);
   if (cap < 1) return fail(FO_EINVAL, "max_ctas too small for CTA pairs");
-  SplitPlan pl = plan_split(p.num_tiles, p.k_blocks, cap, !ln, cfg->split_k);
+  SplitPlan pl = plan_split(p.num_tiles, p.k_blocks, cap, !ln, cfg->split_k, bn);
   const size_t split_need = split_workspace(pl, bn, pair ? 2 : 1);
   if (split_need == 0 || d->workspace == nullptr || d->workspace_bytes < split_need || !aligned16(d->workspace))
     pl = plan_split(p.num_tiles, p.k_blocks, cap, false);  // no room for partials: whole tiles only
@@ -505,7 +523,7 @@ extern "C" size_t fo_conv2d_workspace_size(const FoConvDesc* d, const FoTileCfg*
   int tiles = 0, kb = 0;
   if (!conv_grid(d, cfg, &tiles, &kb)) return 0;
   const int cap = cfg->max_ctas > 0 ? cfg->max_ctas : sm_count_or_default();
-  return split_workspace(plan_split(tiles, kb, cap, true, cfg->split_k), cfg->block_n);
+  return split_workspace(plan_split(tiles, kb, cap, true, cfg->split_k, cfg->block_n, true), cfg->block_n);
 }
 
 int fo_conv2d(const FoConvDesc* d, const FoTileCfg* cfg, void* stream) {
@@ -626,7 +644,7 @@ int fo_conv2d(const FoConvDesc* d, const FoTileCfg* cfg, void* stream) {
   if (cap < 1) return fail(FO_EINVAL, "max_ctas too small for CTA pairs");
   la.pair = pair;
   la.swap = swap;
-  SplitPlan pl = plan_split(p.num_tiles, p.k_blocks, cap, !pair && p.conv_tma, cfg->split_k);
+  SplitPlan pl = plan_split(p.num_tiles, p.k_blocks, cap, !pair && p.conv_tma, cfg->split_k, bn, true);
   const size_t split_need = split_workspace(pl, bn);
   if (split_need == 0 || d->workspace == nullptr || d->workspace_bytes < split_need || !aligned16(d->workspace))
     pl = plan_split(p.num_tiles, p.k_blocks, cap, false);

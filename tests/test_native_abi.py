@@ -149,11 +149,13 @@ def test_split_k_field():
     auto = N.lib().fo_gemm_workspace_size(ctypes.byref(d), ctypes.byref(N.tile_cfg(256, 4, 8)))
     never = N.lib().fo_gemm_workspace_size(ctypes.byref(d), ctypes.byref(N.tile_cfg(256, 4, 8, split_k=1)))
     four = N.lib().fo_gemm_workspace_size(ctypes.byref(d), ctypes.byref(N.tile_cfg(256, 4, 8, split_k=4)))
-    # 32 tiles < 148 SMs: the automatic plan splits each into 4 parts of 16 k-blocks;
-    # 4 counters per tile (512 B), then 4 fp32 partial tiles per tile
-    assert never == 0 and auto == four == 512 + 32 * 4 * 128 * 256 * 4
+    # 32 tiles < 148 SMs, 64 k-blocks: at most 4 parts fit the idle SMs; the cost model
+    # (k-blocks per part vs reading 128 KB partials at ~30 GB/s) picks 3; 4 counters per
+    # tile (512 B), then one fp32 partial tile per part
+    assert never == 0
+    assert auto == 512 + 32 * 3 * 128 * 256 * 4 and four == 512 + 32 * 4 * 128 * 256 * 4
     pair = N.lib().fo_gemm_workspace_size(ctypes.byref(d), ctypes.byref(N.tile_cfg(256, 6, 8, block_m=256)))
-    assert pair == 512 + 16 * 2 * 4 * 128 * 256 * 4  # 16 pair tiles, 2 halves (slots) each, 4 parts
+    assert pair == 512 + 16 * 2 * 3 * 128 * 256 * 4  # 16 pair tiles, 2 halves (slots) each, 3 parts
 
 
 def test_timeout_setting():
