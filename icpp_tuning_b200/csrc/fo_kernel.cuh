@@ -677,15 +677,42 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
       if constexpr (SWAP) {
         // TMEM lane = output channel f, column = output pixel.  Each 32-pixel chunk is
         // transposed through shared memory ([pixel][32 channels], unswizzled) and stored
-        // as a 32 x 32 block of the NHWC output.
+        // as a 32 x 32 block of the NHWC output.  The warp's 8 KB of staging holds
+        // kSwapBufs such blocks, so that many TMA stores stay in flight.
         const int f = tm * kBM + quarter * 32 + lane;
+        const int f0 = tm * kBM + quarter * 32;
         const float2 aff = channel_affine(p, f);
-        const unsigned short* add_col = OUT_DT != DT_F32 && p.add_src != nullptr && f < p.N
+        constexpr int kRowB = 32 * kOutBytes;
+        constexpr int kSwapBox = 32 * kRowB;
+        constexpr int kSwapBufs = 2 * kEpiBufBytes / kSwapBox;
+        // Residual of the BN-add-ReLU epilogue.  Whole 32-channel groups: each lane loads
+        // one pixel's 32 channels (4 x 16 B) one chunk ahead, and the chunk is transposed
+        // through the staging block it will be stored from.  A partial channel group
+        // (F not a multiple of 32) reads element by element.
+        const bool vec_add = OUT_DT != DT_F32 && p.add_src != nullptr && f0 + 32 <= p.N;
+        const unsigned short* add_col = OUT_DT != DT_F32 && p.add_src != nullptr && !vec_add && f < p.N
                                             ? reinterpret_cast<const unsigned short*>(p.add_src) + f
                                             : nullptr;
-        constexpr int kRowB = 32 * kOutBytes;
+        const unsigned short* add_grp = vec_add ? reinterpret_cast<const unsigned short*>(p.add_src) + f0 : nullptr;
+        uint4 qn[4] = {};
+        auto load_res = [&](int c) {
+          const int px = tn * BN + c * 32 + lane;
+          if (px < p.M) {
+            const uint4* src = reinterpret_cast<const uint4*>(add_grp + static_cast<long long>(px) * p.ld_add);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) qn[j] = __ldg(src + j);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) qn[j] = make_uint4(0u, 0u, 0u, 0u);
+          }
+        };
+        if (vec_add) load_res(0);
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
+          uint4 q[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) q[j] = qn[j];
+          if (vec_add && c + 1 < BN / 32) load_res(c + 1);
           uint32_t r[32];
           tmem_ld_32x32b_x32(tmem_base + lane_off + acc * BN + c * 32, r);
           tc_wait_ld_regs(r);
@@ -694,9 +721,9 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(bar_tempty + 8 * acc);
           }
-          const uint32_t buf = buf0 + (nstore & 1) * kEpiBufBytes;
-          if (nstore >= 2) {
-            if (lane == 0) bulk_wait_read<1>();
+          const uint32_t buf = buf0 + (nstore % kSwapBufs) * kSwapBox;
+          if (nstore >= kSwapBufs) {
+            if (lane == 0) bulk_wait_read<kSwapBufs - 1>();
             __syncwarp();
           }
 #pragma unroll
@@ -704,27 +731,43 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) acc_v[i] = has_k ? __uint_as_float(r[i]) : 0.f;
           if (split_tile != nullptr) {
-            for (int q = 0; q < p.split; ++q) {
-              if (q == un.part) continue;
-              const float* other = split_tile + static_cast<long long>(q) * BN * 128 + quarter * 32 + lane;
+            for (int qq = 0; qq < p.split; ++qq) {
+              if (qq == un.part) continue;
+              const float* other = split_tile + static_cast<long long>(qq) * BN * 128 + quarter * 32 + lane;
 #pragma unroll
               for (int i = 0; i < 32; ++i) acc_v[i] += __ldcg(other + (c * 32 + i) * 128);
             }
           }
-          if (add_col != nullptr) {  // residual of the BN-add-ReLU epilogue: pixel rows
-            const int px0 = tn * BN + c * 32;
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const float a = px0 + i < p.M ? load_vec(add_col + static_cast<long long>(px0 + i) * p.ld_add, OUT_DT, 0)
-                                            : 0.f;
-              acc_v[i] = fmaf(round_in(acc_v[i], p.ab_bf16), aff.x, aff.y) + a;
-            }
-          } else if (p.bn_mode) {
+          if (p.bn_mode) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) acc_v[i] = fmaf(round_in(acc_v[i], p.ab_bf16), aff.x, aff.y);
           } else {
 #pragma unroll
             for (int i = 0; i < 32; ++i) acc_v[i] = fmaf(acc_v[i], aff.x, aff.y);
+          }
+          if constexpr (OUT_DT != DT_F32) {
+            if (vec_add) {
+              // pixel rows in, channel columns out: every lane reads back exactly the
+              // elements it overwrites below, so one warp barrier suffices
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(buf + lane * kRowB + j * 16),
+                             "r"(q[j].x), "r"(q[j].y), "r"(q[j].z), "r"(q[j].w)
+                             : "memory");
+              __syncwarp();
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                unsigned short h;
+                asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(buf + i * kRowB + lane * 2) : "memory");
+                acc_v[i] += unpack2<OUT_DT>(static_cast<uint32_t>(h)).x;
+              }
+            } else if (add_col != nullptr) {
+              const int px0 = tn * BN + c * 32;
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                acc_v[i] += px0 + i < p.M ? load_vec(add_col + static_cast<long long>(px0 + i) * p.ld_add, OUT_DT, 0)
+                                          : 0.f;
+            }
           }
 #pragma unroll
           for (int i = 0; i < 32; ++i) {

@@ -140,31 +140,69 @@ def run_gemm_sweep(op: str, Ms: Sequence[int], N: int = 2304, K: int = 768, base
     return rows
 
 
+CONV_OPS = ("conv2d", "conv2d_bn_relu", "conv_bn_add_relu")
+
+
+def _conv_case(op, N, C, H, W, Fo, KH, KW, S, P, baseline, g):
+    """(ours, theirs, check, descriptor, config, score) for one conv shape of `op`.  The
+    BatchNorm ops follow their reference checks (conv2d_bn_relu.py:293-316,
+    conv_bn_add_relu.py:188-216): randn gamma / beta / mean, var = rand + 0.5."""
+    from .conv import conv2d_bn_relu, conv_bn_add_relu
+
+    X = torch.randn(N, H, W, C, generator=g).half().cuda()
+    Wt = (torch.randn(KH, KW, C, Fo, generator=g) / (KH * KW * C) ** 0.5).half().cuda()
+    mod = {"conv2d": conv_mod, "conv2d_bn_relu": conv2d_bn_relu, "conv_bn_add_relu": conv_bn_add_relu}[op]
+    cfg, score = select_best(mod.DESCRIPTOR, N=N, C=C, H=H, W=W, OC=Fo, KH=KH, KW=KW, stride=S, padding=P)
+    OH, OW = conv_mod.calc_oh_ow(H, W, KH, KW, S, P, 1)
+    Y = torch.empty(N, OH, OW, Fo, dtype=torch.float16, device="cuda")
+    Yr = torch.empty_like(Y)
+    ref = mod.get_ref_program(S, P, 1)
+    Xc = X.permute(0, 3, 1, 2)
+    Wc = Wt.permute(3, 2, 0, 1).contiguous(memory_format=torch.channels_last)
+    if op == "conv2d":
+        kern = conv_mod.build_conv2d_kernel(N, C, H, W, Fo, KH, KW, S, P, config=cfg)
+        ours, run_ref = (lambda: kern(X, Wt, Y)), (lambda: ref(X, Wt, Yr))
+        native = lambda: F.conv2d(Xc, Wc, stride=S, padding=P)
+    else:
+        gamma, beta, mean = (torch.randn(Fo, generator=g).half().cuda() for _ in range(3))
+        var = (torch.rand(Fo, generator=g) + 0.5).half().cuda()
+        eps = mod.EPS
+        scale = (gamma.float() * torch.rsqrt(var.float() + eps)).view(1, -1, 1, 1)
+        shift = (beta.float() - mean.float() * scale.view(-1)).view(1, -1, 1, 1)
+        if op == "conv2d_bn_relu":
+            kern = conv2d_bn_relu.build_conv2d_bn_relu_kernel(N, C, H, W, Fo, KH, KW, S, P, config=cfg)
+            ours = lambda: kern(X, Wt, gamma, beta, mean, var, Y)
+            run_ref = lambda: ref(X, Wt, gamma, beta, mean, var, Yr)
+            native = lambda: torch.relu(F.conv2d(Xc, Wc, stride=S, padding=P) * scale + shift)
+        else:
+            res = torch.randn(N, OH, OW, Fo, generator=g).half().cuda()
+            resc = res.permute(0, 3, 1, 2)
+            kern = conv_bn_add_relu.build_conv2d_bn_add_relu_kernel(N, C, H, W, Fo, KH, KW, S, P, config=cfg)
+            ours = lambda: kern(X, Wt, res, gamma, beta, mean, var, Y)
+            run_ref = lambda: ref(X, Wt, res, gamma, beta, mean, var, Yr)
+            native = lambda: torch.relu(F.conv2d(Xc, Wc, stride=S, padding=P) * scale + shift + resc)
+
+    def check():
+        ours()
+        run_ref()
+        return bool(torch.allclose(Y.float(), Yr.float(), rtol=1e-2, atol=1e-2))
+
+    return ours, (run_ref if baseline == "reference" else native), check, mod.DESCRIPTOR, cfg, score
+
+
 def run_conv_sweep(shapes=CONV_SHAPES, baseline: str = "reference", warmup: int = 10, rep: int = 50,
-                   log=print) -> List[Dict[str, object]]:
+                   log=print, op: str = "conv2d") -> List[Dict[str, object]]:
+    """`native` baselines: cuDNN on channels-last views (no permute copies) plus the
+    BatchNorm / residual / ReLU as PyTorch elementwise ops."""
     rows = []
     g = torch.Generator().manual_seed(0)
     for idx, (N, C, H, W, Fo, KH, KW, S, P) in enumerate(shapes, 1):
-        X = torch.randn(N, H, W, C, generator=g).half().cuda()
-        Wt = (torch.randn(KH, KW, C, Fo, generator=g) / (KH * KW * C) ** 0.5).half().cuda()
-        cfg, score = select_best(conv_mod.DESCRIPTOR, N=N, C=C, H=H, W=W, OC=Fo, KH=KH, KW=KW, stride=S, padding=P)
-        kern = conv_mod.build_conv2d_kernel(N, C, H, W, Fo, KH, KW, S, P, config=cfg)
-        Y = torch.empty(kern.out_shape, dtype=torch.float16, device="cuda")
-        Yr = torch.empty_like(Y)
-        ref = conv_mod.get_ref_program(S, P, 1)
-        if baseline == "reference":
-            theirs = lambda: ref(X, Wt, Yr)
-        else:  # channels-last tensors: cuDNN runs NHWC directly, no permute copies
-            Xc = X.permute(0, 3, 1, 2)
-            Wc = Wt.permute(3, 2, 0, 1).contiguous(memory_format=torch.channels_last)
-            theirs = lambda: F.conv2d(Xc, Wc, stride=S, padding=P)
-        t_ours = do_bench(lambda: kern(X, Wt, Y), warmup, rep)
+        ours, theirs, check, desc, cfg, score = _conv_case(op, N, C, H, W, Fo, KH, KW, S, P, baseline, g)
+        t_ours = do_bench(ours, warmup, rep)
         t_torch = do_bench(theirs, warmup, rep)
-        kern(X, Wt, Y)
-        ref(X, Wt, Yr)
-        ok = bool(torch.allclose(Y.float(), Yr.float(), rtol=1e-2, atol=1e-2))
-        cfg_str = conv_mod.DESCRIPTOR.format_config(cfg)
-        log(f"conv [{idx}] N={N} C={C} H={H} W={W} F={Fo} {KH}x{KW} s{S} p{P}  {cfg_str}  formula {t_ours:.4f} ms  "
+        ok = check()
+        cfg_str = desc.format_config(cfg)
+        log(f"{op} [{idx}] N={N} C={C} H={H} W={W} F={Fo} {KH}x{KW} s{S} p{P}  {cfg_str}  formula {t_ours:.4f} ms  "
             f"torch {t_torch:.4f} ms  speedup {t_torch / t_ours:.4f}x  correct={ok}")
         rows.append({"Index": idx, "N": N, "C": C, "H": H, "W": W, "F_out": Fo, "Kernel_H": KH, "Kernel_W": KW,
                      "Stride": S, "Pad": P, "Formula_Config": cfg_str, "Formula_Score": f"{score:.6f}",
@@ -200,7 +238,7 @@ def summarize(rows: Sequence[Dict[str, object]], worst: int = 5) -> str:
 
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description="formula top-1 kernels vs torch over the reference's sweeps")
-    ap.add_argument("--op", default="all", choices=("all", "conv2d") + GEMM_OPS)
+    ap.add_argument("--op", default="all", choices=("all",) + CONV_OPS + GEMM_OPS)
     ap.add_argument("--m-start", type=int, default=1)
     ap.add_argument("--m-stop", type=int, default=128)
     ap.add_argument("--m-step", type=int, default=5)
@@ -226,8 +264,9 @@ def main(argv=None) -> None:
         write_csv(out / "gemm_three_ops_formula_summary.csv", GEMM_FIELDS, all_rows)
         if args.report:
             Path(args.report).write_text(summarize(all_rows))
-    if args.op in ("all", "conv2d"):
-        write_csv(out / "conv2d_formula.csv", CONV_FIELDS, run_conv_sweep(baseline=args.torch_baseline))
+    for op in CONV_OPS:
+        if args.op in ("all", op):
+            write_csv(out / f"{op}_formula.csv", CONV_FIELDS, run_conv_sweep(baseline=args.torch_baseline, op=op))
 
 
 if __name__ == "__main__":
