@@ -280,10 +280,11 @@ SplitPlan plan_split(int tiles, int k_blocks, int cap, bool allow, int forced = 
   return pl;
 }
 
-// Counters then fp32 partials, per 128-row slot of each split tile (`halves` slots per
-// tile: 2 for CTA pairs).
+// Counters (8 per slot: 4 row quarters x 2 column halves, one per epilogue warp) then
+// fp32 partials, per 128-row slot of each split tile (`halves` slots per tile: 2 for
+// CTA pairs).
 size_t split_counter_bytes(const SplitPlan& pl, int halves) {
-  return round_up(static_cast<size_t>(pl.split_tiles) * halves * 4 * sizeof(int), 256);
+  return round_up(static_cast<size_t>(pl.split_tiles) * halves * 8 * sizeof(int), 256);
 }
 
 size_t split_workspace(const SplitPlan& pl, int bn, int halves = 1) {
@@ -301,10 +302,14 @@ int sm_count_or_default() {
   return 148;
 }
 
+// LayerNorm statistics: one float4 per row per slice, a slice being the column half of
+// an N tile that one epilogue warp covers (the whole tile for block_n 64).
+int ln_halves(int bn) { return bn >= 128 ? 2 : 1; }
+
 size_t ln_workspace(int64_t M, int64_t N, int bn) {
   const int64_t tiles_m = (M + 127) / 128;
-  const int64_t tiles_n = (N + bn - 1) / bn;
-  return round_up(static_cast<size_t>(tiles_m) * 4, 256) + static_cast<size_t>(tiles_n * M) * 16;
+  const int64_t slices = (N + bn - 1) / bn * ln_halves(bn);
+  return round_up(static_cast<size_t>(tiles_m) * 4, 256) + static_cast<size_t>(slices * M) * 16;
 }
 
 void fill_common(fo::KParams& p, const DevInfo& di) {
@@ -655,7 +660,7 @@ int fo_conv2d(const FoConvDesc* d, const FoTileCfg* cfg, void* stream) {
   if (pl.split > 1) {
     p.split_cnt = static_cast<int*>(d->workspace);
     p.split_ws = reinterpret_cast<float*>(static_cast<char*>(d->workspace) +
-                                          round_up(static_cast<size_t>(pl.split_tiles) * 4 * sizeof(int), 256));
+                                          split_counter_bytes(pl, 1));
   }
   la.grid = pl.grid * (pair ? 2 : 1);
   la.smem = fo::smem_bytes_for(bn, cfg->stages, pair);

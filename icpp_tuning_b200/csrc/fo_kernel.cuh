@@ -35,9 +35,13 @@ enum : int { ACT_NONE = 0, ACT_RELU = 1, ACT_GELU_TANH = 2, ACT_GELU_ERF = 3 };
 constexpr int kBM = 128;
 constexpr int kBK = 64;  // 64 16-bit elements = one 128-byte swizzle row
 constexpr int kAStageBytes = kBM * kBK * 2;
-constexpr int kEpiWarps = 4;
+// Eight epilogue warps: two per TMEM lane quarter (a warp may read only lanes
+// 32 * (warp % 4) ..), each taking half of the tile's columns, so the per-element work of
+// the epilogue (activation, statistics, conversion) is spread over two warps per SM
+// sub-partition.  Each warp stages its stores in one 4 KB block (32 rows x 128 B).
+constexpr int kEpiWarps = 8;
 constexpr int kEpiBufBytes = 32 * 128;
-constexpr int kEpiBytes = kEpiWarps * 2 * kEpiBufBytes;
+constexpr int kEpiBytes = kEpiWarps * kEpiBufBytes;
 constexpr int kMiscBytes = 1536;
 constexpr int kMaxStages = 8;
 
@@ -126,6 +130,20 @@ __device__ __forceinline__ float load_vec(const void* ptr, int dt, int i) {
   return __half2float(__ushort_as_half(raw));
 }
 
+// erf(z) by Abramowitz & Stegun, Handbook of Mathematical Functions, 7.1.26:
+// erf(z) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-z^2), t = 1 / (1 + p z),
+// |error| <= 1.5e-7 (about 5e-7 evaluated in fp32 with the approximate reciprocal and
+// exponential below), odd in z.  One reciprocal, one ex2 and six FMAs, branch-free.
+__device__ __forceinline__ float erf_as7126(float z) {
+  const float az = fabsf(z);
+  const float t = __fdividef(1.0f, fmaf(0.3275911f, az, 1.0f));
+  const float poly =
+      fmaf(fmaf(fmaf(fmaf(1.061405429f, t, -1.453152027f), t, 1.421413741f), t, -0.284496736f), t, 0.254829592f) * t;
+  float e;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-1.4426950408889634f * az * az));  // exp(-z^2)
+  return copysignf(fmaf(-poly, e, 1.0f), z);
+}
+
 template <int ACT>
 __device__ __forceinline__ float apply_act(float x) {
   if constexpr (ACT == ACT_RELU) {
@@ -137,7 +155,7 @@ __device__ __forceinline__ float apply_act(float x) {
     asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(u));
     return 0.5f * x * (1.0f + t);
   } else if constexpr (ACT == ACT_GELU_ERF) {
-    return 0.5f * x * (1.0f + erff(x * 0.7071067811865476f));
+    return 0.5f * x * (1.0f + erf_as7126(x * 0.7071067811865476f));
   } else {
     return x;
   }
@@ -161,6 +179,24 @@ __device__ __forceinline__ float2 unpack2(uint32_t u) {
   } else {
     __half2 h = *reinterpret_cast<__half2*>(&u);
     return __half22float2(h);
+  }
+}
+
+// Eight consecutive vector elements i..i+7 (16-byte aligned) as fp32.
+__device__ __forceinline__ void load_vec8(const void* ptr, int dt, int i, float (&f)[8]) {
+  if (dt == DT_F32) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(ptr) + i / 4);
+    const float4 b = __ldg(reinterpret_cast<const float4*>(ptr) + i / 4 + 1);
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+    return;
+  }
+  const uint4 u = __ldg(reinterpret_cast<const uint4*>(ptr) + i / 8);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 v = dt == DT_BF16 ? unpack2<DT_BF16>(w[e]) : unpack2<DT_F16>(w[e]);
+    f[2 * e] = v.x;
+    f[2 * e + 1] = v.y;
   }
 }
 
@@ -244,7 +280,7 @@ __device__ __forceinline__ void drain_loads(uint32_t bar_full, int stages, int i
 }
 
 template <int BN, int ACT, int OUT_DT, bool LN, bool CONV, bool PAIR, bool SWAP = false>
-__global__ void __launch_bounds__(CONV ? 288 : 192, 1)
+__global__ void __launch_bounds__(CONV ? 416 : 320, 1)
     fo_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const __grid_constant__ CUtensorMap tmC, const KParams p) {
   constexpr int kProducerWarps = CONV ? 4 : 1;
@@ -264,6 +300,11 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
   constexpr int kOutBytes = OUT_DT == DT_F32 ? 4 : 2;
   constexpr int kCPC = 128 / kOutBytes;  // output columns per 128-byte chunk
   constexpr int kChunks = BN / kCPC;
+  // Column halves of the epilogue: each half is taken by one warp of a lane quarter.  A
+  // 16-bit BN 64 tile is a single 128-byte store chunk, so only its first half has work.
+  constexpr int kHalves = SWAP ? 2 : (kChunks >= 2 ? 2 : 1);
+  constexpr int kHalfChunks = kChunks / kHalves;   // store chunks per half (non-swapped)
+  constexpr int kHalfCols = BN / kHalves;          // columns per half
   constexpr uint32_t kTmemCols = 2 * BN;
   static_assert(!LN || OUT_DT != DT_F32, "LayerNorm output is 16-bit");
 
@@ -616,10 +657,13 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
     }
   } else if (warp < kFirstEpiWarp + kEpiWarps) {
     // ------------------------------------------------------------------ epilogue
-    const int ew = warp - kFirstEpiWarp;  // 0..3
+    const int ew = warp - kFirstEpiWarp;  // 0..7
     const int quarter = warp & 3;         // TMEM lane quarter this warp may access
+    const int half = ew >> 2;             // column half of the tile this warp takes
+    const bool idle = half >= kHalves;    // (16-bit BN 64: the second half is empty)
+    const int hcol = half * kHalfCols;    // first tile column of this warp's half
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t buf0 = sEpi + ew * 2 * kEpiBufBytes;
+    const uint32_t buf0 = sEpi + ew * kEpiBufBytes;
     int acc = 0;
     uint32_t acc_ph = 0;
     uint32_t nstore = 0;
@@ -633,9 +677,23 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
         break;
       }
       tc_fence_after();
-      // Split tile: publish this part's fp32 partial ([column][128 rows], coalesced), then
-      // the warp whose arrival completes its row quarter adds the other parts and runs
-      // the epilogue; the other warps release the accumulator and move on.
+      if (idle) {
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (PAIR) {
+            mbar_arrive_cluster(mapa_shared(bar_tempty + 8 * acc, 0));
+          } else {
+            mbar_arrive(bar_tempty + 8 * acc);
+          }
+        }
+        acc ^= 1;
+        if (acc == 0) acc_ph ^= 1;
+        continue;
+      }
+      // Split tile: publish this part's fp32 partial of the warp's (quarter, half)
+      // ([column][128 rows], coalesced), then the warp whose arrival completes that
+      // (quarter, half) adds the other parts and runs the epilogue; the other warps
+      // release the accumulator and move on.
       float* split_tile = nullptr;
       // split slot of this CTA's 128 rows (a CTA pair's tile has two)
       const int sti = PAIR ? un.st * 2 + static_cast<int>(rank) : un.st;
@@ -643,7 +701,7 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
         split_tile = p.split_ws + static_cast<long long>(sti) * p.split * BN * 128;
         float* mine = split_tile + static_cast<long long>(un.part) * BN * 128 + quarter * 32 + lane;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = hcol / 32; c < (hcol + kHalfCols) / 32; ++c) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(tmem_base + lane_off + acc * BN + c * 32, r);
           tc_wait_ld_regs(r);
@@ -653,7 +711,7 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
         __threadfence();
         __syncwarp();
         int last = 0;
-        if (lane == 0) last = atomicAdd(p.split_cnt + sti * 4 + quarter, 1) == p.split - 1;
+        if (lane == 0) last = atomicAdd(p.split_cnt + sti * 8 + quarter * 2 + half, 1) == p.split - 1;
         last = __shfl_sync(0xffffffffu, last, 0);
         if (!last) {
           tc_fence_before();
@@ -670,21 +728,24 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
           continue;
         }
         __threadfence();
-        if (lane == 0) p.split_cnt[sti * 4 + quarter] = 0;
+        if (lane == 0) p.split_cnt[sti * 8 + quarter * 2 + half] = 0;
       }
       float st_cnt = 0.f, st_mean = 0.f, st_m2 = 0.f;
       float shift = 0.f;  // LayerNorm: the tile is stored centred on its first chunk's mean
       if constexpr (SWAP) {
         // TMEM lane = output channel f, column = output pixel.  Each 32-pixel chunk is
         // transposed through shared memory ([pixel][32 channels], unswizzled) and stored
-        // as a 32 x 32 block of the NHWC output.  The warp's 8 KB of staging holds
-        // kSwapBufs such blocks, so that many TMA stores stay in flight.
+        // as a 32 x 32 block of the NHWC output.  The warp's 4 KB of staging holds
+        // kSwapBufs such blocks, so that many TMA stores stay in flight.  The warp takes
+        // the chunks of its column half (pixels hcol .. hcol + BN/2 of the tile).
         const int f = tm * kBM + quarter * 32 + lane;
         const int f0 = tm * kBM + quarter * 32;
         const float2 aff = channel_affine(p, f);
         constexpr int kRowB = 32 * kOutBytes;
         constexpr int kSwapBox = 32 * kRowB;
-        constexpr int kSwapBufs = 2 * kEpiBufBytes / kSwapBox;
+        constexpr int kSwapBufs = kEpiBufBytes / kSwapBox;
+        constexpr int kC0 = 0, kCn = kHalfCols / 32;  // chunks of a half
+        const int cfirst = hcol / 32;
         // Residual of the BN-add-ReLU epilogue.  Whole 32-channel groups: each lane loads
         // one pixel's 32 channels (4 x 16 B) one chunk ahead, and the chunk is transposed
         // through the staging block it will be stored from.  A partial channel group
@@ -706,17 +767,18 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
             for (int j = 0; j < 4; ++j) qn[j] = make_uint4(0u, 0u, 0u, 0u);
           }
         };
-        if (vec_add) load_res(0);
+        if (vec_add) load_res(cfirst);
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int ci = kC0; ci < kCn; ++ci) {
+          const int c = cfirst + ci;
           uint4 q[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) q[j] = qn[j];
-          if (vec_add && c + 1 < BN / 32) load_res(c + 1);
+          if (vec_add && ci + 1 < kCn) load_res(c + 1);
           uint32_t r[32];
           tmem_ld_32x32b_x32(tmem_base + lane_off + acc * BN + c * 32, r);
           tc_wait_ld_regs(r);
-          if (c == BN / 32 - 1) {
+          if (ci == kCn - 1) {
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar_tempty + 8 * acc);
@@ -795,7 +857,7 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
       const int row0 = tm * kTileM + static_cast<int>(rank) * kBM + quarter * 32;
       const int col0 = tn * BN;
 #pragma unroll 1
-      for (int c = 0; c < kChunks; ++c) {
+      for (int c = half * kHalfChunks; c < (half + 1) * kHalfChunks; ++c) {
         const int cbase = col0 + c * kCPC;
         float v[kCPC];
         {
@@ -820,7 +882,7 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
             for (int i = 0; i < kCPC; ++i) v[i] += __ldcg(other + (c * kCPC + i) * 128);
           }
         }
-        if (c == kChunks - 1) {
+        if (c == (half + 1) * kHalfChunks - 1) {
           // The accumulator buffer is free once every lane's loads of it have completed.
           tc_fence_before();
           __syncwarp();
@@ -890,7 +952,7 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
               q += (i < cv) ? d * d : 0.f;
             }
             chan_merge(st_cnt, st_mean, st_m2, static_cast<float>(cv), cm, q);
-            if (c == 0) shift = cm;
+            if (c == half * kHalfChunks) shift = cm;
           }
           // Store x - shift: the bf16/fp16 rounding then scales with the row's spread,
           // not with its mean; the normaliser adds (shift - row mean) back in fp32.
@@ -898,9 +960,9 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
           for (int i = 0; i < kCPC; ++i) v[i] -= shift;
         }
         // Stage the 32 x 128 B block in swizzled shared memory, then TMA-store it.
-        const uint32_t buf = buf0 + (nstore & 1) * kEpiBufBytes;
-        if (nstore >= 2) {
-          if (lane == 0) bulk_wait_read<1>();
+        const uint32_t buf = buf0;
+        if (nstore >= 1) {
+          if (lane == 0) bulk_wait_read<0>();
           __syncwarp();
         }
         const uint32_t rowp = buf + lane * 128;
@@ -937,7 +999,9 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
         // Per-tile row statistics; the row pass (launched next on the same stream)
         // merges them and normalises every row in place.
         const int row = row0 + lane;
-        if (row < p.M) p.ln_stats[static_cast<long long>(tn) * p.M + row] = make_float4(st_mean, st_m2, shift, 0.f);
+        // slice = this warp's column half of the tile (the row pass merges the slices)
+        if (row < p.M)
+          p.ln_stats[static_cast<long long>(tn * kHalves + half) * p.M + row] = make_float4(st_mean, st_m2, shift, 0.f);
       }
     }
     if (!ok) {
@@ -962,22 +1026,6 @@ __global__ void __launch_bounds__(CONV ? 288 : 192, 1)
 }
 
 // Eight consecutive elements of a parameter vector (16-byte aligned start) as floats.
-__device__ __forceinline__ void load_vec8(const void* ptr, int dt, int i, float (&f)[8]) {
-  if (dt == DT_F32) {
-    const float4 a = __ldg(reinterpret_cast<const float4*>(ptr) + i / 4);
-    const float4 b = __ldg(reinterpret_cast<const float4*>(ptr) + i / 4 + 1);
-    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
-    return;
-  }
-  const uint4 u = __ldg(reinterpret_cast<const uint4*>(ptr) + i / 8);
-  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const float2 v = dt == DT_BF16 ? unpack2<DT_BF16>(w[e]) : unpack2<DT_F16>(w[e]);
-    f[2 * e] = v.x;
-    f[2 * e + 1] = v.y;
-  }
-}
 
 // Second pass of the fused LayerNorm: one warp per output row.  The lanes merge the
 // row's tiles_n slice statistics (Chan et al.) into mean / rstd with a butterfly of

@@ -32,7 +32,7 @@ cudaError_t launch_tc(const LaunchArgs& a) {
     if (e != cudaSuccess) return e;
     opted.fetch_or(bit, std::memory_order_acq_rel);
   }
-  constexpr int kThreads = CONV ? 288 : 192;
+  constexpr int kThreads = CONV ? 416 : 320;  // producer(s) + MMA + 8 epilogue warps
   if constexpr (PAIR) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.grid, 1, 1);

@@ -13,7 +13,8 @@
 //
 // Limits and rules:
 //   * the scratch holds FO_NOALLOC_LN_SCRATCH_BYTES (8 MiB); a problem whose statistics
-//     need more (fo_gemm_workspace_size > 8 MiB, e.g. M * ceil(N / block_n) > ~520k) is
+//     need more (fo_gemm_workspace_size > 8 MiB, e.g. M * ceil(N / block_n) > ~260k for
+//     block_n >= 128, whose statistics come in half-tile slices) is
 //     rejected with FO_EINVAL and a message naming both sizes;
 //   * every GPU that loads this library holds the 8 MiB array until the process exits;
 //   * every call shares the one array per device and it keeps the last call's contents;

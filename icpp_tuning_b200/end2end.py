@@ -86,12 +86,39 @@ class FusedBert:
         return h.reshape(b, s, hidden)
 
 
+def torch_sdpa_bert(w: Dict[str, List[torch.Tensor]], head_num: int):
+    """FusedBert's graph with PyTorch at the three fusion sites (matmul + bias + residual
+    + layer_norm, addmm + gelu): isolates what the fused operators gain from what the
+    attention (SDPA in both) gains over the reference's unfused softmax(QK^T)V."""
+    hidden = w["attr_output_kernel"][0].shape[0]
+
+    def run(x):
+        b, s, _ = x.shape
+        h = x.reshape(b * s, hidden)
+        for layer in range(len(w["qkv"])):
+            inp = h
+            qkv = w["qkv"][layer] + w["qkv_bias"][layer]
+            q, k, v = (t.reshape(b, s, head_num, HEAD_SIZE).transpose(1, 2) for t in qkv.chunk(3, dim=-1))
+            ctx = F.scaled_dot_product_attention(q, k, v, is_causal=True).transpose(1, 2).reshape(b * s, hidden)
+            h = torch.addmm(w["attr_output_bias"][layer], ctx, w["attr_output_kernel"][layer])
+            h = F.layer_norm(h + inp, (hidden,), w["attr_ln_gamma"][layer], w["attr_ln_beta"][layer])
+            res = h
+            u = F.gelu(torch.addmm(w["inter_bias"][layer], h, w["inter_kernel"][layer]))
+            h = torch.addmm(w["output_bias"][layer], u, w["output_kernel"][layer])
+            h = F.layer_norm(h + res, (hidden,), w["out_ln_gamma"][layer], w["out_ln_beta"][layer])
+        return h.reshape(b, s, hidden)
+
+    return run
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description="BERT forward with B200 fused operators")
     ap.add_argument("--model", default="bert_base", choices=sorted(MODELS))
     ap.add_argument("--batch_size", type=int, default=1)
     ap.add_argument("--seq_len", type=int, default=128)
-    ap.add_argument("--method", default="B200Fused", choices=["B200Fused", "TorchNative"])
+    ap.add_argument("--method", default="B200Fused", choices=["B200Fused", "TorchNative", "TorchSDPA"],
+                    help="TorchNative: the reference's PyTorch formulation; TorchSDPA: this module's graph "
+                         "with PyTorch ops at the fusion sites")
     args = ap.parse_args()
     heads, layers = MODELS[args.model]
     hidden = heads * HEAD_SIZE
@@ -100,6 +127,8 @@ def main() -> None:
     x = (torch.rand(args.batch_size, args.seq_len, hidden) * 0.8 - 0.4).half().cuda()
     if args.method == "B200Fused":
         runner, label = FusedBert(w, heads, args.batch_size * args.seq_len), "B200 Fused"
+    elif args.method == "TorchSDPA":
+        runner, label = torch_sdpa_bert(w, heads), "Torch SDPA"
     else:
         from oracle.end2end_ref import bert_forward  # the reference's PyTorch formulation
 

@@ -46,6 +46,34 @@ def test_gemm_bias_act(act, odt):
     status_clean()
 
 
+@pytest.mark.parametrize("act", ["gelu_erf", "gelu_tanh"])
+def test_gelu_fp32_accuracy(act):
+    """GELU epilogues into fp32 against the fp32-upcast oracle over pre-activations of
+    about +-10 (the erf is Abramowitz & Stegun 7.1.26, |error| ~5e-7 in fp32; tanh uses
+    tanh.approx)."""
+    g = gen(60)
+    M, Nn, K = 300, 520, 256
+    a, b = randn(g, M, K, scale=0.6), randn(g, K, Nn, scale=K ** -0.5 * 5)
+    bias = randn(g, Nn, scale=1.0)
+    out = fused.gemm(*cuda(a, b), epilogue=f"bias_{act}", bias=bias.cuda(), out_dtype=torch.float32,
+                     config=N.tile_cfg(256, 4, 0))
+    ref = R.gemm_bias_act(a, b, bias, act, upcast=True)
+    assert ref.abs().max() > 5
+    tol = dict(atol=2e-5, rtol=2e-5) if act == "gelu_erf" else dict(atol=2e-3, rtol=2e-3)
+    assert_close(out, ref, tol)
+
+
+def test_misaligned_bias_vector():
+    """A bias view that is not 16-byte aligned takes the per-lane load path."""
+    g = gen(61)
+    M, Nn, K = 200, 512, 128
+    a, b = randn(g, M, K), randn(g, K, Nn, scale=K ** -0.5)
+    store = randn(g, Nn + 1, scale=0.5).cuda()
+    bias = store[1:]  # 2-byte offset
+    out = fused.gemm(*cuda(a, b), epilogue="bias_relu", bias=bias, out_dtype=torch.float32, config=N.tile_cfg(128, 6, 0))
+    assert_close(out, R.gemm_bias_act(a, b, bias.cpu(), "relu"), TOL)
+
+
 @pytest.mark.parametrize("M", [1, 2, 127, 128, 129])
 def test_small_m(M):
     a, b, bias = _inputs(3, M, 2304, 768, torch.float16, "kn")

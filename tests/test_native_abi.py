@@ -74,8 +74,9 @@ def test_gemm_layernorm_needs_workspace():
     d = _desc(epilogue=N.FO_EPI_BIAS_LN, bias=1 << 20, gamma=1 << 20, beta=1 << 20)
     assert _call(d) == N.FO_EINVAL and "workspace" in N.last_error()
     need = N.lib().fo_gemm_workspace_size(ctypes.byref(d), ctypes.byref(N.tile_cfg(256, 4, 0)))
-    # counters for 2 row blocks padded to 256 B + (mean, M2, shift, pad) per row per N tile
-    assert need == 256 + 256 * 1 * 16
+    # counters for 2 row blocks padded to 256 B + (mean, M2, shift, pad) per row per slice
+    # (a slice is half of a 256-column N tile: one epilogue warp's columns)
+    assert need == 256 + 256 * 2 * 16
 
 
 def test_gemm_bad_config():
@@ -150,12 +151,12 @@ def test_split_k_field():
     never = N.lib().fo_gemm_workspace_size(ctypes.byref(d), ctypes.byref(N.tile_cfg(256, 4, 8, split_k=1)))
     four = N.lib().fo_gemm_workspace_size(ctypes.byref(d), ctypes.byref(N.tile_cfg(256, 4, 8, split_k=4)))
     # 32 tiles < 148 SMs, 64 k-blocks: at most 4 parts fit the idle SMs; the cost model
-    # (k-blocks per part vs reading 128 KB partials at ~30 GB/s) picks 3; 4 counters per
-    # tile (512 B), then one fp32 partial tile per part
+    # (k-blocks per part vs reading 128 KB partials at ~30 GB/s) picks 3; 8 counters per
+    # tile (one per epilogue warp: 1 KB), then one fp32 partial tile per part
     assert never == 0
-    assert auto == 512 + 32 * 3 * 128 * 256 * 4 and four == 512 + 32 * 4 * 128 * 256 * 4
+    assert auto == 1024 + 32 * 3 * 128 * 256 * 4 and four == 1024 + 32 * 4 * 128 * 256 * 4
     pair = N.lib().fo_gemm_workspace_size(ctypes.byref(d), ctypes.byref(N.tile_cfg(256, 6, 8, block_m=256)))
-    assert pair == 512 + 16 * 2 * 3 * 128 * 256 * 4  # 16 pair tiles, 2 halves (slots) each, 3 parts
+    assert pair == 1024 + 16 * 2 * 3 * 128 * 256 * 4  # 16 pair tiles, 2 slots each, 3 parts
 
 
 def test_timeout_setting():
