@@ -27,6 +27,7 @@ SOURCES = [
     ("fo_family_gemm.cu", "fo_family_gemm_pair", ["-DFO_PAIR=1"]),
     ("fo_family_ln.cu", "fo_family_ln", []),
     ("fo_family_conv.cu", "fo_family_conv", []),
+    ("fo_family_direct.cu", "fo_family_direct", []),
     ("fo_noalloc.cu", "fo_noalloc", []),
 ]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -15,6 +15,7 @@
 
 #include "../../include/b200fo.h"
 #include "fo_launch.cuh"
+#include "fo_direct.cuh"
 
 namespace {
 
@@ -186,13 +187,16 @@ int check_cfg(int op, int out_dtype, const FoTileCfg* cfg, char* why, size_t why
   if (cfg->stages < min_stages || cfg->stages > fo::kMaxStages)
     return say("stages out of range: %d", cfg->stages);
   if (cfg->group_m < 0) return say("group_m must be >= 0, got %d", cfg->group_m);
-  if (cfg->swap_ab != 0 && cfg->swap_ab != 1) return say("swap_ab must be 0 or 1, got %d", cfg->swap_ab);
+  if (cfg->swap_ab < 0 || cfg->swap_ab > 2) return say("swap_ab must be 0, 1 or 2 (direct conv), got %d", cfg->swap_ab);
   if (cfg->swap_ab && (op != 1 || cfg->block_m != 128 || cfg->block_n < 128))
     return say("swap_ab is a conv2d mode with block_m 128 and block_n >= 128 (block_n %d)", cfg->block_n);
+  if (cfg->swap_ab == 2 && cfg->block_n != 256)
+    return say("the direct conv (swap_ab 2) computes 256-position tiles: block_n must be 256, got %d", cfg->block_n);
   if (cfg->max_ctas < 0) return say("max_ctas must be >= 0, got %d", cfg->max_ctas);
   if (cfg->split_k < 0 || cfg->split_k > 16) return say("split_k must be 0 (automatic) .. 16, got %d", cfg->split_k);
+  // (the direct conv's shared memory depends on the image width: fo_conv2d checks it)
   const int smem = fo::smem_bytes_for(cfg->block_n, cfg->stages, cfg->block_m == 256);
-  if (smem > 232448) return say("shared memory %d B exceeds the 227 KB per-block limit", smem);
+  if (cfg->swap_ab != 2 && smem > 232448) return say("shared memory %d B exceeds the 227 KB per-block limit", smem);
   // TMEM: two fp32 accumulators of block_n columns each, <= 512 columns.
   if (2 * cfg->block_n > 512) return say("TMEM columns %d exceed 512", 2 * cfg->block_n);
   if (out_dtype < 0 || out_dtype > 2) return say("bad output dtype %d", out_dtype);
@@ -315,6 +319,7 @@ size_t ln_workspace(int64_t M, int64_t N, int bn) {
 void fill_common(fo::KParams& p, const DevInfo& di) {
   p.status = di.status;
   p.timeout_ns = g_timeout_ns.load();
+
 }
 
 }  // namespace
@@ -514,7 +519,7 @@ static bool conv_grid(const FoConvDesc* d, const FoTileCfg* cfg, int* tiles, int
   const int ow = (d->w + 2 * d->pad - d->dil * (d->kw - 1) - 1) / d->stride + 1;
   if (oh <= 0 || ow <= 0) return false;
   const int64_t M = static_cast<int64_t>(d->n) * oh * ow;
-  if (cfg->block_m == 256) return false;  // CTA pairs run whole tiles
+  if (cfg->block_m == 256 || cfg->swap_ab == 2) return false;  // CTA pairs and the direct conv run whole tiles
   const int bn = cfg->block_n;
   if (cfg->swap_ab)
     *tiles = static_cast<int>(((d->f + 127) / 128) * ((M + bn - 1) / bn));
@@ -529,6 +534,50 @@ extern "C" size_t fo_conv2d_workspace_size(const FoConvDesc* d, const FoTileCfg*
   if (!conv_grid(d, cfg, &tiles, &kb)) return 0;
   const int cap = cfg->max_ctas > 0 ? cfg->max_ctas : sm_count_or_default();
   return split_workspace(plan_split(tiles, kb, cap, true, cfg->split_k, cfg->block_n, true), cfg->block_n);
+}
+
+// Geometry of the direct conv (swap_ab 2): pitch P of the padded rows (W + 2 pad rounded
+// up to 32, dividing 256), rows per pixel slot, and how many slots fit beside `stages`
+// weight stages.  Returns false (with the reason) when the shape does not qualify.
+struct DirectPlan {
+  int P, Hp, nR, pslots, smem;
+};
+
+bool plan_direct(const FoConvDesc* d, int stages, DirectPlan* pl, char* why, size_t n) {
+  auto no = [&](const char* msg) {
+    snprintf(why, n, "%s", msg);
+    return false;
+  };
+  if (d->stride != 1 || d->dil != 1) return no("the direct conv needs stride 1 and dilation 1");
+  if (d->c % 64 != 0) return no("the direct conv needs C % 64 == 0");
+  const int wp = d->w + 2 * d->pad;
+  const int P = (wp + 31) / 32 * 32;
+  if (P > 256 || 256 % P != 0) return no("the direct conv needs W + 2 pad <= 256 with its 32-rounded pitch dividing 256");
+  if (d->kw - 1 >= P) return no("filter wider than the padded row");
+  pl->P = P;
+  pl->Hp = d->h + 2 * d->pad;
+  pl->nR = (fo::kDirectBN - 1 + (d->kh - 1) * P + d->kw - 1) / P + 1;
+  const int slot = pl->nR * P * 128;
+  for (int slots = 2; slots >= 1; --slots) {
+    const int smem = fo::direct_smem_bytes(stages, slots, slot);
+    if (smem <= 232448) {
+      pl->pslots = slots;
+      pl->smem = smem;
+      return true;
+    }
+  }
+  return no("the direct conv's input rows and weight stages exceed 227 KB of shared memory; use fewer stages");
+}
+
+int make_tmap_4d(CUtensorMap* m, int dt, const void* base, const cuuint64_t (&dims)[4], const cuuint64_t (&strides)[3],
+                 const cuuint32_t (&box)[4], CUtensorMapSwizzle swizzle, const char* what) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return fail(FO_ECUDA, "cuTensorMapEncodeTiled is unavailable in the driver");
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(m, tma_dt(dt), 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FO_EINVAL, "tensor map for %s rejected by the driver (CUresult %d)", what, static_cast<int>(r));
+  return FO_OK;
 }
 
 int fo_conv2d(const FoConvDesc* d, const FoTileCfg* cfg, void* stream) {
@@ -623,6 +672,48 @@ int fo_conv2d(const FoConvDesc* d, const FoTileCfg* cfg, void* stream) {
   p.pad = d->pad;
   p.dil = d->dil;
   fill_common(p, di);
+  if (cfg->swap_ab == 2) {
+    // direct conv: one 4-D box per padded input row, 4-D output boxes of 32 x 32
+    DirectPlan dp;
+    char why[160];
+    if (!plan_direct(d, cfg->stages, &dp, why, sizeof(why))) return fail(FO_EINVAL, "%s", why);
+    p.P = dp.P;
+    p.Hp = dp.Hp;
+    p.nR = dp.nR;
+    p.pslots = dp.pslots;
+    p.nimg = d->n;
+    p.c_blocks = d->c / 64;
+    const long long positions = static_cast<long long>(d->n) * dp.Hp * dp.P;
+    p.tiles_m = (p.N + 127) / 128;
+    p.tiles_n = static_cast<int>((positions + fo::kDirectBN - 1) / fo::kDirectBN);
+    p.num_tiles = p.tiles_m * p.tiles_n;
+    p.num_units = p.num_tiles;
+    p.dp_units = p.num_tiles;
+    p.split = 1;
+    const cuuint64_t xd[4] = {static_cast<cuuint64_t>(d->c), static_cast<cuuint64_t>(d->w),
+                              static_cast<cuuint64_t>(d->h), static_cast<cuuint64_t>(d->n)};
+    const cuuint64_t xs[3] = {static_cast<cuuint64_t>(d->c) * 2, static_cast<cuuint64_t>(d->w) * d->c * 2,
+                              static_cast<cuuint64_t>(d->h) * d->w * d->c * 2};
+    const cuuint32_t xb[4] = {64, static_cast<cuuint32_t>(dp.P), 1, 1};
+    if (int rc = make_tmap_4d(&la.tmA, d->in_dtype, d->x, xd, xs, xb, CU_TENSOR_MAP_SWIZZLE_128B, "input rows")) return rc;
+    if (int rc = make_tmap(&la.tmB, d->in_dtype, d->wgt, d->f, K64, static_cast<uint64_t>(d->f) * 2, 64, 64, "weights"))
+      return rc;
+    const cuuint64_t yd[4] = {static_cast<cuuint64_t>(d->f), static_cast<cuuint64_t>(ow), static_cast<cuuint64_t>(oh),
+                              static_cast<cuuint64_t>(d->n)};
+    const cuuint64_t ys[3] = {static_cast<cuuint64_t>(d->f) * ob, static_cast<cuuint64_t>(ow) * d->f * ob,
+                              static_cast<cuuint64_t>(oh) * ow * d->f * ob};
+    const cuuint32_t yb[4] = {32, 32, 1, 1};
+    if (int rc = make_tmap_4d(&la.tmC, d->out_dtype, d->out, yd, ys, yb, CU_TENSOR_MAP_SWIZZLE_NONE, "output")) return rc;
+    const int cap = cfg->max_ctas > 0 ? cfg->max_ctas : di.sms;
+    la.grid = p.num_units < cap ? p.num_units : cap;
+    la.smem = dp.smem;
+    la.stream = static_cast<cudaStream_t>(stream);
+    const int out_dt = d->out_dtype == FO_DT_F16 ? fo::DT_F16 : d->out_dtype == FO_DT_BF16 ? fo::DT_BF16 : fo::DT_F32;
+    cudaError_t e = fo::launch_direct_conv(act, out_dt, la);
+    if (e != cudaSuccess) return fail(FO_ECUDA, "kernel launch failed: %s", cudaGetErrorString(e));
+    g_launches.fetch_add(1);
+    return ok();
+  }
   p.conv_tma = (d->stride <= 8 && !conv_gather_forced() && make_im2col_map(&la.tmA, d, swap ? bn : 128)) ? 1 : 0;
   if (!p.conv_tma) pair = swap = false;  // both need the TMA im2col producer
   if (swap) {

@@ -1,0 +1,360 @@
+// fo_direct.cuh -- direct convolution for stride-1 NHWC convs on sm_100a.
+//
+// The im2col kernel (fo_tc_kernel<..., CONV>) loads every input pixel once per filter
+// tap from L2: a 3x3 conv moves 9x its input through each SM's load path, which bounds
+// it well below the tensor rate.  Here each input pixel is loaded into shared memory
+// once per 128-channel output tile and every tap is a shifted view of the same rows:
+//
+//   * The image is viewed with padded rows of P positions (P = W + 2*pad rounded up to
+//     32, P dividing 256) and Hp = H + 2*pad padded rows per image.  Output position
+//     o = (n * Hp + oh) * P + ow; tap (dy, dx) reads input position o + dy * P + dx, a
+//     constant shift.  Positions with ow >= OW or oh >= OH are computed and discarded.
+//   * A tile is BN = 256 consecutive positions (256 / P whole padded rows) x 128 output
+//     channels (operand-swapped: M = channels from the weights, N = positions).  The
+//     producer loads the nR padded rows the tile's taps touch, one 4-D TMA box of
+//     (64 channels, P positions) per row starting at w = -pad (the padding is the
+//     hardware's out-of-range zero fill; every box lands 1024-byte aligned because
+//     P * 128 B is a multiple of 4 KB).
+//   * For each channel block and tap the MMA issuer points the B descriptor at the rows
+//     shifted by dy * P + dx positions (128 B each); the swizzle is anchored on absolute
+//     shared-memory addresses, so any row shift is a plain start-address offset.
+//   * The weights stream through a ring of 128 x 64 stages as in the im2col kernel.
+//   * Eight epilogue warps (two per TMEM lane quarter) take 32-position chunks: with
+//     P % 32 == 0 each chunk is part of one padded row, stored with one 4-D TMA box
+//     (32 channels x 32 columns) whose out-of-range columns the hardware clips.
+// Per 128 x 256 x 64 MMA step an SM now loads 16 KB of weights plus 1/(KH*KW) of the
+// rows instead of 48 KB.  Every wait is bounded as in fo_tc_kernel.
+#pragma once
+#include "fo_kernel.cuh"
+
+namespace fo {
+
+constexpr int kDirectBN = 256;          // positions per tile
+constexpr int kDirectWStage = 128 * 64 * 2;  // 128 channels x 64 K of weights
+
+__host__ __device__ constexpr int direct_smem_bytes(int stages, int pslots, int slot_bytes) {
+  return 1024 + pslots * slot_bytes + stages * kDirectWStage + kEpiBytes + kMiscBytes;
+}
+
+template <int ACT, int OUT_DT>
+__global__ void __launch_bounds__(320, 1)
+    fo_direct_conv_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                          const __grid_constant__ CUtensorMap tmY, const KParams p) {
+  constexpr int BN = kDirectBN;
+  constexpr int kMmaWarp = 1, kFirstEpiWarp = 2;
+  constexpr int kOutBytes = OUT_DT == DT_F32 ? 4 : 2;
+  constexpr uint32_t kTmemCols = 2 * BN;
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const int stages = p.stages;
+  const int slot_bytes = p.nR * p.P * 128;
+  const uint32_t sPix = smem_u32(smem);
+  const uint32_t sW = sPix + p.pslots * slot_bytes;
+  const uint32_t sEpi = sW + stages * kDirectWStage;
+  uint8_t* misc = smem + (sEpi - sPix) + kEpiBytes;
+  // misc: [0,64) full[8] | [64,128) empty[8] | [128,144) pfull[2] | [144,160) pempty[2]
+  //       | [160,176) tfull[2] | [176,192) tempty[2] | [192,200) drain | [248,256) tmem addr + abort
+  const uint32_t mb = smem_u32(misc);
+  const uint32_t bar_full = mb, bar_empty = mb + 64, bar_pfull = mb + 128, bar_pempty = mb + 144;
+  const uint32_t bar_tfull = mb + 160, bar_tempty = mb + 176, bar_drain = mb + 192;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 248);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 252);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cid = blockIdx.x, ncl = gridDim.x;
+  const uint64_t tmo = p.timeout_ns;
+  const int taps = p.KH * p.KW;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_empty + 8 * s, 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(bar_pfull + 8 * a, 1);
+      mbar_init(bar_pempty + 8 * a, 1);
+      mbar_init(bar_tfull + 8 * a, 1);
+      mbar_init(bar_tempty + 8 * a, kEpiWarps);
+    }
+    mbar_init(bar_drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  if (threadIdx.x == 32 * kFirstEpiWarp) {
+    tma_prefetch_desc(&tmX);
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmY);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer
+    if (lane == 0) {
+      int s = 0, ps = 0;
+      uint32_t ph = 0, pph = 0;
+      int issued = 0, pissued = 0;
+      bool ok = true;
+      const uint32_t row_bytes = static_cast<uint32_t>(p.P) * 128;
+      for (int u = cid; u < p.num_units && ok; u += ncl) {
+        const int tm = u % p.tiles_m, tn = u / p.tiles_m;
+        const int r0 = tn * (BN / p.P);  // first padded row of the tile (BN % P == 0)
+        for (int cb = 0; cb < p.c_blocks && ok; ++cb) {
+          if (!mbar_wait(bar_pempty + 8 * ps, pph ^ 1, tmo, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t pb = bar_pfull + 8 * ps;
+          mbar_arrive_expect_tx(pb, static_cast<uint32_t>(p.nR) * row_bytes);
+          for (int r = 0; r < p.nR; ++r) {
+            const int R = r0 + r;
+            const int n = R / p.Hp;
+            const int hp = R - n * p.Hp;
+            tma_load_4d(sPix + ps * slot_bytes + r * row_bytes, &tmX, pb, cb * 64, -p.pad, hp - p.pad, n);
+          }
+          ++pissued;
+          if (++ps == p.pslots) {
+            ps = 0;
+            pph ^= 1;
+          }
+          for (int t = 0; t < taps; ++t) {
+            if (!mbar_wait(bar_empty + 8 * s, ph ^ 1, tmo, abort_flag)) {
+              ok = false;
+              break;
+            }
+            const uint32_t fb = bar_full + 8 * s;
+            mbar_arrive_expect_tx(fb, kDirectWStage);
+#pragma unroll
+            for (int j = 0; j < 2; ++j)  // 128 output channels x 64 K, MN-major
+              tma_load_2d(sW + s * kDirectWStage + j * 64 * 128, &tmW, fb, tm * 128 + j * 64, t * p.C + cb * 64);
+            ++issued;
+            if (++s == stages) {
+              s = 0;
+              ph ^= 1;
+            }
+          }
+        }
+      }
+      if (!ok) {
+        record_error(p, kStatusTimeout, 0x40);
+        *abort_flag = 1;
+      }
+      drain_loads(bar_full, stages, issued);
+      drain_loads(bar_pfull, p.pslots, pissued);
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      // The issuing thread is the bottleneck of this loop (each tcgen05.mma takes ~60 issue
+      // cycles, a commit ~60, against 540 tensor cycles per tap), so every descriptor is
+      // stepped, not recomputed: the weights by one stage (16 KB) per tap, the rows by one
+      // position (128 B) per dx and by P - KW + 1 positions at the end of a filter row.
+      const uint32_t idesc = idesc_f16(p.ab_bf16, 0, BN, 128) | (1u << 15);  // A (weights) MN-major
+      const uint64_t a_desc0 = sdesc_sw128(sW, 64 * 128, 1024);
+      const uint64_t b_desc0 = sdesc_sw128_rows(sPix);
+      const uint32_t slot_units = static_cast<uint32_t>(slot_bytes) >> 4;
+      const uint32_t wrap_units = static_cast<uint32_t>(p.P - p.KW + 1) * 8;
+      int s = 0, ps = 0, acc = 0;
+      uint32_t ph = 0, pph = 0, acc_ph = 0;
+      uint64_t ad = a_desc0;
+      bool ok = true;
+      for (int u = cid; u < p.num_units && ok; u += ncl) {
+        if (!mbar_wait(bar_tempty + 8 * acc, acc_ph ^ 1, tmo, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + acc * BN;
+        uint32_t accum = 0;
+        for (int cb = 0; cb < p.c_blocks && ok; ++cb) {
+          if (!mbar_wait(bar_pfull + 8 * ps, pph, tmo, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          uint64_t bd = b_desc0 + static_cast<uint64_t>(ps * slot_units);
+          int dx = 0;
+          for (int t = 0; t < taps; ++t) {
+            if (!mbar_wait(bar_full + 8 * s, ph, tmo, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            tc_mma_f16(d, ad, bd, idesc, accum);
+            tc_mma_f16(d, ad + (2048 >> 4), bd + (32 >> 4), idesc, 1u);
+            tc_mma_f16(d, ad + 2 * (2048 >> 4), bd + 2 * (32 >> 4), idesc, 1u);
+            tc_mma_f16(d, ad + 3 * (2048 >> 4), bd + 3 * (32 >> 4), idesc, 1u);
+            accum = 1u;
+            tc_commit(bar_empty + 8 * s);
+            if (++s == stages) {
+              s = 0;
+              ph ^= 1;
+              ad = a_desc0;
+            } else {
+              ad += kDirectWStage >> 4;
+            }
+            if (++dx == p.KW) {
+              dx = 0;
+              bd += wrap_units;
+            } else {
+              bd += 8;
+            }
+          }
+          tc_commit(bar_pempty + 8 * ps);
+          if (++ps == p.pslots) {
+            ps = 0;
+            pph ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit(bar_tfull + 8 * acc);
+        acc ^= 1;
+        if (acc == 0) acc_ph ^= 1;
+      }
+      if (!ok) {
+        record_error(p, kStatusTimeout, 0x41);
+        *abort_flag = 1;
+      }
+      tc_commit(bar_drain);
+      mbar_wait(bar_drain, 0, kDrainTimeoutNs, nullptr);
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    const int ew = warp - kFirstEpiWarp;  // 0..7
+    const int quarter = warp & 3;         // TMEM lane quarter = 32 output channels
+    const int half = ew >> 2;             // 128-position half of the tile
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t buf0 = sEpi + ew * kEpiBufBytes;
+    constexpr int kRowB = 32 * kOutBytes;  // one staged pixel: 32 channels
+    constexpr int kBox = 32 * kRowB;
+    constexpr int kBufs = kEpiBufBytes / kBox;
+    int acc = 0;
+    uint32_t acc_ph = 0, nstore = 0;
+    bool ok = true;
+    for (int u = cid; u < p.num_units; u += ncl) {
+      const int tm = u % p.tiles_m, tn = u / p.tiles_m;
+      if (!mbar_wait(bar_tfull + 8 * acc, acc_ph, tmo, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int f0 = tm * 128 + quarter * 32;
+      const int f = f0 + lane;
+      const float2 aff = channel_affine(p, f);
+      const bool has_add = OUT_DT != DT_F32 && p.add_src != nullptr && f0 < p.N;
+#pragma unroll 1
+      for (int ci = 0; ci < 4; ++ci) {
+        const int c = half * 4 + ci;
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + lane_off + acc * BN + c * 32, r);
+        tc_wait_ld_regs(r);
+        if (ci == 3) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar_tempty + 8 * acc);
+        }
+        const int pos0 = tn * BN + c * 32;  // 32 positions inside one padded row
+        const int R = pos0 / p.P;
+        const int n = R / p.Hp;
+        const int oh = R - n * p.Hp;
+        const int ow0 = pos0 - R * p.P;
+        if (n >= p.nimg || oh >= p.OH || ow0 >= p.OW || f0 >= p.N) continue;  // padding positions
+        float acc_v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc_v[i] = __uint_as_float(r[i]);
+        if (p.bn_mode) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc_v[i] = fmaf(round_in(acc_v[i], p.ab_bf16), aff.x, aff.y);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc_v[i] = fmaf(acc_v[i], aff.x, aff.y);
+        }
+        const uint32_t buf = buf0 + (nstore % kBufs) * kBox;
+        if (nstore >= kBufs) {
+          if (lane == 0) bulk_wait_read<kBufs - 1>();
+          __syncwarp();
+        }
+        if constexpr (OUT_DT != DT_F32) {
+          if (has_add) {
+            // residual: lane = pixel ow0 + lane, 32 channels (4 x 16 B); transposed
+            // through the staging block it will be stored from
+            const int ow = ow0 + lane;
+            uint4 q[4] = {};
+            if (ow < p.OW && f0 + 32 <= p.N) {
+              const uint4* src = reinterpret_cast<const uint4*>(
+                  reinterpret_cast<const unsigned short*>(p.add_src) +
+                  ((static_cast<long long>(n) * p.OH + oh) * p.OW + ow) * p.ld_add + f0);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) q[j] = __ldg(src + j);
+            } else if (ow < p.OW) {  // partial channel group
+              const unsigned short* src = reinterpret_cast<const unsigned short*>(p.add_src) +
+                                          ((static_cast<long long>(n) * p.OH + oh) * p.OW + ow) * p.ld_add + f0;
+              unsigned short tmp[32];
+#pragma unroll
+              for (int e = 0; e < 32; ++e) tmp[e] = f0 + e < p.N ? src[e] : static_cast<unsigned short>(0);
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                q[j] = make_uint4(tmp[8 * j] | (tmp[8 * j + 1] << 16), tmp[8 * j + 2] | (tmp[8 * j + 3] << 16),
+                                  tmp[8 * j + 4] | (tmp[8 * j + 5] << 16), tmp[8 * j + 6] | (tmp[8 * j + 7] << 16));
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(buf + lane * kRowB + j * 16), "r"(q[j].x),
+                           "r"(q[j].y), "r"(q[j].z), "r"(q[j].w)
+                           : "memory");
+            __syncwarp();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              unsigned short h;
+              asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(buf + i * kRowB + lane * 2) : "memory");
+              acc_v[i] += unpack2<OUT_DT>(static_cast<uint32_t>(h)).x;
+            }
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float val = apply_act<ACT>(acc_v[i]);
+          const uint32_t addr = buf + i * kRowB + lane * kOutBytes;
+          if constexpr (OUT_DT == DT_F32) {
+            asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(__float_as_uint(val)) : "memory");
+          } else {
+            const unsigned short h = static_cast<unsigned short>(pack2<OUT_DT>(val, 0.f) & 0xFFFFu);
+            asm volatile("st.shared.b16 [%0], %1;" ::"r"(addr), "h"(h) : "memory");
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_4d(&tmY, buf, f0, ow0, oh, n);
+          bulk_commit();
+        }
+        ++nstore;
+      }
+      acc ^= 1;
+      if (acc == 0) acc_ph ^= 1;
+    }
+    if (!ok) {
+      record_error(p, kStatusTimeout, 0x42);
+      *abort_flag = 1;
+    }
+    if (lane == 0) bulk_wait<0>();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace fo

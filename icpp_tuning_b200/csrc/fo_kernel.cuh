@@ -72,6 +72,9 @@ struct KParams {
   const void* x;
   int H, W, C, OH, OW, KH, KW, stride, pad, dil, c_blocks;
   int conv_tma;  // 1: A tiles by TMA im2col loads (tmA); 0: cp.async gather
+  // direct conv (fo_direct_conv_kernel): input rows padded to pitch P positions, Hp padded
+  // rows per image, nR rows per pixel slot, pslots slots, nimg images
+  int P, Hp, nR, pslots, nimg;
   // work units: units [0, dp_units) are whole tiles; the remaining tiles are split along K
   // into `split` parts of kb_per_part k-blocks, reduced through split_ws / split_cnt.
   int num_units, dp_units, split, kb_per_part;
@@ -583,8 +586,14 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
       const uint32_t a_kstep = SWAP ? (2048 >> 4) : (32 >> 4);
       const uint64_t b_desc0 = b_mn ? sdesc_sw128(sB, 64 * 128, 1024) : sdesc_sw128(sB, 16, 1024);
       const uint32_t b_kstep = b_mn ? (2048 >> 4) : (32 >> 4);
+      // One thread issues every MMA (~60 cycles each) and commit; the descriptors are
+      // stepped per stage, not recomputed, and a pair's remote barrier addresses are
+      // translated once, so the issue loop stays shorter than the MMAs it feeds.
+      const uint32_t empty_r0 = PAIR ? mapa_shared(bar_empty, 0) : 0u;
+      const uint32_t empty_r1 = PAIR ? mapa_shared(bar_empty, 1) : 0u;
       int s = 0;
       uint32_t ph = 0;
+      uint64_t ad = a_desc0, bd = b_desc0;
       int acc = 0;
       uint32_t acc_ph = 0;
       bool ok = true;
@@ -598,36 +607,36 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
         }
         tc_fence_after();
         const uint32_t d = tmem_base + acc * BN;
+        uint32_t accum = 0;
         for (int kb = un.kb0; kb < un.kb1; ++kb) {
           if (!mbar_wait(bar_full + 8 * s, ph, tmo, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          // Descriptors of this stage; the K step is an add on the start-address field
-          // (+32 B for K-major rows, +2048 B = 16 rows for MN-major B).
-          const uint64_t ad0 = a_desc0 + static_cast<uint64_t>((s * kAStageBytes) >> 4);
-          const uint64_t bd0 = b_desc0 + static_cast<uint64_t>((s * kBStage) >> 4);
-#pragma unroll
-          for (int k = 0; k < kBK / 16; ++k) {
-            const uint64_t ad = ad0 + static_cast<uint64_t>(k * a_kstep);
-            const uint64_t bd = bd0 + static_cast<uint64_t>(k * b_kstep);
-            const uint32_t accum = (kb != un.kb0 || k != 0) ? 1u : 0u;
-            if constexpr (PAIR) {
-              tc_mma_f16_pair(d, ad, bd, idesc, accum);
-            } else {
-              tc_mma_f16(d, ad, bd, idesc, accum);
-            }
-          }
-          if constexpr (PAIR) {  // free the stage in both CTAs
-            tc_commit_pair(mapa_shared(bar_empty + 8 * s, 0));
-            tc_commit_pair(mapa_shared(bar_empty + 8 * s, 1));
+          if constexpr (PAIR) {
+            tc_mma_f16_pair(d, ad, bd, idesc, accum);
+            tc_mma_f16_pair(d, ad + a_kstep, bd + b_kstep, idesc, 1u);
+            tc_mma_f16_pair(d, ad + 2 * a_kstep, bd + 2 * b_kstep, idesc, 1u);
+            tc_mma_f16_pair(d, ad + 3 * a_kstep, bd + 3 * b_kstep, idesc, 1u);
+            tc_commit_pair(empty_r0 + 8 * s);  // free the stage in both CTAs
+            tc_commit_pair(empty_r1 + 8 * s);
           } else {
+            tc_mma_f16(d, ad, bd, idesc, accum);
+            tc_mma_f16(d, ad + a_kstep, bd + b_kstep, idesc, 1u);
+            tc_mma_f16(d, ad + 2 * a_kstep, bd + 2 * b_kstep, idesc, 1u);
+            tc_mma_f16(d, ad + 3 * a_kstep, bd + 3 * b_kstep, idesc, 1u);
             tc_commit(bar_empty + 8 * s);
           }
+          accum = 1u;
           if (++s == stages) {
             s = 0;
             ph ^= 1;
+            ad = a_desc0;
+            bd = b_desc0;
+          } else {
+            ad += kAStageBytes >> 4;
+            bd += kBStage >> 4;
           }
         }
         if (!ok) break;
@@ -788,7 +797,6 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
             if (lane == 0) bulk_wait_read<kSwapBufs - 1>();
             __syncwarp();
           }
-#pragma unroll
           float acc_v[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) acc_v[i] = has_k ? __uint_as_float(r[i]) : 0.f;

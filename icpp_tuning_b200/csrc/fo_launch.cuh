@@ -73,6 +73,8 @@ cudaError_t launch_gemm_family_pair(int bn, int act, int out_dt, const LaunchArg
 cudaError_t launch_ln_family(int bn, int out_dt, const LaunchArgs& a);
 cudaError_t launch_residual_ln(int bn, int out_dt, const LaunchArgs& a);
 cudaError_t launch_conv_family(int bn, int act, int out_dt, const LaunchArgs& a);
+// Direct (padded-pitch) conv: tmA = input rows (4-D), tmB = weights, tmC = output (4-D).
+cudaError_t launch_direct_conv(int act, int out_dt, const LaunchArgs& a);
 
 // Sets the message fo_last_error returns on the calling thread (defined in fo_api.cu).
 void set_last_error(int code, const char* msg);

@@ -145,6 +145,22 @@ __device__ __forceinline__ void tma_load_im2col_4d_pair(uint32_t dst, const CUte
       "l"(m), "r"(bar), "r"(c), "r"(w), "r"(h), "r"(n), "h"(off_w), "h"(off_h)
       : "memory");
 }
+// 4-D tiled load (x = innermost coordinate); out-of-range elements read as zero.
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* m, uint32_t bar, int32_t x, int32_t y,
+                                            int32_t z, int32_t w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+      "l"(m), "r"(bar), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
+// 4-D tiled store; elements outside the tensor are not written.  Coordinates >= 0.
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* m, uint32_t src, int32_t x, int32_t y, int32_t z,
+                                             int32_t w) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(m),
+               "r"(src), "r"(x), "r"(y), "r"(z), "r"(w)
+               : "memory");
+}
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, uint32_t src, int32_t x,
                                              int32_t y) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(m),
@@ -293,6 +309,14 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo, ui
   d |= static_cast<uint64_t>(2) << 61;
   return d;
 }
+
+// K-major 128B-swizzled operand that starts at any 128-byte row of a swizzled buffer
+// (a view shifted by whole rows, not necessarily on a 1024-byte pattern boundary).  The
+// tensor core applies the 128B swizzle to absolute shared-memory address bits, as TMA
+// does when it writes the buffer, so the shifted start address alone is right and the
+// matrix base-offset field stays 0 (measured on B200: setting it to the row phase, or to
+// its complement, breaks every view whose shift is not a multiple of 8 rows).
+__device__ __forceinline__ uint64_t sdesc_sw128_rows(uint32_t saddr) { return sdesc_sw128(saddr, 16, 1024); }
 
 // Instruction descriptor for kind::f16 with fp32 accumulate, M = 128 (or 256 for pairs).
 //   [4,6) D format (1 = f32), [7,10) A format, [10,13) B format (0 = f16, 1 = bf16),
