@@ -587,10 +587,8 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
       const uint64_t b_desc0 = b_mn ? sdesc_sw128(sB, 64 * 128, 1024) : sdesc_sw128(sB, 16, 1024);
       const uint32_t b_kstep = b_mn ? (2048 >> 4) : (32 >> 4);
       // One thread issues every MMA (~60 cycles each) and commit; the descriptors are
-      // stepped per stage, not recomputed, and a pair's remote barrier addresses are
-      // translated once, so the issue loop stays shorter than the MMAs it feeds.
-      const uint32_t empty_r0 = PAIR ? mapa_shared(bar_empty, 0) : 0u;
-      const uint32_t empty_r1 = PAIR ? mapa_shared(bar_empty, 1) : 0u;
+      // stepped per stage, not recomputed, and a pair frees a stage in both CTAs with one
+      // commit, so the issue loop stays shorter than the MMAs it feeds.
       int s = 0;
       uint32_t ph = 0;
       uint64_t ad = a_desc0, bd = b_desc0;
@@ -619,8 +617,7 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
             tc_mma_f16_pair(d, ad + a_kstep, bd + b_kstep, idesc, 1u);
             tc_mma_f16_pair(d, ad + 2 * a_kstep, bd + 2 * b_kstep, idesc, 1u);
             tc_mma_f16_pair(d, ad + 3 * a_kstep, bd + 3 * b_kstep, idesc, 1u);
-            tc_commit_pair(empty_r0 + 8 * s);  // free the stage in both CTAs
-            tc_commit_pair(empty_r1 + 8 * s);
+            tc_commit_pair_both(bar_empty + 8 * s);  // free the stage in both CTAs
           } else {
             tc_mma_f16(d, ad, bd, idesc, accum);
             tc_mma_f16(d, ad + a_kstep, bd + b_kstep, idesc, 1u);
@@ -641,8 +638,7 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
         }
         if (!ok) break;
         if constexpr (PAIR) {  // both halves of the accumulator are ready
-          tc_commit_pair(mapa_shared(bar_tfull + 8 * acc, 0));
-          tc_commit_pair(mapa_shared(bar_tfull + 8 * acc, 1));
+          tc_commit_pair_both(bar_tfull + 8 * acc);
         } else {
           tc_commit(bar_tfull + 8 * acc);
         }

@@ -269,6 +269,14 @@ __device__ __forceinline__ void tc_commit_pair(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
                : "memory");
 }
+// One commit that arrives on the barrier at shared offset `bar` in both CTAs of the pair
+// (CTA mask 0b11): the completion signal, not a memory load, is multicast.
+__device__ __forceinline__ void tc_commit_pair_both(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+                   bar),
+               "h"(static_cast<uint16_t>(3))
+               : "memory");
+}
 
 // Arrives once on `bar` when every tcgen05.mma this thread issued before it has completed.
 __device__ __forceinline__ void tc_commit(uint32_t bar) {
