@@ -251,8 +251,9 @@ def run_ours(args):
         "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded randn, BASELINE configs[1] shapes)",
         "config": {"workload": WORKLOAD, "parallelism": f"M-shard x{ws} (weak: 4096 rows per GPU)",
-                   "tile": "BM%d_BN%d_BK64_S%d_G%d" % (kern.config["block_M"], kern.config["block_N"],
-                                                        kern.config["num_stages"], kern.config.get("group_m", 0)),
+                   "tile": "BM%d_BN%d_BK%d_S%d_G%d" % (kern.config["block_M"], kern.config["block_N"],
+                                                        kern.config.get("block_K", 64), kern.config["num_stages"],
+                                                        kern.config.get("group_m", 0)),
                    "l2": "flushed between timed steps (256 MiB write outside the events)"},
         "e2e": e2e,
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": UNIT,

@@ -37,6 +37,10 @@ CONSTANTS = {
     "mma_rate_bn": {256: 1.0, 128: 0.66, 64: 0.37},
     # CTA pairs (block_M 256): each SM loads half of B (4096^3: BN=128 pairs 837, BN=256 pairs 1274)
     "mma_rate_bn_pair": {256: 1.03, 128: 0.66},  # measured: pairs do not lift narrow tiles
+    "mma_rate_bn_bk128": {256: 0.85, 128: 0.71, 64: 0.39},  # two K slices per stage (4096^3 sweeps)
+    # pairs, two K slices per stage: 4096^3 107 vs 127 us and 8192^3 692 vs 860 us against
+    # block_K 64 on one box (box-to-box: 0-20% faster, never slower beyond noise)
+    "mma_rate_bn_pair_bk128": {256: 1.08, 128: 0.7},
     "hbm_efficiency": 0.8,  # achievable fraction of the HBM figure in the GPU spec
     "mem_overlap": 0.35,  # share of the shorter of (compute, HBM) time that does not overlap
     # stages - 1 loads in flight must cover this latency (4096^3: 3 stages run at 0.9 of 4)
@@ -160,7 +164,14 @@ def _model(op: OpSpec, c: TuneConfig, hw: GPUSpec) -> dict:
     rate = _sm_rate(hw) * (2 if pair else 1)
 
     # -- mainloop: padded MMA work of one tile at the BN-dependent tensor rate
-    e_bn = (K["mma_rate_bn_pair"] if pair else K["mma_rate_bn"]).get(bn, 0.6)
+    if pair:
+        e_bn = (K["mma_rate_bn_pair_bk128"] if bk == 128 else K["mma_rate_bn_pair"]).get(bn, 0.6)
+    else:
+        e_bn = (K["mma_rate_bn_bk128"] if bk == 128 else K["mma_rate_bn"]).get(bn, 0.6)
+    if bk == 128 and waves < 2:
+        # a single wave is latency-bound, and two K slices per stage halve the stages in
+        # flight: measured 15.4 vs 13.3-14.4 us on 1024^3 with 64-column tiles
+        e_bn = K["mma_rate_bn"].get(bn, 0.6) * 0.86
     padding = (rows * cols * op.K) / float(tiles_m * bm * tiles_n * bn * k_blocks * bk)
     t_kb = 2.0 * bm * bn * bk / (rate * e_bn)
     # -- pipeline: stages - 1 loads in flight while one stage is consumed

@@ -1,8 +1,9 @@
 """Raw config spaces of the sm_100a kernels and their descriptor base class.
 
 A raw config is the dict the operator modules pass to the kernel (and that
-`select_best` returns): block_M (tcgen05 M = 128), block_N (64 / 128 / 256), block_K (64
-= one 128-byte swizzle row of 16-bit elements), num_stages, thread_num (6 warps for
+`select_best` returns): block_M (tcgen05 M = 128, or 256 for a CTA pair), block_N (64 /
+128 / 256), block_K (64 = one 128-byte swizzle row of 16-bit elements per stage, or 128 =
+two), num_stages, thread_num (6 warps for
 GEMMs, 9 for conv: producer / MMA / 4 epilogue) and group_m (tile raster).  Legality is
 the C ABI's (fo_query_config_legal): shared memory <= 227 KB, TMEM <= 512 columns.
 """
@@ -25,9 +26,9 @@ def smem_bytes(block_n: int, stages: int, block_m: int = 128, block_k: int = 64)
     return 1024 + stages * (128 + b_cols) * block_k * 2 + 32768 + 1536
 
 
-def max_stages(block_n: int, block_m: int = 128) -> int:
+def max_stages(block_n: int, block_m: int = 128, block_k: int = 64) -> int:
     s = 8
-    while s > 2 and smem_bytes(block_n, s, block_m) > SMEM_LIMIT:
+    while s > 2 and smem_bytes(block_n, s, block_m, block_k) > SMEM_LIMIT:
         s -= 1
     return s
 
@@ -48,6 +49,18 @@ def tcgen05_configs(block_ns: Sequence[int] = (64, 128, 256), group_ms: Sequence
                 for g in group_ms:
                     out.append({"block_M": bm, "block_N": bn, "block_K": 64, "num_stages": s,
                                 "thread_num": CONV_THREADS if conv else GEMM_THREADS, "group_m": g})
+    # block_K 128 (two K slices per stage: half the waits and commits per MMA for the one
+    # issuing thread) measured +5-7% on 128- and 64-column single-CTA tiles, +1-20% on
+    # CTA pairs (whose issuing thread has no slack at block_K 64), and a loss on 256-column
+    # single-CTA tiles, which it leaves with two stages
+    for bm, bn in ((128, 64), (128, 128), (256, 128), (256, 256)):
+        if bn not in block_ns or bm not in block_ms:
+            continue
+        top = max_stages(bn, bm, 128)
+        if top >= 3 or (top >= 2 and not conv and bm == 128):
+            for g in group_ms:
+                out.append({"block_M": bm, "block_N": bn, "block_K": 128, "num_stages": top,
+                            "thread_num": CONV_THREADS if conv else GEMM_THREADS, "group_m": g})
     if conv:  # operand-swapped conv: 128 output channels x block_N pixels per tile
         for bn in (128, 256):
             for s in sorted({x for x in (stages or (3, 4)) if 3 <= x <= max_stages(bn)}, reverse=True):

@@ -182,7 +182,8 @@ int check_cfg(int op, int out_dtype, const FoTileCfg* cfg, char* why, size_t why
   if (cfg->block_m == 256 && cfg->block_n < 128) return say("CTA pairs (block_m 256) need block_n >= 128, got %d", cfg->block_n);
   if (cfg->block_n != 64 && cfg->block_n != 128 && cfg->block_n != 256)
     return say("block_n must be 64, 128 or 256, got %d", cfg->block_n);
-  if (cfg->block_k != 64) return say("block_k must be 64 (one 128-byte swizzle row), got %d", cfg->block_k);
+  if (cfg->block_k != 64 && cfg->block_k != 128)
+    return say("block_k must be 64 or 128 (one or two 128-byte swizzle rows per stage), got %d", cfg->block_k);
   const int min_stages = op == 1 ? 3 : 2;
   if (cfg->stages < min_stages || cfg->stages > fo::kMaxStages)
     return say("stages out of range: %d", cfg->stages);
@@ -195,7 +196,7 @@ int check_cfg(int op, int out_dtype, const FoTileCfg* cfg, char* why, size_t why
   if (cfg->max_ctas < 0) return say("max_ctas must be >= 0, got %d", cfg->max_ctas);
   if (cfg->split_k < 0 || cfg->split_k > 16) return say("split_k must be 0 (automatic) .. 16, got %d", cfg->split_k);
   // (the direct conv's shared memory depends on the image width: fo_conv2d checks it)
-  const int smem = fo::smem_bytes_for(cfg->block_n, cfg->stages, cfg->block_m == 256);
+  const int smem = fo::smem_bytes_for(cfg->block_n, cfg->stages, cfg->block_m == 256, cfg->block_k / 64);
   if (cfg->swap_ab != 2 && smem > 232448) return say("shared memory %d B exceeds the 227 KB per-block limit", smem);
   // TMEM: two fp32 accumulators of block_n columns each, <= 512 columns.
   if (2 * cfg->block_n > 512) return say("TMEM columns %d exceed 512", 2 * cfg->block_n);
@@ -351,7 +352,7 @@ int fo_set_wait_timeout_ns(uint64_t ns) {
 
 size_t fo_config_smem_bytes(int32_t op, int32_t out_dtype, const FoTileCfg* cfg) {
   if (check_cfg(op, out_dtype, cfg, nullptr, 0) != FO_OK) return 0;
-  return static_cast<size_t>(fo::smem_bytes_for(cfg->block_n, cfg->stages, cfg->block_m == 256));
+  return static_cast<size_t>(fo::smem_bytes_for(cfg->block_n, cfg->stages, cfg->block_m == 256, cfg->block_k / 64));
 }
 
 int fo_query_config_legal(int32_t op, int32_t out_dtype, const FoTileCfg* cfg, char* why,
@@ -497,7 +498,8 @@ int fo_gemm(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
   }
   la.grid = pair ? 2 * pl.grid : pl.grid;
   la.pair = pair;
-  la.smem = fo::smem_bytes_for(bn, cfg->stages, pair);
+  p.kps = cfg->block_k / 64;
+  la.smem = fo::smem_bytes_for(bn, cfg->stages, pair, p.kps);
   la.stream = static_cast<cudaStream_t>(stream);
   const int out_dt = d->out_dtype == FO_DT_F16 ? fo::DT_F16 : d->out_dtype == FO_DT_BF16 ? fo::DT_BF16 : fo::DT_F32;
   cudaError_t e = ln ? fo::launch_ln_family(bn, out_dt, la)
@@ -754,7 +756,8 @@ int fo_conv2d(const FoConvDesc* d, const FoTileCfg* cfg, void* stream) {
                                           split_counter_bytes(pl, 1));
   }
   la.grid = pl.grid * (pair ? 2 : 1);
-  la.smem = fo::smem_bytes_for(bn, cfg->stages, pair);
+  p.kps = p.conv_tma ? cfg->block_k / 64 : 1;  // the cp.async gather fills one k-block per stage
+  la.smem = fo::smem_bytes_for(bn, cfg->stages, pair, p.kps);
   la.stream = static_cast<cudaStream_t>(stream);
   const int out_dt = d->out_dtype == FO_DT_F16 ? fo::DT_F16 : d->out_dtype == FO_DT_BF16 ? fo::DT_BF16 : fo::DT_F32;
   cudaError_t e = fo::launch_conv_family(bn, act, out_dt, la);

@@ -75,6 +75,10 @@ struct KParams {
   // direct conv (fo_direct_conv_kernel): input rows padded to pitch P positions, Hp padded
   // rows per image, nR rows per pixel slot, pslots slots, nimg images
   int P, Hp, nR, pslots, nimg;
+  // k-blocks (64-wide K slices) per pipeline stage: 1 or 2 (block_k 128).  Two per stage
+  // halve the barrier waits, fences and commits the single MMA-issuing thread spends per
+  // MMA (8 MMAs per wait / commit instead of 4).
+  int kps;
   // work units: units [0, dp_units) are whole tiles; the remaining tiles are split along K
   // into `split` parts of kb_per_part k-blocks, reduced through split_ws / split_cnt.
   int num_units, dp_units, split, kb_per_part;
@@ -93,8 +97,9 @@ struct KParams {
 
 __host__ __device__ constexpr int b_stage_bytes(int bn) { return bn * kBK * 2; }
 // pair: CTA-pair kernel (block_m 256), where each CTA holds half of the B tile.
-__host__ __device__ constexpr int smem_bytes_for(int bn, int stages, bool pair = false) {
-  return 1024 + stages * (kAStageBytes + b_stage_bytes(pair ? bn / 2 : bn)) + kEpiBytes + kMiscBytes;
+// kps: k-blocks per stage (block_k / 64).
+__host__ __device__ constexpr int smem_bytes_for(int bn, int stages, bool pair = false, int kps = 1) {
+  return 1024 + stages * kps * (kAStageBytes + b_stage_bytes(pair ? bn / 2 : bn)) + kEpiBytes + kMiscBytes;
 }
 
 __device__ __forceinline__ void record_error(const KParams& p, int code, int where) {
@@ -316,8 +321,9 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
                                              ~static_cast<uintptr_t>(1023));
   const int stages = p.stages;
   const uint32_t sA = smem_u32(smem);
-  const uint32_t sB = sA + stages * kAStageBytes;
-  const uint32_t sEpi = sB + stages * kBStage;
+  const int kps = p.kps;
+  const uint32_t sB = sA + stages * kps * kAStageBytes;
+  const uint32_t sEpi = sB + stages * kps * kBStage;
   uint8_t* misc = smem + (sEpi - sA) + kEpiBytes;
   // misc: [0,64) full[8] | [64,128) empty[8] | [128,144) tfull[2] | [144,160) tempty[2]
   //       | [160,168) drain | [248,256) tmem addr + abort flag
@@ -383,7 +389,8 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
         for (int u = cid; u < p.num_units && ok; u += ncl) {
           const Unit un = unit_of(p, u);
           const int tm = un.tm, tn = un.tn;
-          for (int kb = un.kb0; kb < un.kb1; ++kb) {
+          for (int kb0 = un.kb0; kb0 < un.kb1; kb0 += kps) {
+            const int nk = min(kps, un.kb1 - kb0);  // k-blocks in this stage
             if (!mbar_wait(bar_empty + 8 * s, ph ^ 1, tmo, abort_flag)) {
               ok = false;
               break;
@@ -394,24 +401,32 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
             if constexpr (PAIR) {
               // Both CTAs' bytes complete on the leader's barrier; only the leader arrives.
               const uint32_t fbl = mapa_shared(fb, 0);
-              if (rank == 0) mbar_arrive_expect_tx(fb, 2 * (kAStageBytes + kBStage));
-              tma_load_2d_pair(sA + s * kAStageBytes, &tmA, fbl, kb * kBK, arow);
-              if (p.b_mn) {
+              if (rank == 0) mbar_arrive_expect_tx(fb, 2 * nk * (kAStageBytes + kBStage));
+              for (int i = 0; i < nk; ++i) {
+                const int kb = kb0 + i;
+                const uint32_t sa = sA + (s * kps + i) * kAStageBytes, sb = sB + (s * kps + i) * kBStage;
+                tma_load_2d_pair(sa, &tmA, fbl, kb * kBK, arow);
+                if (p.b_mn) {
 #pragma unroll
-                for (int j = 0; j < kBHalf / 64; ++j)
-                  tma_load_2d_pair(sB + s * kBStage + j * 64 * 128, &tmB, fbl, bcol + j * 64, kb * kBK);
-              } else {
-                tma_load_2d_pair(sB + s * kBStage, &tmB, fbl, kb * kBK, bcol);
+                  for (int j = 0; j < kBHalf / 64; ++j)
+                    tma_load_2d_pair(sb + j * 64 * 128, &tmB, fbl, bcol + j * 64, kb * kBK);
+                } else {
+                  tma_load_2d_pair(sb, &tmB, fbl, kb * kBK, bcol);
+                }
               }
             } else {
-              mbar_arrive_expect_tx(fb, kAStageBytes + kBStage);
-              tma_load_2d(sA + s * kAStageBytes, &tmA, fb, kb * kBK, arow);
-              if (p.b_mn) {
+              mbar_arrive_expect_tx(fb, nk * (kAStageBytes + kBStage));
+              for (int i = 0; i < nk; ++i) {
+                const int kb = kb0 + i;
+                const uint32_t sa = sA + (s * kps + i) * kAStageBytes, sb = sB + (s * kps + i) * kBStage;
+                tma_load_2d(sa, &tmA, fb, kb * kBK, arow);
+                if (p.b_mn) {
 #pragma unroll
-                for (int j = 0; j < BN / 64; ++j)
-                  tma_load_2d(sB + s * kBStage + j * 64 * 128, &tmB, fb, bcol + j * 64, kb * kBK);
-              } else {
-                tma_load_2d(sB + s * kBStage, &tmB, fb, kb * kBK, bcol);
+                  for (int j = 0; j < BN / 64; ++j)
+                    tma_load_2d(sb + j * 64 * 128, &tmB, fb, bcol + j * 64, kb * kBK);
+                } else {
+                  tma_load_2d(sb, &tmB, fb, kb * kBK, bcol);
+                }
               }
             }
             ++issued;
@@ -448,37 +463,44 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
           const int ow = rem - oh * p.OW;
           const int w0 = ow * p.stride - p.pad;
           const int h0 = oh * p.stride - p.pad;
-          for (int kb = un.kb0; kb < un.kb1; ++kb) {
-            const int tap = kb / p.c_blocks;
-            const int cb = kb - tap * p.c_blocks;
-            const int kh = tap / p.KW;
-            const int kw = tap - kh * p.KW;
+          for (int kb0 = un.kb0; kb0 < un.kb1; kb0 += kps) {
+            const int nk = min(kps, un.kb1 - kb0);  // k-blocks in this stage
             if (!mbar_wait(bar_empty + 8 * s, ph ^ 1, tmo, abort_flag)) {
               ok = false;
               break;
             }
             const uint32_t fb = bar_full + 8 * s;
             const int bcol = tn * BN + static_cast<int>(rank) * kBHalf;
-            const uint16_t ow16 = static_cast<uint16_t>(kw * p.dil), oh16 = static_cast<uint16_t>(kh * p.dil);
-            if constexpr (SWAP) {
-              mbar_arrive_expect_tx(fb, kAStageBytes + kBStage);
-#pragma unroll
-              for (int j = 0; j < 2; ++j)  // A: 128 channels x 64 K of the weights, MN-major
-                tma_load_2d(sA + s * kAStageBytes + j * 64 * 128, &tmB, fb, tm * kBM + j * 64, tap * p.C + cb * kBK);
-              tma_load_im2col_4d(sB + s * kBStage, &tmA, fb, cb * kBK, w0, h0, n_img, ow16, oh16);  // B: BN pixels
-            } else if constexpr (PAIR) {
-              const uint32_t fbl = mapa_shared(fb, 0);
-              if (rank == 0) mbar_arrive_expect_tx(fb, 2 * (kAStageBytes + kBStage));
-              tma_load_im2col_4d_pair(sA + s * kAStageBytes, &tmA, fbl, cb * kBK, w0, h0, n_img, ow16, oh16);
-#pragma unroll
-              for (int j = 0; j < kBHalf / 64; ++j)
-                tma_load_2d_pair(sB + s * kBStage + j * 64 * 128, &tmB, fbl, bcol + j * 64, tap * p.C + cb * kBK);
+            if constexpr (PAIR) {
+              if (rank == 0) mbar_arrive_expect_tx(fb, 2 * nk * (kAStageBytes + kBStage));
             } else {
-              mbar_arrive_expect_tx(fb, kAStageBytes + kBStage);
-              tma_load_im2col_4d(sA + s * kAStageBytes, &tmA, fb, cb * kBK, w0, h0, n_img, ow16, oh16);
+              mbar_arrive_expect_tx(fb, nk * (kAStageBytes + kBStage));
+            }
+            for (int i = 0; i < nk; ++i) {
+              const int kb = kb0 + i;
+              const int tap = kb / p.c_blocks;
+              const int cb = kb - tap * p.c_blocks;
+              const int kh = tap / p.KW;
+              const int kw = tap - kh * p.KW;
+              const uint16_t ow16 = static_cast<uint16_t>(kw * p.dil), oh16 = static_cast<uint16_t>(kh * p.dil);
+              const uint32_t sa = sA + (s * kps + i) * kAStageBytes, sb = sB + (s * kps + i) * kBStage;
+              if constexpr (SWAP) {
 #pragma unroll
-              for (int j = 0; j < BN / 64; ++j)
-                tma_load_2d(sB + s * kBStage + j * 64 * 128, &tmB, fb, bcol + j * 64, tap * p.C + cb * kBK);
+                for (int j = 0; j < 2; ++j)  // A: 128 channels x 64 K of the weights, MN-major
+                  tma_load_2d(sa + j * 64 * 128, &tmB, fb, tm * kBM + j * 64, tap * p.C + cb * kBK);
+                tma_load_im2col_4d(sb, &tmA, fb, cb * kBK, w0, h0, n_img, ow16, oh16);  // B: BN pixels
+              } else if constexpr (PAIR) {
+                const uint32_t fbl = mapa_shared(fb, 0);
+                tma_load_im2col_4d_pair(sa, &tmA, fbl, cb * kBK, w0, h0, n_img, ow16, oh16);
+#pragma unroll
+                for (int j = 0; j < kBHalf / 64; ++j)
+                  tma_load_2d_pair(sb + j * 64 * 128, &tmB, fbl, bcol + j * 64, tap * p.C + cb * kBK);
+              } else {
+                tma_load_im2col_4d(sa, &tmA, fb, cb * kBK, w0, h0, n_img, ow16, oh16);
+#pragma unroll
+                for (int j = 0; j < BN / 64; ++j)
+                  tma_load_2d(sb + j * 64 * 128, &tmB, fb, bcol + j * 64, tap * p.C + cb * kBK);
+              }
             }
             ++issued;
             if (++s == stages) {
@@ -606,34 +628,43 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
         tc_fence_after();
         const uint32_t d = tmem_base + acc * BN;
         uint32_t accum = 0;
-        for (int kb = un.kb0; kb < un.kb1; ++kb) {
+        for (int kb0 = un.kb0; kb0 < un.kb1; kb0 += kps) {
+          const int nk = min(kps, un.kb1 - kb0);
           if (!mbar_wait(bar_full + 8 * s, ph, tmo, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
+#pragma unroll 2
+          for (int i = 0; i < nk; ++i) {
+            const uint64_t a = ad + static_cast<uint64_t>(i * (kAStageBytes >> 4));
+            const uint64_t b = bd + static_cast<uint64_t>(i * (kBStage >> 4));
+            if constexpr (PAIR) {
+              tc_mma_f16_pair(d, a, b, idesc, accum);
+              tc_mma_f16_pair(d, a + a_kstep, b + b_kstep, idesc, 1u);
+              tc_mma_f16_pair(d, a + 2 * a_kstep, b + 2 * b_kstep, idesc, 1u);
+              tc_mma_f16_pair(d, a + 3 * a_kstep, b + 3 * b_kstep, idesc, 1u);
+            } else {
+              tc_mma_f16(d, a, b, idesc, accum);
+              tc_mma_f16(d, a + a_kstep, b + b_kstep, idesc, 1u);
+              tc_mma_f16(d, a + 2 * a_kstep, b + 2 * b_kstep, idesc, 1u);
+              tc_mma_f16(d, a + 3 * a_kstep, b + 3 * b_kstep, idesc, 1u);
+            }
+            accum = 1u;
+          }
           if constexpr (PAIR) {
-            tc_mma_f16_pair(d, ad, bd, idesc, accum);
-            tc_mma_f16_pair(d, ad + a_kstep, bd + b_kstep, idesc, 1u);
-            tc_mma_f16_pair(d, ad + 2 * a_kstep, bd + 2 * b_kstep, idesc, 1u);
-            tc_mma_f16_pair(d, ad + 3 * a_kstep, bd + 3 * b_kstep, idesc, 1u);
             tc_commit_pair_both(bar_empty + 8 * s);  // free the stage in both CTAs
           } else {
-            tc_mma_f16(d, ad, bd, idesc, accum);
-            tc_mma_f16(d, ad + a_kstep, bd + b_kstep, idesc, 1u);
-            tc_mma_f16(d, ad + 2 * a_kstep, bd + 2 * b_kstep, idesc, 1u);
-            tc_mma_f16(d, ad + 3 * a_kstep, bd + 3 * b_kstep, idesc, 1u);
             tc_commit(bar_empty + 8 * s);
           }
-          accum = 1u;
           if (++s == stages) {
             s = 0;
             ph ^= 1;
             ad = a_desc0;
             bd = b_desc0;
           } else {
-            ad += kAStageBytes >> 4;
-            bd += kBStage >> 4;
+            ad += static_cast<uint64_t>(kps * (kAStageBytes >> 4));
+            bd += static_cast<uint64_t>(kps * (kBStage >> 4));
           }
         }
         if (!ok) break;

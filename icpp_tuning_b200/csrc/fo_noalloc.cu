@@ -197,7 +197,8 @@ int run(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
   p.num_units = p.dp_units = p.num_tiles;  // whole tiles
   p.split = 1;
   p.kb_per_part = p.k_blocks;
-  la.smem = fo::smem_bytes_for(bn, cfg->stages, pair);
+  p.kps = cfg->block_k / 64;
+  la.smem = fo::smem_bytes_for(bn, cfg->stages, pair, p.kps);
   la.stream = st;
   cudaError_t e = fo::launch_ln_family(bn, d->out_dtype == FO_DT_F16 ? fo::DT_F16 : fo::DT_BF16, la);
   if (e != cudaSuccess) {

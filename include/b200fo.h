@@ -69,7 +69,8 @@ extern "C" {
 typedef struct FoTileCfg {
   int32_t block_m;  /* 128 (one CTA) or 256 (a CTA pair, tcgen05 cta_group::2)         */
   int32_t block_n;  /* 64, 128 or 256                                                   */
-  int32_t block_k;  /* 64                                                               */
+  int32_t block_k;  /* 64, or 128: two 64-wide K slices per pipeline stage (one barrier  */
+                    /* wait and one commit per 8 MMAs instead of 4)                       */
   int32_t stages;   /* shared-memory pipeline depth, 2..8 (bounded by 227 KB)          */
   int32_t group_m;  /* tile raster: 0 = row-major, g>0 = groups of g row blocks        */
   int32_t max_ctas; /* persistent grid size cap; 0 = one CTA per SM                     */

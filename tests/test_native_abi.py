@@ -142,6 +142,18 @@ def test_conv_batchnorm_rejects(kw, msg):
     assert msg in N.last_error()
 
 
+def test_block_k_values():
+    assert N.config_legal(0, N.FO_DT_BF16, N.tile_cfg(128, 3, 8, block_k=128))[0]
+    ok, why = N.config_legal(0, N.FO_DT_BF16, N.tile_cfg(128, 3, 8, block_k=96))
+    assert not ok and "block_k" in why
+    ok, why = N.config_legal(0, N.FO_DT_BF16, N.tile_cfg(256, 3, 8, block_k=128))  # 3 x 96 KB stages
+    assert not ok and "shared memory" in why
+    # two 64-wide K slices per stage double each stage's bytes
+    one = N.config_smem_bytes(0, N.FO_DT_BF16, N.tile_cfg(128, 3, 8))
+    two = N.config_smem_bytes(0, N.FO_DT_BF16, N.tile_cfg(128, 3, 8, block_k=128))
+    assert two - one == 3 * (128 * 64 * 2 + 128 * 64 * 2)
+
+
 def test_split_k_field():
     ok, why = N.config_legal(0, N.FO_DT_BF16, N.tile_cfg(256, 4, 8, split_k=17))
     assert not ok and "split_k" in why
