@@ -54,7 +54,7 @@ def tcgen05_configs(block_ns: Sequence[int] = (64, 128, 256), group_ms: Sequence
     # CTA pairs (whose issuing thread has no slack at block_K 64), and a loss on 256-column
     # single-CTA tiles, which it leaves with two stages
     for bm, bn in ((128, 64), (128, 128), (256, 128), (256, 256)):
-        if bn not in block_ns or bm not in block_ms:
+        if conv or bn not in block_ns or bm not in block_ms:  # the conv kernels stage one K slice
             continue
         top = max_stages(bn, bm, 128)
         if top >= 3 or (top >= 2 and not conv and bm == 128):

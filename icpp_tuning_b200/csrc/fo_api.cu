@@ -623,6 +623,8 @@ int fo_conv2d(const FoConvDesc* d, const FoTileCfg* cfg, void* stream) {
   const int64_t xelems = static_cast<int64_t>(d->n) * d->h * d->w * d->c;
   if (M64 > (1ll << 31) - 1 || xelems > (1ll << 40)) return fail(FO_EINVAL, "conv problem too large");
   if (M64 == 0) return ok();
+  if (cfg->block_k != 64 && cfg->swap_ab != 2)
+    return fail(FO_EINVAL, "conv2d stages one 64-wide K slice: block_k must be 64, got %d", cfg->block_k);
   if (d->x == nullptr || d->wgt == nullptr || d->out == nullptr || !aligned16(d->x) || !aligned16(d->wgt) ||
       !aligned16(d->out))
     return fail(FO_EINVAL, "x, wgt and out must be 16-byte aligned device pointers");
@@ -756,7 +758,7 @@ int fo_conv2d(const FoConvDesc* d, const FoTileCfg* cfg, void* stream) {
                                           split_counter_bytes(pl, 1));
   }
   la.grid = pl.grid * (pair ? 2 : 1);
-  p.kps = p.conv_tma ? cfg->block_k / 64 : 1;  // the cp.async gather fills one k-block per stage
+  p.kps = 1;  // conv kernels stage one K slice (block_k 128 is a GEMM-family option)
   la.smem = fo::smem_bytes_for(bn, cfg->stages, pair, p.kps);
   la.stream = static_cast<cudaStream_t>(stream);
   const int out_dt = d->out_dtype == FO_DT_F16 ? fo::DT_F16 : d->out_dtype == FO_DT_BF16 ? fo::DT_BF16 : fo::DT_F32;

@@ -287,7 +287,7 @@ __device__ __forceinline__ void drain_loads(uint32_t bar_full, int stages, int i
   }
 }
 
-template <int BN, int ACT, int OUT_DT, bool LN, bool CONV, bool PAIR, bool SWAP = false>
+template <int BN, int ACT, int OUT_DT, bool LN, bool CONV, bool PAIR, bool SWAP = false, int KPS = 1>
 __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
     fo_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const __grid_constant__ CUtensorMap tmC, const KParams p) {
@@ -321,7 +321,10 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
                                              ~static_cast<uintptr_t>(1023));
   const int stages = p.stages;
   const uint32_t sA = smem_u32(smem);
-  const int kps = p.kps;
+  // KPS (k-blocks per stage) is a template parameter: the single MMA-issuing thread is
+  // the bottleneck of this loop, and a runtime stage depth costs it measurable time
+  constexpr int kps = KPS;
+  static_assert(KPS == 1 || (KPS == 2 && !CONV), "two K slices per stage: GEMM family only");
   const uint32_t sB = sA + stages * kps * kAStageBytes;
   const uint32_t sEpi = sB + stages * kps * kBStage;
   uint8_t* misc = smem + (sEpi - sA) + kEpiBytes;
@@ -390,7 +393,7 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
           const Unit un = unit_of(p, u);
           const int tm = un.tm, tn = un.tn;
           for (int kb0 = un.kb0; kb0 < un.kb1; kb0 += kps) {
-            const int nk = min(kps, un.kb1 - kb0);  // k-blocks in this stage
+            const int nk = KPS == 1 ? 1 : min(KPS, un.kb1 - kb0);  // k-blocks in this stage
             if (!mbar_wait(bar_empty + 8 * s, ph ^ 1, tmo, abort_flag)) {
               ok = false;
               break;
@@ -464,7 +467,7 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
           const int w0 = ow * p.stride - p.pad;
           const int h0 = oh * p.stride - p.pad;
           for (int kb0 = un.kb0; kb0 < un.kb1; kb0 += kps) {
-            const int nk = min(kps, un.kb1 - kb0);  // k-blocks in this stage
+            const int nk = KPS == 1 ? 1 : min(KPS, un.kb1 - kb0);  // k-blocks in this stage
             if (!mbar_wait(bar_empty + 8 * s, ph ^ 1, tmo, abort_flag)) {
               ok = false;
               break;
@@ -629,7 +632,7 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
         const uint32_t d = tmem_base + acc * BN;
         uint32_t accum = 0;
         for (int kb0 = un.kb0; kb0 < un.kb1; kb0 += kps) {
-          const int nk = min(kps, un.kb1 - kb0);
+          const int nk = KPS == 1 ? 1 : min(KPS, un.kb1 - kb0);
           if (!mbar_wait(bar_full + 8 * s, ph, tmo, abort_flag)) {
             ok = false;
             break;

@@ -19,9 +19,9 @@ struct LaunchArgs {
   bool swap;  // conv: operand-swapped kernel (M = output channels, N = pixels)
 };
 
-template <int BN, int ACT, int OUT_DT, bool LN, bool CONV, bool PAIR, bool SWAP = false>
-cudaError_t launch_tc(const LaunchArgs& a) {
-  auto kern = fo_tc_kernel<BN, ACT, OUT_DT, LN, CONV, PAIR, SWAP>;
+template <int BN, int ACT, int OUT_DT, bool LN, bool CONV, bool PAIR, bool SWAP, int KPS>
+cudaError_t launch_tc_k(const LaunchArgs& a) {
+  auto kern = fo_tc_kernel<BN, ACT, OUT_DT, LN, CONV, PAIR, SWAP, KPS>;
   // Opt in to the full 227 KB of dynamic shared memory once per device.
   static std::atomic<uint64_t> opted{0};
   int dev = 0;
@@ -62,6 +62,18 @@ cudaError_t launch_tc(const LaunchArgs& a) {
   } else {
     kern<<<a.grid, kThreads, a.smem, a.stream>>>(a.tmA, a.tmB, a.tmC, a.p);
     return cudaGetLastError();
+  }
+}
+
+// One k-block per stage, or two (p.kps == 2, block_k 128; GEMM family only).
+template <int BN, int ACT, int OUT_DT, bool LN, bool CONV, bool PAIR, bool SWAP = false>
+cudaError_t launch_tc(const LaunchArgs& a) {
+  if constexpr (CONV) {
+    if (a.p.kps != 1) return cudaErrorInvalidValue;
+    return launch_tc_k<BN, ACT, OUT_DT, LN, CONV, PAIR, SWAP, 1>(a);
+  } else {
+    return a.p.kps == 2 ? launch_tc_k<BN, ACT, OUT_DT, LN, CONV, PAIR, SWAP, 2>(a)
+                        : launch_tc_k<BN, ACT, OUT_DT, LN, CONV, PAIR, SWAP, 1>(a);
   }
 }
 

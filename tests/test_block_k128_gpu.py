@@ -42,16 +42,9 @@ def test_split_tail_block_k128(block_m):
     status_clean()
 
 
-@pytest.mark.parametrize("tile", [dict(block_n=128, stages=3, swap_ab=1), dict(block_n=128, stages=3),
-                                  dict(block_n=256, stages=3, block_m=256)], ids=str)
-@pytest.mark.parametrize("shape", [(2, 28, 28, 128, 128, 3, 1, 1), (3, 13, 11, 72, 256, 3, 2, 1)], ids=str)
-def test_conv_block_k128(tile, shape):
-    n, h, w, c, f, k, s, p = shape
-    g = gen(82)
-    x = randn(g, n, h, w, c)
-    wt = randn(g, k, k, c, f, scale=(k * k * c) ** -0.5)
-    bias = randn(g, f, scale=0.1)
-    cfg = N.tile_cfg(group_m=0, block_k=128, **tile)
-    out = fused.conv2d_nhwc(*cuda(x, wt), bias=bias.cuda(), relu=True, stride=s, padding=p, config=cfg)
-    assert_close(out, R.conv2d_bias_relu(x, wt, bias, True, s, p, 1, out_dtype=torch.bfloat16), TOL)
-    status_clean()
+def test_conv_rejects_block_k128():
+    """The conv kernels stage one 64-wide K slice; block_k 128 is a GEMM-family option."""
+    x = torch.zeros(2, 8, 8, 64, dtype=torch.bfloat16, device="cuda")
+    wt = torch.zeros(3, 3, 64, 128, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(N.FoError, match="block_k must be 64"):
+        fused.conv2d_nhwc(x, wt, config=N.tile_cfg(128, 3, 0, block_k=128))
