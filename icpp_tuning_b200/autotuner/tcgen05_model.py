@@ -61,6 +61,13 @@ CONSTANTS = {
     "split_read_bytes_per_s": 30e9,
     # one k-block of a 128 x 256 tile on one SM under the power cap (4096^3: 101 us / 3.46 waves / 64)
     "split_t_kb256_s": 0.45e-6,
+    # cluster split-K (fo_api.cu plan_cluster_split): one 64-wide k-block of a single-wave
+    # 128-row tile (any block_N), the cluster's start / exchange / exit cost as
+    # c0 + c1 x parts per block_N, and how many clusters of each size the GPU holds at
+    # once (measured on B200 with one CTA per SM)
+    "cluster_t_kb64_s": 0.30e-6,
+    "cluster_cost_s": {64: (0.9e-6, 0.32e-6), 128: (1.9e-6, 0.5e-6), 256: (2.3e-6, 1.1e-6)},
+    "cluster_capacity": {2: 74, 3: 45, 4: 33, 5: 26, 6: 22, 7: 15, 8: 15},
     "l2_resident_fraction": 0.4,  # share of L2 an operand can hold across waves (two dies)
     "l2_fraction": 0.6,  # share of L2 that holds one wave's operand working set
 }
@@ -106,6 +113,41 @@ def split_plan(tiles: int, k_blocks: int, cap: int, bn: int = 256, conv: bool = 
     kbp = -(-k_blocks // split)
     split = -(-k_blocks // kbp)
     return full * cap, left, max(1, split)
+
+
+def _smem_bytes(bn: int, stages: int, kps: int, csplit: int) -> int:
+    """fo_kernel.cuh smem_bytes_for of a single-CTA tile with a cluster split's receive area."""
+    recv = (csplit - 1) * -(-(4 * (bn // 32)) // csplit) * 32 * 144 if csplit > 1 else 0
+    return 1024 + stages * kps * (128 + bn) * 64 * 2 + max(32768, recv) + 1536
+
+
+def cluster_stages(bn: int, stages: int, kps: int, s: int) -> int:
+    while stages > 2 and _smem_bytes(bn, stages, kps, s) > 232448:
+        stages -= 1
+    return stages if _smem_bytes(bn, stages, kps, s) <= 232448 else 0
+
+
+def cluster_split_plan(tiles: int, k_blocks: int, kps: int, cap: int, bn: int, stages: int) -> int:
+    """Mirror of fo_api.cu plan_cluster_split (automatic mode) and the launch's fallback
+    over cluster sizes that do not all fit the GPU: the part count used, or 0."""
+    K = CONSTANTS
+    nst = -(-k_blocks // kps)
+    if 2 * tiles > cap or nst < 2:
+        return 0
+    t_kb = K["cluster_t_kb64_s"]
+    c0, c1 = K["cluster_cost_s"][bn]
+    t1 = k_blocks * t_kb
+    cands = []
+    for s in range(2, 9):
+        if tiles * s > cap or s > nst or cluster_stages(bn, stages, kps, s) == 0:
+            continue
+        t = -(-nst // s) * kps * t_kb + c0 + c1 * s
+        if t < 0.9 * t1:
+            cands.append((t, s))
+    for _, s in sorted(cands):
+        if tiles <= K["cluster_capacity"].get(s, 0):
+            return s
+    return 0
 
 
 def _traffic_bytes(op: OpSpec, c: TuneConfig, hw: GPUSpec, ctas: int) -> float:
@@ -194,7 +236,14 @@ def _model(op: OpSpec, c: TuneConfig, hw: GPUSpec) -> dict:
     # last, less than half-full wave is split along K, so it costs 1/split of a wave plus
     # the partials' reduction
     t_work = waves * t_tile
-    if not op.has_reduction_epilogue and not (pair and ml.kind == "implicit_gemm_conv"):
+    csplit = 0
+    if not op.has_reduction_epilogue and not pair and ml.kind != "implicit_gemm_conv":
+        # cluster split (no workspace needed): each part runs 1/s of the stages
+        csplit = cluster_split_plan(tiles, k_blocks * bk // 64, bk // 64, cap, bn, c.num_stages)
+        if csplit > 1:
+            c0, c1 = K["cluster_cost_s"][bn]
+            t_work = t_tile * (-(-k_blocks // csplit)) / k_blocks + c0 + c1 * csplit
+    if csplit < 2 and not op.has_reduction_epilogue and not (pair and ml.kind == "implicit_gemm_conv"):
         # the planner sees the whole persistent grid (cap), not just the busy CTAs
         conv = ml.kind == "implicit_gemm_conv"
         dp_units, left, split = split_plan(tiles, k_blocks, cap, bn, conv)

@@ -45,12 +45,15 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
   std::call_once(once, [] {
+    cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;  // legal under a capture
+    cudaThreadExchangeStreamCaptureMode(&mode);
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
             cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
       fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    cudaThreadExchangeStreamCaptureMode(&mode);
   });
   return fn;
 }
@@ -66,24 +69,33 @@ struct DevInfo {
   int* status;
 };
 
+// The status word lives in this module's own device memory (zero at module load), so
+// the first call on a device allocates and synchronises nothing: a first call made
+// while the caller's stream is being captured into a CUDA graph stays legal.
+__device__ int g_status_words[4];
+
 int device_info(DevInfo* out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
     return fail(FO_ENODEVICE, "no current CUDA device");
   std::lock_guard<std::mutex> lk(g_dev_mu);
   if (g_status[dev] == nullptr) {
+    // Attribute and symbol queries enqueue nothing; relaxed mode keeps them legal under
+    // a global-mode capture on another thread's stream.
+    cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+    cudaThreadExchangeStreamCaptureMode(&mode);
     int major = 0, sms = 0;
     cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    void* st = nullptr;
+    const cudaError_t e = major == 10 ? cudaGetSymbolAddress(&st, g_status_words) : cudaSuccess;
+    cudaThreadExchangeStreamCaptureMode(&mode);
     if (major != 10)
       return fail(FO_ENODEVICE, "device %d has compute capability %d.x; this library is built for sm_100a",
                   dev, major);
-    int* st = nullptr;
-    if (cudaMalloc(&st, 4 * sizeof(int)) != cudaSuccess)
-      return fail(FO_ECUDA, "cudaMalloc of the device status word failed");
-    cudaMemset(st, 0, 4 * sizeof(int));
-    cudaDeviceSynchronize();
-    g_status[dev] = st;
+    if (e != cudaSuccess || st == nullptr)
+      return fail(FO_ECUDA, "locating the device status word failed: %s", cudaGetErrorString(e));
+    g_status[dev] = static_cast<int*>(st);
     g_sms[dev] = sms;
   }
   out->dev = dev;
@@ -130,11 +142,14 @@ PFN_cuTensorMapEncodeIm2col_v12000 encode_im2col_fn() {
   static PFN_cuTensorMapEncodeIm2col_v12000 fn = nullptr;
   static std::once_flag once;
   std::call_once(once, [] {
+    cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;  // legal under a capture
+    cudaThreadExchangeStreamCaptureMode(&mode);
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", &p, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
       fn = reinterpret_cast<PFN_cuTensorMapEncodeIm2col_v12000>(p);
+    cudaThreadExchangeStreamCaptureMode(&mode);
   });
   return fn;
 }
@@ -195,6 +210,8 @@ int check_cfg(int op, int out_dtype, const FoTileCfg* cfg, char* why, size_t why
     return say("the direct conv (swap_ab 2) computes 256-position tiles: block_n must be 256, got %d", cfg->block_n);
   if (cfg->max_ctas < 0) return say("max_ctas must be >= 0, got %d", cfg->max_ctas);
   if (cfg->split_k < 0 || cfg->split_k > 16) return say("split_k must be 0 (automatic) .. 16, got %d", cfg->split_k);
+  if (cfg->split_mode < 0 || cfg->split_mode > 2)
+    return say("split_mode must be 0 (automatic), 1 (workspace) or 2 (cluster), got %d", cfg->split_mode);
   // (the direct conv's shared memory depends on the image width: fo_conv2d checks it)
   const int smem = fo::smem_bytes_for(cfg->block_n, cfg->stages, cfg->block_m == 256, cfg->block_k / 64);
   if (cfg->swap_ab != 2 && smem > 232448) return say("shared memory %d B exceeds the 227 KB per-block limit", smem);
@@ -285,6 +302,66 @@ SplitPlan plan_split(int tiles, int k_blocks, int cap, bool allow, int forced = 
   return pl;
 }
 
+// Cluster split of a single-CTA GEMM with fewer than half a wave of tiles: the s parts
+// of each tile run as one cluster (s <= 8 CTAs, all co-resident) and reduce-scatter their
+// fp32 partials through distributed shared memory, so a split costs no workspace, no
+// global round trip and no fence / atomic chain.  Candidates are ranked by the cost
+// fitted to B200 sweeps of single-wave problems (M = 64..512, K = 768..8192):
+//   stages-per-part x kps x 0.30 us  +  c0(bn) + c1(bn) x s
+// where 0.30 us is one 64-wide k-block of a 128-row tile whatever block_n (these tiles
+// are bound by load latency, not by the tensor pipe), and (c0, c1) = (0.9, 0.32),
+// (1.9, 0.5), (2.3, 1.1) us for block_n 64, 128, 256 is the cluster's start, the
+// exchange of (s - 1) / s of the tile's fp32 partials and the exit (the exchanged bytes
+// grow with block_n).  A split must beat the unsplit tile by 10%.  Every part holds at
+// least one stage and the shared memory of a CTA (pipeline + receive area) must fit
+// 227 KB: a part's short K loop needs no deep pipeline, so the stages drop (not below
+// 2) until it does (cluster_stages).  forced = s >= 2 asks for exactly s parts.  Fills
+// `cand` best first; returns how many (0: no cluster split).
+int cluster_stages(int bn, int stages, int kps, int s) {
+  while (stages > 2 && fo::smem_bytes_for(bn, stages, false, kps, s) > 232448) --stages;
+  return fo::smem_bytes_for(bn, stages, false, kps, s) <= 232448 ? stages : 0;
+}
+
+int plan_cluster_split(int tiles, int k_blocks, int kps, int cap, int bn, int stages, int forced, int cand[8],
+                       const char** why) {
+  *why = nullptr;
+  if (forced == 1) return 0;
+  const int nst = (k_blocks + kps - 1) / kps;
+  auto fits = [&](int s) {
+    return s >= 2 && s <= 8 && tiles * s <= cap && s <= nst && cluster_stages(bn, stages, kps, s) > 0;
+  };
+  if (forced >= 2) {
+    if (!fits(forced)) {
+      *why = "cluster split needs parts <= 8, tiles x parts <= the CTA cap, a stage per part and the receive area "
+             "to fit shared memory";
+      return 0;
+    }
+    cand[0] = forced;
+    return 1;
+  }
+  if (2 * tiles > cap || nst < 2) return 0;
+  const double t_kb = 0.30e-6;
+  const double c0 = bn >= 256 ? 2.3e-6 : bn >= 128 ? 1.9e-6 : 0.9e-6;
+  const double c1 = bn >= 256 ? 1.1e-6 : bn >= 128 ? 0.5e-6 : 0.32e-6;
+  const double t1 = k_blocks * t_kb;
+  double cost[8];
+  int n = 0;
+  for (int s = 2; s <= 8; ++s) {
+    if (!fits(s)) continue;
+    const double t = (nst + s - 1) / s * kps * t_kb + c0 + c1 * s;
+    if (t >= 0.9 * t1) continue;
+    int k = n++;
+    while (k > 0 && cost[k - 1] > t) {  // insertion: best first
+      cost[k] = cost[k - 1];
+      cand[k] = cand[k - 1];
+      --k;
+    }
+    cost[k] = t;
+    cand[k] = s;
+  }
+  return n;
+}
+
 // Counters (8 per slot: 4 row quarters x 2 column halves, one per epilogue warp) then
 // fp32 partials, per 128-row slot of each split tile (`halves` slots per tile: 2 for
 // CTA pairs).
@@ -308,8 +385,8 @@ int sm_count_or_default() {
 }
 
 // LayerNorm statistics: one float4 per row per slice, a slice being the column half of
-// an N tile that one epilogue warp covers (the whole tile for block_n 64).
-int ln_halves(int bn) { return bn >= 128 ? 2 : 1; }
+// an N tile that one epilogue warp covers.
+int ln_halves(int) { return 2; }
 
 size_t ln_workspace(int64_t M, int64_t N, int bn) {
   const int64_t tiles_m = (M + 127) / 128;
@@ -484,27 +561,69 @@ int fo_gemm(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
   // Persistent grid: one CTA (or CTA pair) per SM (pair of SMs).
   const int cap = pair ? (cfg->max_ctas > 0 ? cfg->max_ctas / 2 : di.sms / 2) : (cfg->max_ctas > 0 ? cfg->max_ctas : di.sms);
   if (cap < 1) return fail(FO_EINVAL, "max_ctas too small for CTA pairs");
-  SplitPlan pl = plan_split(p.num_tiles, p.k_blocks, cap, !ln, cfg->split_k, bn);
-  const size_t split_need = split_workspace(pl, bn, pair ? 2 : 1);
-  if (split_need == 0 || d->workspace == nullptr || d->workspace_bytes < split_need || !aligned16(d->workspace))
-    pl = plan_split(p.num_tiles, p.k_blocks, cap, false);  // no room for partials: whole tiles only
-  p.num_units = pl.num_units;
-  p.dp_units = pl.dp_units;
-  p.split = pl.split;
-  p.kb_per_part = pl.kb_per_part;
-  if (pl.split > 1) {
-    p.split_cnt = static_cast<int*>(d->workspace);
-    p.split_ws = reinterpret_cast<float*>(static_cast<char*>(d->workspace) + split_counter_bytes(pl, pair ? 2 : 1));
-  }
-  la.grid = pair ? 2 * pl.grid : pl.grid;
-  la.pair = pair;
   p.kps = cfg->block_k / 64;
-  la.smem = fo::smem_bytes_for(bn, cfg->stages, pair, p.kps);
+  la.pair = pair;
   la.stream = static_cast<cudaStream_t>(stream);
   const int out_dt = d->out_dtype == FO_DT_F16 ? fo::DT_F16 : d->out_dtype == FO_DT_BF16 ? fo::DT_BF16 : fo::DT_F32;
-  cudaError_t e = ln ? fo::launch_ln_family(bn, out_dt, la)
-                 : rln ? fo::launch_residual_ln(bn, out_dt, la)
-                       : fo::launch_gemm_family(bn, act, out_dt, la);
+  auto launch = [&]() {
+    return ln ? fo::launch_ln_family(bn, out_dt, la)
+              : rln ? fo::launch_residual_ln(bn, out_dt, la)
+                    : fo::launch_gemm_family(bn, act, out_dt, la);
+  };
+  cudaError_t e = cudaErrorNotReady;
+  if (cfg->split_mode == 2 && (pair || ln))
+    return fail(FO_EINVAL, "cluster split needs block_m 128 and an epilogue other than FO_EPI_BIAS_LN");
+  // Cluster split first (automatic or asked for), then the workspace split / whole tiles.
+  // A cluster size whose clusters do not all fit the GPU at once is skipped for the next.
+  if (!pair && !ln && p.K > 0 && cfg->split_mode != 1) {
+    const char* cwhy = nullptr;
+    int cand[8];
+    const int n = plan_cluster_split(p.num_tiles, p.k_blocks, p.kps, cap, bn, cfg->stages,
+                                     cfg->split_mode == 2 ? (cfg->split_k >= 2 ? cfg->split_k : 0) : cfg->split_k,
+                                     cand, &cwhy);
+    if (cfg->split_mode == 2 && n == 0)
+      return fail(FO_EINVAL, "cluster split not possible for this shape and config: %s",
+                  cwhy != nullptr ? cwhy : "a whole wave of tiles or too few k-blocks (set split_k to force)");
+    for (int i = 0; i < n; ++i) {
+      const int s = cand[i];
+      p.csplit = s;
+      p.split = s;
+      p.kb_per_part = 0;  // parts take ranges of stages (unit_of)
+      p.dp_units = 0;
+      p.num_units = p.num_tiles * s;
+      la.csplit = s;
+      la.grid = p.num_units;
+      p.stages = cluster_stages(bn, cfg->stages, p.kps, s);
+      la.smem = fo::smem_bytes_for(bn, p.stages, false, p.kps, s);
+      e = launch();
+      if (e != cudaErrorCooperativeLaunchTooLarge) break;
+    }
+    if (e == cudaErrorCooperativeLaunchTooLarge) {
+      if (cfg->split_mode == 2)
+        return fail(FO_EINVAL, "cluster split: %d clusters of %d CTAs do not fit the GPU at once", p.num_tiles,
+                    cand[0]);
+      p.csplit = 0;  // no size fits: plan without it
+      la.csplit = 0;
+      p.stages = cfg->stages;
+    }
+  }
+  if (e == cudaErrorNotReady || e == cudaErrorCooperativeLaunchTooLarge) {
+    SplitPlan pl = plan_split(p.num_tiles, p.k_blocks, cap, !ln, cfg->split_k, bn);
+    const size_t split_need = split_workspace(pl, bn, pair ? 2 : 1);
+    if (split_need == 0 || d->workspace == nullptr || d->workspace_bytes < split_need || !aligned16(d->workspace))
+      pl = plan_split(p.num_tiles, p.k_blocks, cap, false);  // no room for partials: whole tiles only
+    p.num_units = pl.num_units;
+    p.dp_units = pl.dp_units;
+    p.split = pl.split;
+    p.kb_per_part = pl.kb_per_part;
+    if (pl.split > 1) {
+      p.split_cnt = static_cast<int*>(d->workspace);
+      p.split_ws = reinterpret_cast<float*>(static_cast<char*>(d->workspace) + split_counter_bytes(pl, pair ? 2 : 1));
+    }
+    la.grid = pair ? 2 * pl.grid : pl.grid;
+    la.smem = fo::smem_bytes_for(bn, cfg->stages, pair, p.kps);
+    e = launch();
+  }
   if (e != cudaSuccess) return fail(FO_ECUDA, "kernel launch failed: %s", cudaGetErrorString(e));
   g_launches.fetch_add(ln || rln ? 2 : 1);  // LayerNorm: GEMM kernel + row kernel
   return ok();

@@ -91,6 +91,7 @@ __global__ void __launch_bounds__(320, 1)
     tma_prefetch_desc(&tmW);
     tma_prefetch_desc(&tmY);
   }
+  __syncwarp();  // reconverge each warp before the CTA-wide barrier
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -345,10 +346,11 @@ __global__ void __launch_bounds__(320, 1)
       record_error(p, kStatusTimeout, 0x42);
       *abort_flag = 1;
     }
-    if (lane == 0) bulk_wait<0>();
+    if (lane == 0) bulk_wait_read<0>();  // the stores complete with the grid
     __syncwarp();
   }
 
+  __syncwarp();  // the producer and MMA warps ran their loops on lane 0 alone
   tc_fence_before();
   __syncthreads();
   if (warp == kMmaWarp) {

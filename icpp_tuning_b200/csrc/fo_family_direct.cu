@@ -12,6 +12,7 @@ static cudaError_t launch_direct(const LaunchArgs& a) {
   cudaGetDevice(&dev);
   const uint64_t bit = 1ull << (dev & 63);
   if ((opted.load(std::memory_order_acquire) & bit) == 0) {
+    RelaxedCapture relaxed;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
     if (e != cudaSuccess) return e;
     opted.fetch_or(bit, std::memory_order_acq_rel);

@@ -58,3 +58,17 @@ cudaError_t launch_gemm_family(int bn, int act, int out_dt, const LaunchArgs& a)
 #endif
 
 }  // namespace fo
+
+#ifdef FO_PHASE_PROBE
+#define FO_PROBE_CAT2(a, b) a##b
+#define FO_PROBE_CAT(a, b) FO_PROBE_CAT2(a, b)
+// Copies this translation unit's phase timestamps to the host (latency studies only).
+extern "C" int FO_PROBE_CAT(fo_probe_read_pair, FO_PAIR)(void* host, size_t bytes) {
+  return static_cast<int>(cudaMemcpyFromSymbol(host, fo::g_fo_probe, bytes));
+}
+extern "C" int FO_PROBE_CAT(fo_probe_clear_pair, FO_PAIR)() {
+  void* a = nullptr;
+  if (cudaGetSymbolAddress(&a, fo::g_fo_probe) != cudaSuccess) return -1;
+  return static_cast<int>(cudaMemset(a, 0, sizeof(fo::g_fo_probe)));
+}
+#endif

@@ -61,9 +61,9 @@ static cudaError_t gemm_then_normalize(const LaunchArgs& a) {
     e = a.pair ? cudaErrorInvalidValue : launch_tc<BN, ACT_NONE, OUT, true, false, false>(a);
   }
   if (e != cudaSuccess) return e;
-  // The statistics come in slices of half a tile (one per epilogue warp; whole tiles
-  // for BN 64): the row pass merges tiles_n x halves slices of BN / halves columns.
-  constexpr int kHalves = BN >= 128 ? 2 : 1;
+  // The statistics come in slices of half a tile (one per epilogue warp): the row pass
+  // merges tiles_n x 2 slices of BN / 2 columns.
+  constexpr int kHalves = 2;
   LaunchArgs r = a;
   r.p.tiles_n = a.p.tiles_n * kHalves;
   return row_pass<OUT, false>(r, BN / kHalves);

@@ -90,16 +90,36 @@ struct KParams {
   const void *bn_gamma, *bn_beta, *bn_mean, *bn_var;  // vec_dtype
   const void* add_src;  // [M pixels, N] of the output dtype, row stride ld_add (or null)
   long long ld_add;
+  // cluster split (csplit = s >= 2): the s parts of a tile are the CTAs of one cluster
+  // (unit = tile * s + cluster rank, one unit per CTA); each CTA owns the 32 x 32 chunks
+  // g (= quarter * BN/32 + column chunk) with g % s == rank, receives the other parts'
+  // fp32 partials of them into shared memory (st.async) and runs their epilogue.
+  int csplit;
   float* split_ws;  // [split slot][part][BN columns][128 rows] fp32 partial accumulators
   int* split_cnt;   // [split slot][4 row quarters] arrival counters, self-resetting
                     // (a slot is a split tile's 128 rows: two per tile for CTA pairs)
 };
 
 __host__ __device__ constexpr int b_stage_bytes(int bn) { return bn * kBK * 2; }
+// Cluster split: a received 32 x 32 fp32 chunk is stored as 32 rows of 144 bytes (128 of
+// data, padded so that 16-byte accesses by consecutive rows hit distinct banks).
+constexpr int kRedRowBytes = 144;
+constexpr int kRedChunkBytes = 32 * kRedRowBytes;
+__host__ __device__ constexpr int csplit_owned_max(int bn, int s) { return (4 * (bn / 32) + s - 1) / s; }
+// Receive area of a cluster-split CTA: (s - 1) senders x its owned chunks.
+__host__ __device__ constexpr int csplit_recv_bytes(int bn, int s) {
+  return s > 1 ? (s - 1) * csplit_owned_max(bn, s) * kRedChunkBytes : 0;
+}
+// The epilogue region holds the store staging or, in a cluster split (whose epilogue
+// stores from registers), the receive area.
+__host__ __device__ constexpr int epi_region_bytes(int bn, int csplit) {
+  return csplit_recv_bytes(bn, csplit) > kEpiBytes ? csplit_recv_bytes(bn, csplit) : kEpiBytes;
+}
 // pair: CTA-pair kernel (block_m 256), where each CTA holds half of the B tile.
-// kps: k-blocks per stage (block_k / 64).
-__host__ __device__ constexpr int smem_bytes_for(int bn, int stages, bool pair = false, int kps = 1) {
-  return 1024 + stages * kps * (kAStageBytes + b_stage_bytes(pair ? bn / 2 : bn)) + kEpiBytes + kMiscBytes;
+// kps: k-blocks per stage (block_k / 64).  csplit: parts of a cluster split (0 or 1: none).
+__host__ __device__ constexpr int smem_bytes_for(int bn, int stages, bool pair = false, int kps = 1, int csplit = 0) {
+  return 1024 + stages * kps * (kAStageBytes + b_stage_bytes(pair ? bn / 2 : bn)) + epi_region_bytes(bn, csplit) +
+         kMiscBytes;
 }
 
 __device__ __forceinline__ void record_error(const KParams& p, int code, int where) {
@@ -221,6 +241,18 @@ __device__ __forceinline__ void tc_wait_ld_regs(uint32_t (&r)[32]) {
                : "memory");
 }
 
+// Orders uses of registers filled by an earlier tcgen05.ld after a tcgen05.wait::ld
+// issued for another load (volatile asm statements keep their relative order).
+__device__ __forceinline__ void tc_pin_regs(uint32_t (&r)[32]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                 "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                 "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]),
+                 "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+                 "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]),
+                 "+r"(r[30]), "+r"(r[31]));
+}
+
 __device__ __forceinline__ void tile_coords(const KParams& p, int t, int& tm, int& tn) {
   if (p.group_m <= 0) {
     tm = t / p.tiles_n;
@@ -256,8 +288,16 @@ __device__ __forceinline__ Unit unit_of(const KParams& p, int u) {
     r.st = v / p.split;
     r.part = v - r.st * p.split;
     tile = p.dp_units + r.st;
-    r.kb0 = r.part * p.kb_per_part;
-    r.kb1 = min(p.k_blocks, r.kb0 + p.kb_per_part);
+    if (p.csplit > 1) {
+      // cluster split: the tile's stages (kps k-blocks each) spread evenly over the
+      // parts, so no part is empty while parts <= stages
+      const int nst = (p.k_blocks + p.kps - 1) / p.kps;
+      r.kb0 = min(p.k_blocks, (r.part * nst / p.split) * p.kps);
+      r.kb1 = min(p.k_blocks, ((r.part + 1) * nst / p.split) * p.kps);
+    } else {
+      r.kb0 = r.part * p.kb_per_part;
+      r.kb1 = min(p.k_blocks, r.kb0 + p.kb_per_part);
+    }
   }
   tile_coords(p, tile, r.tm, r.tn);
   return r;
@@ -287,6 +327,18 @@ __device__ __forceinline__ void drain_loads(uint32_t bar_full, int stages, int i
   }
 }
 
+// Phase timestamps for latency studies, compiled out unless FO_PHASE_PROBE is defined:
+// %globaltimer (ns) at entry (slots 0 and 8), setup done (1), first stage full at the MMA
+// issuer (2), a unit's last MMA issued (3), its accumulator ready in the epilogue (4), all
+// stores complete (5), exit (6 and 7).  Slots 3 and 4 hold the CTA's last unit.  One row
+// of 16 per CTA.
+#ifdef FO_PHASE_PROBE
+static __device__ unsigned long long g_fo_probe[2048][16];
+#define FO_PROBE(slot, v) (g_fo_probe[blockIdx.x & 2047][slot] = (v))
+#else
+#define FO_PROBE(slot, v) ((void)0)
+#endif
+
 template <int BN, int ACT, int OUT_DT, bool LN, bool CONV, bool PAIR, bool SWAP = false, int KPS = 1>
 __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
     fo_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -309,10 +361,13 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
   constexpr int kCPC = 128 / kOutBytes;  // output columns per 128-byte chunk
   constexpr int kChunks = BN / kCPC;
   // Column halves of the epilogue: each half is taken by one warp of a lane quarter.  A
-  // 16-bit BN 64 tile is a single 128-byte store chunk, so only its first half has work.
-  constexpr int kHalves = SWAP ? 2 : (kChunks >= 2 ? 2 : 1);
-  constexpr int kHalfChunks = kChunks / kHalves;   // store chunks per half (non-swapped)
-  constexpr int kHalfCols = BN / kHalves;          // columns per half
+  // 16-bit BN 64 tile is a single 128-byte TMA store chunk; its two 32-column halves are
+  // stored directly from registers instead (kNarrow: each lane writes its row's 64 bytes).
+  constexpr bool kNarrow = !SWAP && kChunks == 1;
+  constexpr int kHalves = 2;
+  constexpr int kCW = kNarrow ? 32 : kCPC;                    // columns per epilogue step
+  constexpr int kHalfChunks = kNarrow ? 1 : kChunks / kHalves;  // steps per half (non-swapped)
+  constexpr int kHalfCols = BN / kHalves;                     // columns per half
   constexpr uint32_t kTmemCols = 2 * BN;
   static_assert(!LN || OUT_DT != DT_F32, "LayerNorm output is 16-bit");
 
@@ -327,15 +382,17 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
   static_assert(KPS == 1 || (KPS == 2 && !CONV), "two K slices per stage: GEMM family only");
   const uint32_t sB = sA + stages * kps * kAStageBytes;
   const uint32_t sEpi = sB + stages * kps * kBStage;
-  uint8_t* misc = smem + (sEpi - sA) + kEpiBytes;
+  uint8_t* misc = smem + (sEpi - sA) + epi_region_bytes(BN, PAIR ? 0 : p.csplit);
   // misc: [0,64) full[8] | [64,128) empty[8] | [128,144) tfull[2] | [144,160) tempty[2]
-  //       | [160,168) drain | [248,256) tmem addr + abort flag
+  //       | [160,168) drain | [168,176) red (cluster split) | [248,256) tmem addr + abort flag
   const uint32_t mb = smem_u32(misc);
   const uint32_t bar_full = mb;
   const uint32_t bar_empty = mb + 64;
   const uint32_t bar_tfull = mb + 128;
   const uint32_t bar_tempty = mb + 144;
   const uint32_t bar_drain = mb + 160;
+  const uint32_t bar_red = mb + 168;  // cluster split: every partial this CTA receives has landed
+  const int csplit = PAIR || CONV || LN ? 0 : p.csplit;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 248);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 252);
 
@@ -344,6 +401,10 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
   const uint32_t rank = PAIR ? cluster_ctarank() : 0;
   const int cid = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
   const int ncl = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  if (threadIdx.x == 0) {
+    FO_PROBE(0, global_timer_ns());
+    FO_PROBE(8, global_timer_ns());
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
@@ -355,8 +416,15 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
       mbar_init(bar_tempty + 8 * a, PAIR ? 2 * kEpiWarps : kEpiWarps);
     }
     mbar_init(bar_drain, 1);
+    if (csplit > 1) mbar_init(bar_red, 1);
     *abort_flag = 0;
     fence_mbar_init();
+    if (csplit > 1) {
+      // Expect every byte the other parts will send: the chunks this CTA owns, once each.
+      const int me = static_cast<int>(cluster_ctarank());
+      const int owned = (4 * (BN / 32) - me + csplit - 1) / csplit;
+      mbar_arrive_expect_tx(bar_red, static_cast<uint32_t>((csplit - 1) * owned * 32 * 128));
+    }
   }
   if (warp == kMmaWarp) {
     if constexpr (PAIR) {
@@ -374,12 +442,20 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
       tma_prefetch_desc(&tmB);
     }
   }
+  // Every warp reconverges before a CTA-wide barrier: bar.sync counts a warp whose
+  // lanes arrive at different times more than once, and would release the CTA early.
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
   if constexpr (PAIR) cluster_sync();  // both CTAs' barriers exist before any remote use
+  if (csplit > 1) cluster_sync();      // every receive barrier exists before any st.async
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const uint64_t tmo = p.timeout_ns;
+  // Launched as a programmatic dependent of the previous kernel on the stream: the setup
+  // above overlapped its tail; nothing below touches global memory before it completed.
+  griddep_wait();
+  if (threadIdx.x == 0) FO_PROBE(1, global_timer_ns());
 
   if (warp < kProducerWarps) {
     // ------------------------------------------------------------------ producer
@@ -638,6 +714,9 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
             break;
           }
           tc_fence_after();
+#ifdef FO_PHASE_PROBE
+          if (u == cid && kb0 == un.kb0) FO_PROBE(2, global_timer_ns());
+#endif
 #pragma unroll 2
           for (int i = 0; i < nk; ++i) {
             const uint64_t a = ad + static_cast<uint64_t>(i * (kAStageBytes >> 4));
@@ -671,6 +750,7 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
           }
         }
         if (!ok) break;
+        FO_PROBE(3, global_timer_ns());
         if constexpr (PAIR) {  // both halves of the accumulator are ready
           tc_commit_pair_both(bar_tfull + 8 * acc);
         } else {
@@ -699,7 +779,7 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
     const int ew = warp - kFirstEpiWarp;  // 0..7
     const int quarter = warp & 3;         // TMEM lane quarter this warp may access
     const int half = ew >> 2;             // column half of the tile this warp takes
-    const bool idle = half >= kHalves;    // (16-bit BN 64: the second half is empty)
+    constexpr bool idle = false;           // every warp has a column half
     const int hcol = half * kHalfCols;    // first tile column of this warp's half
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t buf0 = sEpi + ew * kEpiBufBytes;
@@ -711,11 +791,23 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
       const Unit un = unit_of(p, u);
       const int tm = un.tm, tn = un.tn;
       const bool has_k = un.kb1 > un.kb0;
+      // The tile's per-column vectors (bias, or the BatchNorm affine) do not depend on
+      // the accumulator: lane l loads columns hcol + 32 j + l before the wait, so their
+      // latency overlaps the MMAs instead of following them.
+      constexpr int kPre = SWAP ? 1 : kHalfCols / 32;
+      float2 aff[kPre];
+      if constexpr (!SWAP) {
+        if (!idle) {
+#pragma unroll
+          for (int j = 0; j < kPre; ++j) aff[j] = channel_affine(p, tn * BN + hcol + j * 32 + lane);
+        }
+      }
       if (!mbar_wait(bar_tfull + 8 * acc, acc_ph, tmo, abort_flag)) {
         ok = false;
         break;
       }
       tc_fence_after();
+      if (ew == 0 && lane == 0) FO_PROBE(4, global_timer_ns());
       if (idle) {
         __syncwarp();
         if (lane == 0) {
@@ -728,6 +820,118 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
         acc ^= 1;
         if (acc == 0) acc_ph ^= 1;
         continue;
+      }
+      if constexpr (!PAIR && !CONV && !LN) {
+        if (csplit > 1) {
+          // Cluster split.  This warp covers chunks gc = hcol/32 .. of its lane quarter;
+          // chunk g = quarter * BN/32 + gc belongs to rank g % csplit.  First push the
+          // partials of the chunks other ranks own into their receive areas, then reduce
+          // the owned chunks (parts added in rank order: bitwise reproducible).
+          const int me = static_cast<int>(cluster_ctarank());
+          constexpr int kG = BN / 32;
+          const int nown = csplit_owned_max(BN, csplit);
+#pragma unroll
+          for (int j = 0; j < kPre; ++j) {
+            const int gc = hcol / 32 + j;
+            const int g = quarter * kG + gc;
+            const int owner = g % csplit;
+            if (owner == me) continue;
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tmem_base + lane_off + acc * BN + gc * 32, r);
+            tc_wait_ld_regs(r);
+            if (!has_k) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) r[i] = 0u;
+            }
+            const int slot = (me < owner ? me : me - 1) * nown + g / csplit;
+            const uint32_t dst = mapa_shared(sEpi + slot * kRedChunkBytes + lane * kRedRowBytes, owner);
+            const uint32_t rbar = mapa_shared(bar_red, owner);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) st_async_v4(dst + 16 * i, r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3], rbar);
+          }
+          if (ew == 0 && lane == 0) FO_PROBE(12, global_timer_ns());
+          bool landed = false;
+          const int row = tm * kBM + quarter * 32 + lane;
+#pragma unroll
+          for (int j = 0; j < kPre; ++j) {
+            const int gc = hcol / 32 + j;
+            const int g = quarter * kG + gc;
+            if (g % csplit != me) continue;
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tmem_base + lane_off + acc * BN + gc * 32, r);
+            tc_wait_ld_regs(r);
+            if (!landed) {
+              if (!mbar_wait_cluster(bar_red, 0, tmo, abort_flag)) {
+                ok = false;
+                break;
+              }
+              landed = true;
+              if (lane == 0) FO_PROBE(13, global_timer_ns());
+            }
+            float t[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) t[i] = 0.f;
+            for (int k = 0; k < csplit; ++k) {
+              if (k == me) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) t[i] += has_k ? __uint_as_float(r[i]) : 0.f;
+              } else {
+                const int slot = (k < me ? k : k - 1) * nown + g / csplit;
+                const float4* src = reinterpret_cast<const float4*>(smem + (sEpi - sA) + slot * kRedChunkBytes +
+                                                                    lane * kRedRowBytes);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                  const float4 q4 = src[i];
+                  t[4 * i] += q4.x;
+                  t[4 * i + 1] += q4.y;
+                  t[4 * i + 2] += q4.z;
+                  t[4 * i + 3] += q4.w;
+                }
+              }
+            }
+            if (p.has_bias) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) t[i] += __shfl_sync(0xffffffffu, aff[j].y, i);
+            }
+#pragma unroll
+            for (int i = 0; i < 32; ++i) t[i] = apply_act<ACT>(t[i]);
+            const int cb = tn * BN + gc * 32;
+            if (row < p.M) {
+              char* dst = reinterpret_cast<char*>(p.out) + (static_cast<long long>(row) * p.ldo + cb) * kOutBytes;
+              if (cb + 32 <= p.N) {
+                if constexpr (OUT_DT == DT_F32) {
+#pragma unroll
+                  for (int i = 0; i < 8; ++i)
+                    reinterpret_cast<float4*>(dst)[i] = make_float4(t[4 * i], t[4 * i + 1], t[4 * i + 2], t[4 * i + 3]);
+                } else {
+#pragma unroll
+                  for (int i = 0; i < 4; ++i)
+                    reinterpret_cast<uint4*>(dst)[i] =
+                        make_uint4(pack2<OUT_DT>(t[8 * i], t[8 * i + 1]), pack2<OUT_DT>(t[8 * i + 2], t[8 * i + 3]),
+                                   pack2<OUT_DT>(t[8 * i + 4], t[8 * i + 5]), pack2<OUT_DT>(t[8 * i + 6], t[8 * i + 7]));
+                }
+              } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                  if (cb + i >= p.N) continue;
+                  if constexpr (OUT_DT == DT_F32) {
+                    reinterpret_cast<float*>(dst)[i] = t[i];
+                  } else {
+                    reinterpret_cast<unsigned short*>(dst)[i] = static_cast<unsigned short>(pack2<OUT_DT>(t[i], 0.f) & 0xFFFFu);
+                  }
+                }
+              }
+            }
+          }
+          if (!ok) break;
+          // Every TMEM load of this warp has completed: release the accumulator.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar_tempty + 8 * acc);
+          acc ^= 1;
+          if (acc == 0) acc_ph ^= 1;
+          continue;
+        }
       }
       // Split tile: publish this part's fp32 partial of the warp's (quarter, half)
       // ([column][128 rows], coalesced), then the warp whose arrival completes that
@@ -894,33 +1098,48 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
       }
       const int row0 = tm * kTileM + static_cast<int>(rank) * kBM + quarter * 32;
       const int col0 = tn * BN;
-#pragma unroll 1
-      for (int c = half * kHalfChunks; c < (half + 1) * kHalfChunks; ++c) {
-        const int cbase = col0 + c * kCPC;
-        float v[kCPC];
+#pragma unroll
+      for (int ci = 0; ci < kHalfChunks; ++ci) {
+        const int tc = hcol + ci * kCW;  // first tile column of this step
+        const int cbase = col0 + tc;
+        float v[kCW];
         {
-          uint32_t r0[32];
-          tmem_ld_32x32b_x32(tmem_base + lane_off + acc * BN + c * kCPC, r0);
+          // Both 32-column loads of a 64-column step are in flight before one wait.
+          uint32_t r0[32], r1[32];
+          tmem_ld_32x32b_x32(tmem_base + lane_off + acc * BN + tc, r0);
+          if constexpr (kCW == 64) tmem_ld_32x32b_x32(tmem_base + lane_off + acc * BN + tc + 32, r1);
           tc_wait_ld_regs(r0);
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = has_k ? __uint_as_float(r0[i]) : 0.f;
-          if constexpr (kCPC == 64) {
-            uint32_t r1[32];
-            tmem_ld_32x32b_x32(tmem_base + lane_off + acc * BN + c * kCPC + 32, r1);
-            tc_wait_ld_regs(r1);
+          if constexpr (kCW == 64) {
+            tc_pin_regs(r1);
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[32 + i] = has_k ? __uint_as_float(r1[i]) : 0.f;
           }
         }
         if (split_tile != nullptr) {
-          for (int q = 0; q < p.split; ++q) {
-            if (q == un.part) continue;
-            const float* other = split_tile + static_cast<long long>(q) * BN * 128 + quarter * 32 + lane;
+          // The parts are added in part order whichever part arrived last, so a split
+          // tile's result is bitwise reproducible from run to run.
 #pragma unroll
-            for (int i = 0; i < kCPC; ++i) v[i] += __ldcg(other + (c * kCPC + i) * 128);
+          for (int h = 0; h < kCW / 32; ++h) {
+            float t[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) t[i] = 0.f;
+            for (int q = 0; q < p.split; ++q) {
+              if (q == un.part) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) t[i] += v[h * 32 + i];
+              } else {
+                const float* other = split_tile + static_cast<long long>(q) * BN * 128 + quarter * 32 + lane;
+#pragma unroll
+                for (int i = 0; i < 32; ++i) t[i] += __ldcg(other + (tc + h * 32 + i) * 128);
+              }
+            }
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[h * 32 + i] = t[i];
           }
         }
-        if (c == (half + 1) * kHalfChunks - 1) {
+        if (ci == kHalfChunks - 1) {
           // The accumulator buffer is free once every lane's loads of it have completed.
           tc_fence_before();
           __syncwarp();
@@ -932,32 +1151,31 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
             }
           }
         }
-        if (p.bn_mode) {  // lane i folds column i's BatchNorm; shuffles broadcast it
+        if (p.bn_mode) {  // lane i holds column i's folded BatchNorm; shuffles broadcast it
 #pragma unroll
-          for (int h = 0; h < kCPC / 32; ++h) {
-            const float2 aff = channel_affine(p, cbase + h * 32 + lane);
+          for (int h = 0; h < kCW / 32; ++h) {
+            const float2 a2 = aff[ci * (kCW / 32) + h];
 #pragma unroll
             for (int i = 0; i < 32; ++i)
-              v[h * 32 + i] = fmaf(round_in(v[h * 32 + i], p.ab_bf16), __shfl_sync(0xffffffffu, aff.x, i),
-                                   __shfl_sync(0xffffffffu, aff.y, i));
+              v[h * 32 + i] = fmaf(round_in(v[h * 32 + i], p.ab_bf16), __shfl_sync(0xffffffffu, a2.x, i),
+                                   __shfl_sync(0xffffffffu, a2.y, i));
           }
         } else if (p.has_bias) {
 #pragma unroll
-          for (int h = 0; h < kCPC / 32; ++h) {
-            const int n = cbase + h * 32 + lane;
-            const float bl = n < p.N ? load_vec(p.bias, p.vec_dtype, n) : 0.f;
+          for (int h = 0; h < kCW / 32; ++h) {
+            const float bl = aff[ci * (kCW / 32) + h].y;
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[h * 32 + i] += __shfl_sync(0xffffffffu, bl, i);
           }
         }
         if constexpr (CONV && OUT_DT != DT_F32) {
-          // residual of the BN-add-ReLU epilogue: this lane's output row, kCPC columns
+          // residual of the BN-add-ReLU epilogue: this lane's output row, kCW columns
           const int row = row0 + lane;
           if (p.add_src != nullptr && row < p.M) {
             const unsigned short* ar = reinterpret_cast<const unsigned short*>(p.add_src) + row * p.ld_add + cbase;
-            if (cbase + kCPC <= p.N) {
+            if (cbase + kCW <= p.N) {
 #pragma unroll
-              for (int j = 0; j < kCPC / 8; ++j) {
+              for (int j = 0; j < kCW / 8; ++j) {
                 const uint4 q = __ldg(reinterpret_cast<const uint4*>(ar) + j);
                 const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
@@ -969,66 +1187,86 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
               }
             } else {
 #pragma unroll
-              for (int i = 0; i < kCPC; ++i)
+              for (int i = 0; i < kCW; ++i)
                 if (cbase + i < p.N) v[i] += load_vec(ar, OUT_DT, i);
             }
           }
         }
 #pragma unroll
-        for (int i = 0; i < kCPC; ++i) v[i] = apply_act<ACT>(v[i]);
+        for (int i = 0; i < kCW; ++i) v[i] = apply_act<ACT>(v[i]);
         if constexpr (LN) {
-          const int cv = min(kCPC, p.N - cbase);
+          const int cv = min(kCW, p.N - cbase);
           if (cv > 0) {
             float sum = 0.f;
 #pragma unroll
-            for (int i = 0; i < kCPC; ++i) sum += (i < cv) ? v[i] : 0.f;
+            for (int i = 0; i < kCW; ++i) sum += (i < cv) ? v[i] : 0.f;
             const float cm = sum / static_cast<float>(cv);
             float q = 0.f;
 #pragma unroll
-            for (int i = 0; i < kCPC; ++i) {
+            for (int i = 0; i < kCW; ++i) {
               const float d = v[i] - cm;
               q += (i < cv) ? d * d : 0.f;
             }
             chan_merge(st_cnt, st_mean, st_m2, static_cast<float>(cv), cm, q);
-            if (c == half * kHalfChunks) shift = cm;
+            if (ci == 0) shift = cm;
           }
           // Store x - shift: the bf16/fp16 rounding then scales with the row's spread,
           // not with its mean; the normaliser adds (shift - row mean) back in fp32.
 #pragma unroll
-          for (int i = 0; i < kCPC; ++i) v[i] -= shift;
+          for (int i = 0; i < kCW; ++i) v[i] -= shift;
         }
-        // Stage the 32 x 128 B block in swizzled shared memory, then TMA-store it.
-        const uint32_t buf = buf0;
-        if (nstore >= 1) {
-          if (lane == 0) bulk_wait_read<0>();
-          __syncwarp();
-        }
-        const uint32_t rowp = buf + lane * 128;
+        if constexpr (kNarrow) {
+          // 16-bit BN 64: lane l stores row row0 + l of this 32-column half, 64
+          // contiguous bytes, straight from registers.
+          const int row = row0 + lane;
+          if (row < p.M) {
+            unsigned short* dst = reinterpret_cast<unsigned short*>(p.out) + static_cast<long long>(row) * p.ldo + cbase;
+            if (cbase + 32 <= p.N) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          uint32_t w0, w1, w2, w3;
-          if constexpr (OUT_DT == DT_F32) {
-            w0 = __float_as_uint(v[4 * j + 0]);
-            w1 = __float_as_uint(v[4 * j + 1]);
-            w2 = __float_as_uint(v[4 * j + 2]);
-            w3 = __float_as_uint(v[4 * j + 3]);
-          } else {
-            w0 = pack2<OUT_DT>(v[8 * j + 0], v[8 * j + 1]);
-            w1 = pack2<OUT_DT>(v[8 * j + 2], v[8 * j + 3]);
-            w2 = pack2<OUT_DT>(v[8 * j + 4], v[8 * j + 5]);
-            w3 = pack2<OUT_DT>(v[8 * j + 6], v[8 * j + 7]);
+              for (int j = 0; j < 4; ++j)
+                reinterpret_cast<uint4*>(dst)[j] =
+                    make_uint4(pack2<OUT_DT>(v[8 * j + 0], v[8 * j + 1]), pack2<OUT_DT>(v[8 * j + 2], v[8 * j + 3]),
+                               pack2<OUT_DT>(v[8 * j + 4], v[8 * j + 5]), pack2<OUT_DT>(v[8 * j + 6], v[8 * j + 7]));
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (cbase + i < p.N) dst[i] = static_cast<unsigned short>(pack2<OUT_DT>(v[i], 0.f) & 0xFFFFu);
+            }
           }
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(rowp + ((j ^ (lane & 7)) << 4)),
-                       "r"(w0), "r"(w1), "r"(w2), "r"(w3)
-                       : "memory");
+        } else {
+          // Stage the 32 x 128 B block in swizzled shared memory, then TMA-store it.
+          const uint32_t buf = buf0;
+          if (nstore >= 1) {
+            if (lane == 0) bulk_wait_read<0>();
+            __syncwarp();
+          }
+          const uint32_t rowp = buf + lane * 128;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            uint32_t w0, w1, w2, w3;
+            if constexpr (OUT_DT == DT_F32) {
+              w0 = __float_as_uint(v[4 * j + 0]);
+              w1 = __float_as_uint(v[4 * j + 1]);
+              w2 = __float_as_uint(v[4 * j + 2]);
+              w3 = __float_as_uint(v[4 * j + 3]);
+            } else {
+              w0 = pack2<OUT_DT>(v[8 * j + 0], v[8 * j + 1]);
+              w1 = pack2<OUT_DT>(v[8 * j + 2], v[8 * j + 3]);
+              w2 = pack2<OUT_DT>(v[8 * j + 4], v[8 * j + 5]);
+              w3 = pack2<OUT_DT>(v[8 * j + 6], v[8 * j + 7]);
+            }
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(rowp + ((j ^ (lane & 7)) << 4)),
+                         "r"(w0), "r"(w1), "r"(w2), "r"(w3)
+                         : "memory");
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, buf, cbase, row0);
+            bulk_commit();
+          }
+          ++nstore;
         }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(&tmC, buf, cbase, row0);
-          bulk_commit();
-        }
-        ++nstore;
       }
       acc ^= 1;
       if (acc == 0) acc_ph ^= 1;
@@ -1046,13 +1284,25 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
       record_error(p, kStatusTimeout, 0x30);
       *abort_flag = 1;
     }
-    if (lane == 0) bulk_wait<0>();
+    // Only the staging buffers' reads must finish before the CTA exits; the stores
+    // themselves complete with the grid, before any later kernel on the stream runs.
+    if (lane == 0) bulk_wait_read<0>();
     __syncwarp();
+    if (ew == 0 && lane == 0) FO_PROBE(5, global_timer_ns());
   }
 
+  __syncwarp();  // the producer and MMA warps ran their loops on lane 0 alone
   tc_fence_before();
   __syncthreads();
   if constexpr (PAIR) cluster_sync();  // no CTA leaves while its peer may still use it
+  if (csplit > 1) cluster_sync();
+  if (threadIdx.x == 0) {
+    FO_PROBE(6, global_timer_ns());
+    FO_PROBE(7, global_timer_ns());
+  }
+  if (threadIdx.x == 5) FO_PROBE(9, global_timer_ns());
+  if (threadIdx.x == 32 * kMmaWarp) FO_PROBE(10, global_timer_ns());
+  if (threadIdx.x == 32 * kFirstEpiWarp) FO_PROBE(11, global_timer_ns());
   if (warp == kMmaWarp) {
     tc_fence_after();
     if constexpr (PAIR) {

@@ -9,6 +9,15 @@
 
 namespace fo {
 
+// Function attributes and occupancy queries enqueue nothing, but a global-mode stream
+// capture on another thread would refuse them: switch this thread to relaxed mode for
+// the one-time setup of a kernel so that a first call under capture stays legal.
+struct RelaxedCapture {
+  cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+  RelaxedCapture() { cudaThreadExchangeStreamCaptureMode(&mode); }
+  ~RelaxedCapture() { cudaThreadExchangeStreamCaptureMode(&mode); }
+};
+
 struct LaunchArgs {
   CUtensorMap tmA, tmB, tmC;
   KParams p;
@@ -17,6 +26,7 @@ struct LaunchArgs {
   cudaStream_t stream;
   bool pair;  // launch as clusters of two CTAs (block_m 256, tcgen05 cta_group::2)
   bool swap;  // conv: operand-swapped kernel (M = output channels, N = pixels)
+  int csplit;  // gemm: parts of a cluster split (clusters of csplit CTAs), 0 or 1 = none
 };
 
 template <int BN, int ACT, int OUT_DT, bool LN, bool CONV, bool PAIR, bool SWAP, int KPS>
@@ -28,22 +38,30 @@ cudaError_t launch_tc_k(const LaunchArgs& a) {
   cudaGetDevice(&dev);
   const uint64_t bit = 1ull << (dev & 63);
   if ((opted.load(std::memory_order_acquire) & bit) == 0) {
+    RelaxedCapture relaxed;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
     if (e != cudaSuccess) return e;
     opted.fetch_or(bit, std::memory_order_acq_rel);
   }
   constexpr int kThreads = CONV ? 416 : 320;  // producer(s) + MMA + 8 epilogue warps
+  // Every launch is a programmatic dependent of the previous kernel on the stream (the
+  // kernel waits on griddepcontrol before its first global access), so its CTAs set up
+  // on idle SMs while that kernel finishes.
+  cudaLaunchAttribute pdl;
+  pdl.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  pdl.val.programmaticStreamSerializationAllowed = 1;
   if constexpr (PAIR) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.grid, 1, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = a.smem;
     cfg.stream = a.stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1] = pdl;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     // A persistent grid larger than the number of co-resident pairs would leave a tail
@@ -51,6 +69,7 @@ cudaError_t launch_tc_k(const LaunchArgs& a) {
     static std::atomic<int> max_clusters[64];
     int mc = max_clusters[dev & 63].load(std::memory_order_relaxed);
     if (mc == 0) {
+      RelaxedCapture relaxed;
       if (cudaOccupancyMaxActiveClusters(&mc, kern, &cfg) != cudaSuccess || mc <= 0) {
         cudaGetLastError();
         mc = -1;
@@ -58,10 +77,49 @@ cudaError_t launch_tc_k(const LaunchArgs& a) {
       max_clusters[dev & 63].store(mc, std::memory_order_relaxed);
     }
     if (mc > 0 && static_cast<int>(cfg.gridDim.x) > 2 * mc) cfg.gridDim.x = 2 * mc;
+    cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, kern, a.tmA, a.tmB, a.tmC, a.p);
   } else {
-    kern<<<a.grid, kThreads, a.smem, a.stream>>>(a.tmA, a.tmB, a.tmC, a.p);
-    return cudaGetLastError();
+    if (a.csplit > 1) {
+      // Cluster split: every unit needs its own CTA and a cluster's CTAs run at once, so
+      // the grid must fit the co-resident clusters of this size (queried once per size).
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(a.grid, 1, 1);
+      cfg.blockDim = dim3(kThreads, 1, 1);
+      cfg.dynamicSmemBytes = a.smem;
+      cfg.stream = a.stream;
+      cudaLaunchAttribute attr[2];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = a.csplit;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      attr[1] = pdl;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      static std::atomic<int> max_clusters[64][9];
+      if (a.csplit > 8) return cudaErrorInvalidValue;  // portable cluster sizes only
+      std::atomic<int>& slot = max_clusters[dev & 63][a.csplit];
+      int mc = slot.load(std::memory_order_relaxed);
+      if (mc == 0) {
+        RelaxedCapture relaxed;
+        if (cudaOccupancyMaxActiveClusters(&mc, kern, &cfg) != cudaSuccess || mc <= 0) {
+          cudaGetLastError();
+          mc = -1;
+        }
+        slot.store(mc, std::memory_order_relaxed);
+      }
+      if (mc > 0 && a.grid > mc * a.csplit) return cudaErrorCooperativeLaunchTooLarge;
+      cfg.numAttrs = 2;
+      return cudaLaunchKernelEx(&cfg, kern, a.tmA, a.tmB, a.tmC, a.p);
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.grid, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = a.smem;
+    cfg.stream = a.stream;
+    cfg.attrs = &pdl;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, a.tmA, a.tmB, a.tmC, a.p);
   }
 }
 

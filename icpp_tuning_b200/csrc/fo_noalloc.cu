@@ -13,8 +13,8 @@
 //
 // Limits and rules:
 //   * the scratch holds FO_NOALLOC_LN_SCRATCH_BYTES (8 MiB); a problem whose statistics
-//     need more (fo_gemm_workspace_size > 8 MiB, e.g. M * ceil(N / block_n) > ~260k for
-//     block_n >= 128, whose statistics come in half-tile slices) is
+//     need more (fo_gemm_workspace_size > 8 MiB, e.g. M * ceil(N / block_n) > ~260k, the
+//     statistics coming in half-tile slices) is
 //     rejected with FO_EINVAL and a message naming both sizes;
 //   * every GPU that loads this library holds the 8 MiB array until the process exits;
 //   * every call shares the one array per device and it keeps the last call's contents;
@@ -83,11 +83,14 @@ int tmap(CUtensorMap* m, int dt, const void* base, uint64_t inner, uint64_t oute
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
   std::call_once(once, [] {
+    cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;  // legal under a capture
+    cudaThreadExchangeStreamCaptureMode(&mode);
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
       fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    cudaThreadExchangeStreamCaptureMode(&mode);
   });
   if (fn == nullptr) return say(FO_ECUDA, "cuTensorMapEncodeTiled unavailable");
   const CUtensorMapDataType t = dt == FO_DT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16

@@ -111,6 +111,33 @@ def torch_sdpa_bert(w: Dict[str, List[torch.Tensor]], head_num: int):
     return run
 
 
+def torch_native_bert(w: Dict[str, List[torch.Tensor]], head_num: int):
+    """The reference's unfused PyTorch formulation (evaluation/end2end.py:43-89): attention
+    as explicit scaled scores, a -10000 upper-triangular mask and softmax, then separate
+    matmul / bias / residual / layer_norm and matmul / bias / gelu ops."""
+    hidden = w["attr_output_kernel"][0].shape[0]
+
+    def run(x):
+        b, s, _ = x.shape
+        mask = torch.triu(torch.full((s, s), -10000.0, device=x.device), 1).to(x.dtype)
+        h = x
+        for layer in range(len(w["qkv"])):
+            inp = h
+            qkv = w["qkv"][layer] + w["qkv_bias"][layer]
+            q, k, v = (t.reshape(b, s, head_num, HEAD_SIZE).transpose(1, 2) for t in qkv.chunk(3, dim=-1))
+            att = torch.softmax(torch.matmul(q, k.transpose(-1, -2)) * (HEAD_SIZE ** -0.5) + mask, dim=-1)
+            ctx = torch.matmul(att, v).transpose(1, 2).reshape(b, s, hidden)
+            h = torch.matmul(ctx, w["attr_output_kernel"][layer]) + w["attr_output_bias"][layer]
+            h = F.layer_norm(h + inp, (hidden,), w["attr_ln_gamma"][layer], w["attr_ln_beta"][layer])
+            res = h
+            h = F.gelu(torch.matmul(h, w["inter_kernel"][layer]) + w["inter_bias"][layer])
+            h = torch.matmul(h, w["output_kernel"][layer]) + w["output_bias"][layer]
+            h = F.layer_norm(h + res, (hidden,), w["out_ln_gamma"][layer], w["out_ln_beta"][layer])
+        return h
+
+    return run
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description="BERT forward with B200 fused operators")
     ap.add_argument("--model", default="bert_base", choices=sorted(MODELS))
@@ -119,6 +146,8 @@ def main() -> None:
     ap.add_argument("--method", default="B200Fused", choices=["B200Fused", "TorchNative", "TorchSDPA"],
                     help="TorchNative: the reference's PyTorch formulation; TorchSDPA: this module's graph "
                          "with PyTorch ops at the fusion sites")
+    ap.add_argument("--cuda_graph", action="store_true",
+                    help="capture one forward into a CUDA graph and time its replays")
     args = ap.parse_args()
     heads, layers = MODELS[args.model]
     hidden = heads * HEAD_SIZE
@@ -130,9 +159,13 @@ def main() -> None:
     elif args.method == "TorchSDPA":
         runner, label = torch_sdpa_bert(w, heads), "Torch SDPA"
     else:
-        from oracle.end2end_ref import bert_forward  # the reference's PyTorch formulation
+        runner, label = torch_native_bert(w, heads), "Torch Native"
+    if args.cuda_graph:
+        from .graphs import CapturedStep
 
-        runner, label = (lambda t: bert_forward(w, t, heads, HEAD_SIZE)), "Torch Native"
+        with torch.no_grad():
+            runner = CapturedStep(runner, [x])
+        label += " (CUDA graph)"
     with torch.no_grad():
         for i in range(20):
             if i == 10:

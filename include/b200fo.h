@@ -77,8 +77,16 @@ typedef struct FoTileCfg {
   int32_t swap_ab;  /* conv2d only: 1 = compute Y^T = W^T X^T (M = 128 output channels,  */
                     /* N = block_n output pixels) so few-channel convs use wide MMAs     */
   int32_t split_k;  /* K split of the tiles that do not fill a whole wave of CTAs:        */
-                    /* 0 = automatic (parts of >= 16 k-blocks when under half a wave),    */
-                    /* 1 = never, s = 2..16 = s parts (needs the split workspace)         */
+                    /* 0 = automatic (by a cost model when under half a wave),            */
+                    /* 1 = never, s = 2..16 = s parts                                     */
+  int32_t split_mode; /* how split parts are reduced:                                     */
+                    /* 0 = automatic (cluster when eligible, else workspace),             */
+                    /* 1 = workspace: fp32 partials in the caller's zero-filled workspace */
+                    /*     (fo_gemm_workspace_size), the last-arriving part reduces,      */
+                    /* 2 = cluster: the s parts of a tile run as one thread-block cluster */
+                    /*     and reduce-scatter their partials through distributed shared   */
+                    /*     memory, no workspace (gemm with block_m 128, s <= 8, one wave, */
+                    /*     not with FO_EPI_BIAS_LN)                                       */
 } FoTileCfg;
 
 /* One GEMM-family call.  A[M,K] row-major (row stride lda elements).  B per b_layout

@@ -20,9 +20,10 @@ def test_gemm_block_k128(cfg, M, Nn, K, layout):
     g = gen(80)
     a = randn(g, M, K, scale=K ** -0.25)
     b = randn(g, *((K, Nn) if layout == "kn" else (Nn, K)), scale=K ** -0.25)
-    tile = N.tile_cfg(group_m=8, block_k=128, **cfg)
+    # whole tiles in both (a split would sum its parts in a different order)
+    tile = N.tile_cfg(group_m=8, block_k=128, split_k=1, **cfg)
     out = fused.gemm(*cuda(a, b), b_layout=layout, out_dtype=torch.float32, config=tile)
-    ref_cfg = N.tile_cfg(cfg["block_n"], 4 if cfg["block_n"] == 256 else 6, 8)
+    ref_cfg = N.tile_cfg(cfg["block_n"], 4 if cfg["block_n"] == 256 else 6, 8, split_k=1)
     same = fused.gemm(*cuda(a, b), b_layout=layout, out_dtype=torch.float32, config=ref_cfg)
     assert torch.equal(out, same)  # same K order per output element as block_k 64
     assert_close(out, R.gemm(a, b, layout, upcast=True), dict(atol=1e-4, rtol=1e-4))

@@ -32,3 +32,12 @@ def test_summary_statistics():
 def test_sweep_shapes():
     assert list(range(1, 128, 5))[-1] == 126 and len(range(1, 128, 5)) == 26
     assert len(fb.CONV_SHAPES) == 9
+
+
+def test_captured_step_rejects_host_inputs():
+    import torch
+
+    from icpp_tuning_b200.graphs import CapturedStep
+
+    with pytest.raises(ValueError):
+        CapturedStep(lambda t: t, [torch.zeros(4)])

@@ -95,3 +95,17 @@ def test_lcm_marginal_uniformity():
     for k, vals in pools.items():
         counts = {v: sum(1 for c in cfgs if c[k] == v) for v in vals}
         assert len(set(counts.values())) == 1
+
+
+def test_cluster_split_plan_mirror():
+    """The model's mirror of the library's automatic cluster split (plan_cluster_split plus
+    the fallback over sizes that do not all fit the GPU at once)."""
+    from icpp_tuning_b200.autotuner.tcgen05_model import _smem_bytes, cluster_split_plan, cluster_stages
+    from icpp_tuning_b200.autotuner.tcgen05_space import smem_bytes
+
+    assert _smem_bytes(128, 6, 1, 0) == smem_bytes(128, 6)
+    assert cluster_split_plan(12, 48, 1, 148, 64, 6) in (6, 8)  # 128 x 768 x 3072: a long K loop
+    assert cluster_split_plan(48, 12, 2, 148, 64, 4) == 0      # 128 x 3072 x 768: too little K
+    assert cluster_split_plan(100, 64, 1, 148, 64, 6) == 0     # more than half a wave of tiles
+    assert cluster_split_plan(6, 48, 1, 148, 128, 6) >= 2      # stages drop to fit the receive area
+    assert cluster_stages(128, 6, 1, 8) < 6
