@@ -66,6 +66,22 @@ cudaError_t launch_gemm_family(int bn, int act, int out_dt, const LaunchArgs& a)
 extern "C" int FO_PROBE_CAT(fo_probe_read_pair, FO_PAIR)(void* host, size_t bytes) {
   return static_cast<int>(cudaMemcpyFromSymbol(host, fo::g_fo_probe, bytes));
 }
+namespace {
+__global__ void fo_probe_stamp_kernel(int slot, int smem) {
+  extern __shared__ uint8_t pad[];
+  if (threadIdx.x == 0) {
+    fo::g_fo_probe[2047][slot] = fo::global_timer_ns();
+    if (smem > 0) pad[smem - 1] = 1;  // touch the requested shared memory, inside it
+  }
+}
+}  // namespace
+// One in-stream timestamp into row 2047, slot `slot`; smem > 0 asks for that much dynamic
+// shared memory (the carveout a kernel needs).
+extern "C" int FO_PROBE_CAT(fo_probe_stamp_pair, FO_PAIR)(int slot, int smem, void* stream) {
+  if (smem > 48 * 1024) cudaFuncSetAttribute(fo_probe_stamp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  fo_probe_stamp_kernel<<<1, 32, smem, static_cast<cudaStream_t>(stream)>>>(slot, smem);
+  return static_cast<int>(cudaGetLastError());
+}
 extern "C" int FO_PROBE_CAT(fo_probe_clear_pair, FO_PAIR)() {
   void* a = nullptr;
   if (cudaGetSymbolAddress(&a, fo::g_fo_probe) != cudaSuccess) return -1;

@@ -8,8 +8,8 @@
 // scratch memory for its per-row slice statistics, which those callers
 // cannot provide.  This entry point takes that scratch from a file-scope __device__
 // array of fixed size instead, and it allocates nothing: no cudaMalloc, no cudaFree, no
-// allocating library routine.  (fo_gemm also allocates a small status word on the first
-// call on a device; this path uses a static one as well.)
+// allocating library routine.  (Its device status word is a static array too, separate
+// from the one fo_device_status reads.)
 //
 // Limits and rules:
 //   * the scratch holds FO_NOALLOC_LN_SCRATCH_BYTES (8 MiB); a problem whose statistics
@@ -22,8 +22,8 @@
 //     reads), but calls whose executions overlap on the GPU (different streams, or other
 //     threads) race on the array -- serialise them;
 //   * the first call on a device resolves the array's device address with
-//     cudaGetSymbolAddress (once per device, with that device current); make that first
-//     call before any stream capture begins;
+//     cudaGetSymbolAddress (once per device, with that device current, in relaxed
+//     stream-capture mode, so that even a first call made under a capture is legal);
 //   * a bounded device-side wait that runs out is recorded in this path's own static
 //     status word, not in the one fo_device_status reads.
 #include <cuda.h>
@@ -63,11 +63,16 @@ int setup_device(int dev, void** scratch, int** status, int* sms) {
   if (g_scratch_ptr[dev] == nullptr) {
     void* s = nullptr;
     void* st = nullptr;
-    if (cudaGetSymbolAddress(&s, g_ln_scratch) != cudaSuccess) return say(FO_ECUDA, "cudaGetSymbolAddress(scratch) failed");
-    if (cudaGetSymbolAddress(&st, g_ln_status) != cudaSuccess) return say(FO_ECUDA, "cudaGetSymbolAddress(status) failed");
     int n = 0;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-      return say(FO_ECUDA, "cudaDeviceGetAttribute failed");
+    cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;  // queries only: legal under a capture
+    cudaThreadExchangeStreamCaptureMode(&mode);
+    const cudaError_t e1 = cudaGetSymbolAddress(&s, g_ln_scratch);
+    const cudaError_t e2 = cudaGetSymbolAddress(&st, g_ln_status);
+    const cudaError_t e3 = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cudaThreadExchangeStreamCaptureMode(&mode);
+    if (e1 != cudaSuccess) return say(FO_ECUDA, "cudaGetSymbolAddress(scratch) failed");
+    if (e2 != cudaSuccess) return say(FO_ECUDA, "cudaGetSymbolAddress(status) failed");
+    if (e3 != cudaSuccess) return say(FO_ECUDA, "cudaDeviceGetAttribute failed");
     g_scratch_ptr[dev] = s;
     g_status_ptr[dev] = static_cast<int*>(st);
     g_sm_count[dev] = n;

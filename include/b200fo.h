@@ -198,9 +198,9 @@ int fo_last_error(char* buf, size_t len);
  * statistics live in a static __device__ array of FO_NOALLOC_LN_SCRATCH_BYTES per GPU
  * instead, and nothing is allocated: no cudaMalloc, no cudaFree.  Problems needing more
  * scratch (fo_gemm_workspace_size > FO_NOALLOC_LN_SCRATCH_BYTES) fail with FO_EINVAL.
- * The first call on a device looks up the array's address (make it before any stream
- * capture).  All calls share the array: calls that overlap on the GPU race and must be
- * serialised.  Wait timeouts go to a private status word, not fo_device_status. */
+ * The first call on a device looks up the array's address (legal under a stream
+ * capture too).  All calls share the array: calls that overlap on the GPU race and must
+ * be serialised.  Wait timeouts go to a private status word, not fo_device_status. */
 int fo_gemm_bias_layernorm_noalloc(const FoGemmDesc* desc, const FoTileCfg* cfg, void* stream);
 
 /* Library version string, e.g. "b200fo 0.1.0 sm_100a abi 1". */
