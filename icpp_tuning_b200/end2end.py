@@ -61,9 +61,10 @@ class FusedBert:
         self.w, self.head_num = w, head_num
         hidden = w["attr_output_kernel"][0].shape[0]
         self.hidden = hidden
-        self.cfg_out, _ = select_best(gemm_bias_layernorm.DESCRIPTOR, M=tokens, N=hidden, K=hidden)
+        rln = gemm_bias_layernorm.RESIDUAL_DESCRIPTOR
+        self.cfg_out, _ = select_best(rln, M=tokens, N=hidden, K=hidden)
         self.cfg_up, _ = select_best(gemm_bias_act.DESCRIPTORS["gelu_erf"], M=tokens, N=4 * hidden, K=hidden)
-        self.cfg_down, _ = select_best(gemm_bias_layernorm.DESCRIPTOR, M=tokens, N=hidden, K=4 * hidden)
+        self.cfg_down, _ = select_best(rln, M=tokens, N=hidden, K=4 * hidden)
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         w, hn, hidden = self.w, self.head_num, self.hidden

@@ -57,6 +57,26 @@ class GemmBiasLayerNormDescriptor(Tcgen05Descriptor):
 DESCRIPTOR = GemmBiasLayerNormDescriptor()
 
 
+class GemmBiasResidualLayerNormDescriptor(Tcgen05Descriptor):
+    """FO_EPI_BIAS_RESIDUAL_LN (end2end.py:76-79, :84-87): a plain GEMM + bias kernel,
+    then a row pass adding the residual and normalising.  The row pass costs the same for
+    every tile config, so configs rank as the GEMM + bias kernel (split-K included, which
+    the in-kernel LayerNorm of DESCRIPTOR cannot use)."""
+
+    @property
+    def name(self) -> str:
+        return "gemm_bias_residual_layernorm"
+
+    def make_op_spec(self, raw_config=None, M=0, N=0, K=0, out_bytes: int = 2, **kw):
+        return make_matmul_spec(M=M, N=N, K=K, primitives=["bias_add"], output_element_bytes=out_bytes)
+
+    def get_raw_configs(self, K=0, **kw):
+        return get_gemm_configs(K)
+
+
+RESIDUAL_DESCRIPTOR = GemmBiasResidualLayerNormDescriptor()
+
+
 def build_fused_kernel(M: int, N: int, K: int, gemm_config: Optional[Dict[str, Any]] = None,
                        block_M_ln: int = 16, block_N_ln: int = 128, thread_num_ln: int = 128,
                        eps: float = 1e-5, out_dtype: torch.dtype = torch.float16, b_layout: str = "kn",

@@ -109,3 +109,15 @@ def test_cluster_split_plan_mirror():
     assert cluster_split_plan(100, 64, 1, 148, 64, 6) == 0     # more than half a wave of tiles
     assert cluster_split_plan(6, 48, 1, 148, 128, 6) >= 2      # stages drop to fit the receive area
     assert cluster_stages(128, 6, 1, 8) < 6
+
+
+def test_residual_layernorm_descriptor_ranks_split_configs():
+    """The residual LayerNorm runs a plain GEMM + bias kernel, which may split along K;
+    its descriptor ranks configs as that kernel (128-column tiles with a cluster split
+    for 1024 x 768 x 3072), unlike the in-kernel LayerNorm descriptor."""
+    from icpp_tuning_b200.autotuner.interface import select_best
+    from icpp_tuning_b200.gemm import gemm_bias_layernorm as G
+
+    assert G.RESIDUAL_DESCRIPTOR.name == "gemm_bias_residual_layernorm"
+    cfg, _ = select_best(G.RESIDUAL_DESCRIPTOR, M=1024, N=768, K=3072)
+    assert cfg["block_N"] == 128 and cfg["block_M"] == 128
