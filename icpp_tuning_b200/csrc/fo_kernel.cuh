@@ -95,7 +95,9 @@ struct KParams {
   // g (= quarter * BN/32 + column chunk) with g % s == rank, receives the other parts'
   // fp32 partials of them into shared memory (st.async) and runs their epilogue.
   int csplit;
-  float* split_ws;  // [split slot][part][BN columns][128 rows] fp32 partial accumulators
+  // [split slot][part][row quarter][column half][BN/2 columns][32 rows] fp32 partials:
+  // one contiguous block per (part, epilogue warp)
+  float* split_ws;
   int* split_cnt;   // [split slot][4 row quarters] arrival counters, self-resetting
                     // (a slot is a split tile's 128 rows: two per tile for CTA pairs)
 };
@@ -393,7 +395,8 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
   const uint32_t sEpi = sB + stages * kps * kBStage;
   uint8_t* misc = smem + (sEpi - sA) + epi_region_bytes(BN, PAIR ? 0 : p.csplit);
   // misc: [0,64) full[8] | [64,128) empty[8] | [128,144) tfull[2] | [144,160) tempty[2]
-  //       | [160,168) drain | [168,176) red (cluster split) | [248,256) tmem addr + abort flag
+  //       | [160,168) drain | [168,176) red (cluster split) | [176,240) staged[8] (split
+  //       partials, one per epilogue warp) | [248,256) tmem addr + abort flag
   const uint32_t mb = smem_u32(misc);
   const uint32_t bar_full = mb;
   const uint32_t bar_empty = mb + 64;
@@ -401,6 +404,7 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
   const uint32_t bar_tempty = mb + 144;
   const uint32_t bar_drain = mb + 160;
   const uint32_t bar_red = mb + 168;  // cluster split: every partial this CTA receives has landed
+  const uint32_t bar_staged = mb + 176;  // + 8 x epilogue warp: the other parts' partials are in smem
   const int csplit = PAIR || CONV || LN ? 0 : p.csplit;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 248);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 252);
@@ -426,6 +430,7 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
     }
     mbar_init(bar_drain, 1);
     if (csplit > 1) mbar_init(bar_red, 1);
+    for (int w = 0; w < kEpiWarps; ++w) mbar_init(bar_staged + 8 * w, 1);
     *abort_flag = 0;
     fence_mbar_init();
     if (csplit > 1) {
@@ -948,18 +953,25 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
       // (quarter, half) adds the other parts and runs the epilogue; the other warps
       // release the accumulator and move on.
       float* split_tile = nullptr;
+      // Every part's partial of this warp's block (the own one included), in part order:
+      // in shared memory when staged (kHalfCols x 32 floats apart), else in the workspace
+      // (8 blocks apart).  The sum is taken over these in part order, so a split tile is
+      // bitwise reproducible whichever part arrives last.
+      const float* parts_base = nullptr;
+      bool staged = false;
+      constexpr int kRegionFloats = kHalfCols * 32;  // one (part, quarter, half) block
       // split slot of this CTA's 128 rows (a CTA pair's tile has two)
       const int sti = PAIR ? un.st * 2 + static_cast<int>(rank) : un.st;
       if (un.st >= 0) {
         split_tile = p.split_ws + static_cast<long long>(sti) * p.split * BN * 128;
-        float* mine = split_tile + static_cast<long long>(un.part) * BN * 128 + quarter * 32 + lane;
+        float* mine = split_tile + static_cast<long long>((un.part * 4 + quarter) * 2 + half) * kRegionFloats + lane;
 #pragma unroll 1
-        for (int c = hcol / 32; c < (hcol + kHalfCols) / 32; ++c) {
+        for (int c = 0; c < kHalfCols / 32; ++c) {
           uint32_t r[32];
-          tmem_ld_32x32b_x32(tmem_base + lane_off + acc * BN + c * 32, r);
+          tmem_ld_32x32b_x32(tmem_base + lane_off + acc * BN + hcol + c * 32, r);
           tc_wait_ld_regs(r);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) __stcg(mine + (c * 32 + i) * 128, __uint_as_float(r[i]));
+          for (int i = 0; i < 32; ++i) __stcg(mine + (c * 32 + i) * 32, __uint_as_float(r[i]));
         }
         __threadfence();
         __syncwarp();
@@ -982,7 +994,41 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
         }
         __threadfence();
         if (lane == 0) p.split_cnt[sti * 8 + quarter * 2 + half] = 0;
+        // On the CTA's last unit (automatic plans give every split unit its own CTA, after
+        // all whole tiles) whose MMAs are complete, the pipeline ring is idle: each
+        // epilogue warp copies the other parts' blocks into its share of it with one bulk
+        // copy per part (deep in flight, where loads into registers kept ~4 KB per warp in
+        // flight and ran at ~30 GB/s per SM).  At most once per CTA, so its barrier runs
+        // one phase.
+        const int ring_share = (p.stages * kps * (kAStageBytes + kBStage) / kEpiWarps) & ~15;
+        const uint32_t need = static_cast<uint32_t>(p.split * kRegionFloats * 4);
+        staged = static_cast<int>(need) <= ring_share && u + ncl >= p.num_units;
+        const uint32_t dst = sA + ew * ring_share;
+        const uint32_t wbar = bar_staged + 8 * ew;
+        if (staged) {
+          if (lane == 0) {
+            fence_proxy_async_global();  // the parts' generic stores, seen by the bulk copies
+            mbar_arrive_expect_tx(wbar, need);
+            for (int q = 0; q < p.split; ++q)
+              bulk_load_g2s(dst + q * kRegionFloats * 4,
+                            split_tile + static_cast<long long>((q * 4 + quarter) * 2 + half) * kRegionFloats,
+                            kRegionFloats * 4, wbar);
+          }
+          // one phase per kernel: a CTA runs at most one split unit
+          if (!mbar_wait(wbar, 0, tmo, abort_flag)) {
+            ok = false;
+            break;
+          }
+          parts_base = reinterpret_cast<const float*>(smem + (dst - sA)) + lane;
+        } else {
+          parts_base = split_tile + static_cast<long long>((quarter * 2 + half) * kRegionFloats) + lane;
+        }
       }
+      // Column `col` (within the half) of part q of this warp's block.
+      auto part_value = [&](int q, int col) -> float {
+        if (staged) return parts_base[(q * kHalfCols + col) * 32];
+        return __ldcg(parts_base + static_cast<long long>(q) * 8 * kRegionFloats + col * 32);
+      };
       float st_cnt = 0.f, st_mean = 0.f, st_m2 = 0.f;
       float shift = 0.f;  // LayerNorm: the tile is stored centred on its first chunk's mean
       if constexpr (SWAP) {
@@ -1044,12 +1090,12 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
           float acc_v[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) acc_v[i] = has_k ? __uint_as_float(r[i]) : 0.f;
-          if (split_tile != nullptr) {
-            for (int qq = 0; qq < p.split; ++qq) {
-              if (qq == un.part) continue;
-              const float* other = split_tile + static_cast<long long>(qq) * BN * 128 + quarter * 32 + lane;
+          if (split_tile != nullptr) {  // every part, in part order (reproducible)
 #pragma unroll
-              for (int i = 0; i < 32; ++i) acc_v[i] += __ldcg(other + (c * 32 + i) * 128);
+            for (int i = 0; i < 32; ++i) acc_v[i] = 0.f;
+            for (int qq = 0; qq < p.split; ++qq) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) acc_v[i] += part_value(qq, c * 32 - hcol + i);
             }
           }
           if (p.bn_mode) {
@@ -1127,26 +1173,12 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
             for (int i = 0; i < 32; ++i) v[32 + i] = has_k ? __uint_as_float(r1[i]) : 0.f;
           }
         }
-        if (split_tile != nullptr) {
-          // The parts are added in part order whichever part arrived last, so a split
-          // tile's result is bitwise reproducible from run to run.
+        if (split_tile != nullptr) {  // every part, in part order (reproducible)
 #pragma unroll
-          for (int h = 0; h < kCW / 32; ++h) {
-            float t[32];
+          for (int i = 0; i < kCW; ++i) v[i] = 0.f;
+          for (int q = 0; q < p.split; ++q) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) t[i] = 0.f;
-            for (int q = 0; q < p.split; ++q) {
-              if (q == un.part) {
-#pragma unroll
-                for (int i = 0; i < 32; ++i) t[i] += v[h * 32 + i];
-              } else {
-                const float* other = split_tile + static_cast<long long>(q) * BN * 128 + quarter * 32 + lane;
-#pragma unroll
-                for (int i = 0; i < 32; ++i) t[i] += __ldcg(other + (tc + h * 32 + i) * 128);
-              }
-            }
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[h * 32 + i] = t[i];
+            for (int i = 0; i < kCW; ++i) v[i] += part_value(q, tc - hcol + i);
           }
         }
         if (ci == kHalfChunks - 1) {

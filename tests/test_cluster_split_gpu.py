@@ -122,3 +122,41 @@ def test_cluster_split_rejections():
     ws = torch.zeros(1 << 20, dtype=torch.uint8, device="cuda")
     assert _call(128, 512, 512, _cfg(64, 2), N.FO_EPI_BIAS_LN, ws) == N.FO_EINVAL  # in-kernel LayerNorm
     assert _call(128, 512, 512, _cfg(64, 2)) == N.FO_OK
+
+
+@pytest.mark.parametrize("bm,bn,st,s,max_ctas", [(128, 128, 6, 2, 0), (128, 64, 8, 3, 0), (256, 256, 4, 2, 0),
+                                                 (256, 128, 6, 3, 0), (128, 128, 6, 3, 16), (128, 256, 4, 4, 8)])
+def test_workspace_split_staged_and_fallback(bm, bn, st, s, max_ctas):
+    """Workspace split-K: the last-arriving part stages the other parts' blocks in the idle
+    pipeline ring with bulk copies (a CTA's only split unit), or reads them from L2 (a small
+    max_ctas gives CTAs several split units); both sum the parts in part order."""
+    M, Nn, K = 600, 1000, 2048
+    a, b, bias = _inputs(95, M, Nn, K, layout="nk")
+    cfg = N.tile_cfg(bn, st, 8, block_m=bm, max_ctas=max_ctas, split_k=s, split_mode=N.SPLIT_WORKSPACE)
+    ws = torch.zeros(fused.workspace_bytes(M, Nn, K, "bias_gelu_tanh", cfg), dtype=torch.uint8, device="cuda")
+    assert ws.numel() > 0
+    a, b, bias = a.cuda(), b.cuda(), bias.cuda()
+    outs = [fused.gemm(a, b, b_layout="nk", epilogue="bias_gelu_tanh", bias=bias, out_dtype=torch.float32,
+                       workspace=ws, config=cfg) for _ in range(3)]
+    assert_close(outs[0], R.gemm_bias_act(a.cpu(), b.cpu(), bias.cpu(), "gelu_tanh", "nk", upcast=True),
+                 dict(atol=2e-3, rtol=2e-3))
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    status_clean()
+
+
+def test_swapped_conv_split_is_reproducible():
+    g = gen(96)
+    x = randn(g, 2, 14, 14, 256).cuda()
+    w = randn(g, 3, 3, 256, 128, scale=(9 * 256) ** -0.5).cuda()
+    cfg = N.tile_cfg(256, 4, 0, swap_ab=1, split_k=3)
+    ws = torch.zeros(fused.conv_workspace_bytes(2, 14, 14, 256, 128, 3, 3, 1, 1, 1, config=cfg), dtype=torch.uint8,
+                     device="cuda")
+    assert ws.numel() > 0
+    outs = [fused.conv2d_nhwc(x, w, relu=True, stride=1, padding=1, workspace=ws, config=cfg, out_dtype=torch.float32)
+            for _ in range(3)]
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    ref = R.conv2d_bias_relu(x.cpu(), w.cpu(), None, True, out_dtype=torch.float32, upcast=True)  # NHWC
+    assert_close(outs[0], ref, dict(atol=2e-3, rtol=2e-3))
+    status_clean()
