@@ -171,6 +171,16 @@ def test_split_k_field():
     assert pair == 1024 + 16 * 2 * 3 * 128 * 256 * 4  # 16 pair tiles, 2 slots each, 3 parts
 
 
+def test_split_mode_field():
+    """split_mode: 0 automatic, 1 workspace, 2 cluster; anything else is rejected."""
+    for mode in (0, 1, 2):
+        assert N.config_legal(0, N.FO_DT_BF16, N.tile_cfg(128, 6, 8, split_k=2, split_mode=mode))[0]
+    for bad in (-1, 3):
+        ok, why = N.config_legal(0, N.FO_DT_BF16, N.tile_cfg(128, 6, 8, split_mode=bad))
+        assert not ok and "split_mode" in why
+    assert ctypes.sizeof(N.FoTileCfg) == 9 * 4  # the header's FoTileCfg: nine int32 fields
+
+
 def test_timeout_setting():
     with pytest.raises(N.FoError):
         N.set_wait_timeout_ns(0)
