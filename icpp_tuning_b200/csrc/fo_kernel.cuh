@@ -1001,7 +1001,10 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
         // flight and ran at ~30 GB/s per SM).  At most once per CTA, so its barrier runs
         // one phase.
         const int ring_share = (p.stages * kps * (kAStageBytes + kBStage) / kEpiWarps) & ~15;
-        const uint32_t need = static_cast<uint32_t>(p.split * kRegionFloats * 4);
+        // Two parts: own + other is one addition, the same bits in either order, so only the
+        // other part's block is staged (a 256-column half's 16 KB fits a warp's share).
+        const bool two = p.split == 2;
+        const uint32_t need = static_cast<uint32_t>((two ? 1 : p.split) * kRegionFloats * 4);
         staged = static_cast<int>(need) <= ring_share && u + ncl >= p.num_units;
         const uint32_t dst = sA + ew * ring_share;
         const uint32_t wbar = bar_staged + 8 * ew;
@@ -1009,10 +1012,12 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
           if (lane == 0) {
             fence_proxy_async_global();  // the parts' generic stores, seen by the bulk copies
             mbar_arrive_expect_tx(wbar, need);
-            for (int q = 0; q < p.split; ++q)
-              bulk_load_g2s(dst + q * kRegionFloats * 4,
+            for (int q = 0; q < p.split; ++q) {
+              if (two && q == un.part) continue;
+              bulk_load_g2s(dst + (two ? 0 : q) * kRegionFloats * 4,
                             split_tile + static_cast<long long>((q * 4 + quarter) * 2 + half) * kRegionFloats,
                             kRegionFloats * 4, wbar);
+            }
           }
           // one phase per kernel: a CTA runs at most one split unit
           if (!mbar_wait(wbar, 0, tmo, abort_flag)) {
@@ -1028,6 +1033,11 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
       auto part_value = [&](int q, int col) -> float {
         if (staged) return parts_base[(q * kHalfCols + col) * 32];
         return __ldcg(parts_base + static_cast<long long>(q) * 8 * kRegionFloats + col * 32);
+      };
+      // Two parts: column `col` of the other part's block.
+      auto other_value = [&](int col) -> float {
+        if (staged) return parts_base[col * 32];
+        return __ldcg(parts_base + static_cast<long long>(1 - un.part) * 8 * kRegionFloats + col * 32);
       };
       float st_cnt = 0.f, st_mean = 0.f, st_m2 = 0.f;
       float shift = 0.f;  // LayerNorm: the tile is stored centred on its first chunk's mean
@@ -1090,7 +1100,10 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
           float acc_v[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) acc_v[i] = has_k ? __uint_as_float(r[i]) : 0.f;
-          if (split_tile != nullptr) {  // every part, in part order (reproducible)
+          if (split_tile != nullptr && p.split == 2) {  // own + other: either order, same bits
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc_v[i] += other_value(c * 32 - hcol + i);
+          } else if (split_tile != nullptr) {  // every part, in part order (reproducible)
 #pragma unroll
             for (int i = 0; i < 32; ++i) acc_v[i] = 0.f;
             for (int qq = 0; qq < p.split; ++qq) {
@@ -1173,7 +1186,10 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
             for (int i = 0; i < 32; ++i) v[32 + i] = has_k ? __uint_as_float(r1[i]) : 0.f;
           }
         }
-        if (split_tile != nullptr) {  // every part, in part order (reproducible)
+        if (split_tile != nullptr && p.split == 2) {  // own + other: either order, same bits
+#pragma unroll
+          for (int i = 0; i < kCW; ++i) v[i] += other_value(tc - hcol + i);
+        } else if (split_tile != nullptr) {  // every part, in part order (reproducible)
 #pragma unroll
           for (int i = 0; i < kCW; ++i) v[i] = 0.f;
           for (int q = 0; q < p.split; ++q) {
