@@ -65,6 +65,14 @@ class FusedBert:
         self.cfg_out, _ = select_best(rln, M=tokens, N=hidden, K=hidden)
         self.cfg_up, _ = select_best(gemm_bias_act.DESCRIPTORS["gelu_erf"], M=tokens, N=4 * hidden, K=hidden)
         self.cfg_down, _ = select_best(rln, M=tokens, N=hidden, K=4 * hidden)
+        # One zero-filled split-K workspace for the three sites (they run in order on one
+        # stream, and the library leaves it zeroed): lets tiles of a partial wave split
+        # along K when a cluster split does not apply.
+        dev = w["attr_output_kernel"][0].device
+        need = max(fused.workspace_bytes(tokens, hidden, hidden, "bias", self.cfg_out),
+                   fused.workspace_bytes(tokens, 4 * hidden, hidden, "bias_gelu_erf", self.cfg_up),
+                   fused.workspace_bytes(tokens, hidden, 4 * hidden, "bias", self.cfg_down))
+        self.ws = torch.zeros(max(16, need), dtype=torch.uint8, device=dev)
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         w, hn, hidden = self.w, self.head_num, self.hidden
@@ -77,13 +85,13 @@ class FusedBert:
             ctx = F.scaled_dot_product_attention(q, k, v, is_causal=True).transpose(1, 2).reshape(b * s, hidden)
             h = fused.gemm(ctx, w["attr_output_kernel"][layer], epilogue="bias_residual_layernorm",
                            bias=w["attr_output_bias"][layer], gamma=w["attr_ln_gamma"][layer],
-                           beta=w["attr_ln_beta"][layer], residual=inp, config=self.cfg_out)
+                           beta=w["attr_ln_beta"][layer], residual=inp, config=self.cfg_out, workspace=self.ws)
             res = h
             u = fused.gemm(h, w["inter_kernel"][layer], epilogue="bias_gelu_erf", bias=w["inter_bias"][layer],
-                           config=self.cfg_up)
+                           config=self.cfg_up, workspace=self.ws)
             h = fused.gemm(u, w["output_kernel"][layer], epilogue="bias_residual_layernorm",
                            bias=w["output_bias"][layer], gamma=w["out_ln_gamma"][layer], beta=w["out_ln_beta"][layer],
-                           residual=res, config=self.cfg_down)
+                           residual=res, config=self.cfg_down, workspace=self.ws)
         return h.reshape(b, s, hidden)
 
 
