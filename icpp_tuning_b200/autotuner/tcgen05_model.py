@@ -56,6 +56,7 @@ CONSTANTS = {
     # of a tiled load's rate: measured 589 vs 836 TFLOP/s for BN=128 conv vs GEMM tiles
     "im2col_rate": 0.7,
     "fixed_s": 6.0e-6,  # launch + TMEM alloc + pipeline fill + last epilogue
+    "pair_fixed_s": 1.0e-6,  # extra fixed cost of a CTA-pair launch (cluster start and exit)
     "split_overhead_s": 2.0e-6,  # partial write -> fence -> atomic -> reduce chain
     # the last-arriving CTA reads each other part's fp32 partial (128 x bn x 4 B) at this rate
     "split_read_bytes_per_s": 30e9,
@@ -142,7 +143,7 @@ def cluster_split_plan(tiles: int, k_blocks: int, kps: int, cap: int, bn: int, s
         if tiles * s > cap or s > nst or cluster_stages(bn, stages, kps, s) == 0:
             continue
         t = -(-nst // s) * kps * t_kb + c0 + c1 * s
-        if t < 0.9 * t1:
+        if t < 0.8 * t1:
             cands.append((t, s))
     for _, s in sorted(cands):
         if tiles <= K["cluster_capacity"].get(s, 0):
@@ -253,7 +254,7 @@ def _model(op: OpSpec, c: TuneConfig, hw: GPUSpec) -> dict:
     e_red = t_work / (t_work + t_ln)
     # -- parallel: SM-time used by the persistent grid, plus fixed cost
     quant = tiles / float(waves * sms)
-    t_comp = t_work + t_ln + K["fixed_s"]
+    t_comp = t_work + t_ln + K["fixed_s"] + (K["pair_fixed_s"] if pair else 0.0)
     e_par = quant * (t_work + t_ln) / t_comp
     # -- memory: HBM time of the operand traffic against the compute time
     traffic = _traffic_bytes(op, c, hw, ctas)

@@ -312,7 +312,7 @@ SplitPlan plan_split(int tiles, int k_blocks, int cap, bool allow, int forced = 
 // are bound by load latency, not by the tensor pipe), and (c0, c1) = (0.9, 0.32),
 // (1.9, 0.5), (2.3, 1.1) us for block_n 64, 128, 256 is the cluster's start, the
 // exchange of (s - 1) / s of the tile's fp32 partials and the exit (the exchanged bytes
-// grow with block_n).  A split must beat the unsplit tile by 10%.  Every part holds at
+// grow with block_n).  A split must beat the unsplit tile by 20%.  Every part holds at
 // least one stage and the shared memory of a CTA (pipeline + receive area) must fit
 // 227 KB: a part's short K loop needs no deep pipeline, so the stages drop (not below
 // 2) until it does (cluster_stages).  forced = s >= 2 asks for exactly s parts.  Fills
@@ -349,7 +349,7 @@ int plan_cluster_split(int tiles, int k_blocks, int kps, int cap, int bn, int st
   for (int s = 2; s <= 8; ++s) {
     if (!fits(s)) continue;
     const double t = (nst + s - 1) / s * kps * t_kb + c0 + c1 * s;
-    if (t >= 0.9 * t1) continue;
+    if (t >= 0.8 * t1) continue;
     int k = n++;
     while (k > 0 && cost[k - 1] > t) {  // insertion: best first
       cost[k] = cost[k - 1];
