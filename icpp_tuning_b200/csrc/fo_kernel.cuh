@@ -10,9 +10,10 @@
 //   mma       : one thread issues tcgen05.mma (M=128, N=BN, K=16) into one of two TMEM
 //               accumulators (2 x BN fp32 columns), so the epilogue of tile i overlaps
 //               the mainloop of tile i+1.
-//   epilogue  : four warps (one per TMEM lane quarter) read the accumulator with
-//               tcgen05.ld, apply bias / activation in fp32, convert, stage 32 x 128 B
-//               blocks in 128B-swizzled shared memory and write them with TMA stores.
+//   epilogue  : eight warps (two per TMEM lane quarter, one per column half) read the
+//               accumulator with tcgen05.ld, apply bias / activation in fp32, convert,
+//               stage 32 x 128 B blocks in 128B-swizzled shared memory and write them
+//               with TMA stores (16-bit 64-column tiles store from registers).
 //               For LayerNorm each thread owns one output row, so exact per-row
 //               (mean, M2) of the fp32 tile slice is a register reduction; the slice
 //               is stored centred on a shift and a row pass (next on the stream:
