@@ -145,11 +145,13 @@ def test_workspace_split_staged_and_fallback(bm, bn, st, s, max_ctas):
     status_clean()
 
 
-def test_swapped_conv_split_is_reproducible():
+@pytest.mark.parametrize("parts", [2, 3])
+def test_swapped_conv_split_is_reproducible(parts):
+    """2 parts: own + other (staged); 3 parts: every part in part order."""
     g = gen(96)
     x = randn(g, 2, 14, 14, 256).cuda()
     w = randn(g, 3, 3, 256, 128, scale=(9 * 256) ** -0.5).cuda()
-    cfg = N.tile_cfg(256, 4, 0, swap_ab=1, split_k=3)
+    cfg = N.tile_cfg(256, 4, 0, swap_ab=1, split_k=parts)
     ws = torch.zeros(fused.conv_workspace_bytes(2, 14, 14, 256, 128, 3, 3, 1, 1, 1, config=cfg), dtype=torch.uint8,
                      device="cuda")
     assert ws.numel() > 0
