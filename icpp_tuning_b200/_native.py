@@ -39,7 +39,7 @@ class FoTileCfg(ctypes.Structure):
     _fields_ = [("block_m", ctypes.c_int32), ("block_n", ctypes.c_int32),
                 ("block_k", ctypes.c_int32), ("stages", ctypes.c_int32),
                 ("group_m", ctypes.c_int32), ("max_ctas", ctypes.c_int32), ("swap_ab", ctypes.c_int32),
-                ("split_k", ctypes.c_int32), ("split_mode", ctypes.c_int32)]
+                ("split_k", ctypes.c_int32), ("split_mode", ctypes.c_int32), ("ln_mode", ctypes.c_int32)]
 
 
 class FoGemmDesc(ctypes.Structure):
@@ -145,12 +145,13 @@ def launch_count() -> int:
 
 
 SPLIT_AUTO, SPLIT_WORKSPACE, SPLIT_CLUSTER = 0, 1, 2
+LN_AUTO, LN_TWO_KERNELS, LN_ONE_KERNEL = 0, 1, 2
 
 
 def tile_cfg(block_n: int = 256, stages: int = 4, group_m: int = 8, max_ctas: int = 0,
              block_m: int = 128, block_k: int = 64, swap_ab: int = 0, split_k: int = 0,
-             split_mode: int = 0) -> FoTileCfg:
-    return FoTileCfg(block_m, block_n, block_k, stages, group_m, max_ctas, swap_ab, split_k, split_mode)
+             split_mode: int = 0, ln_mode: int = 0) -> FoTileCfg:
+    return FoTileCfg(block_m, block_n, block_k, stages, group_m, max_ctas, swap_ab, split_k, split_mode, ln_mode)
 
 
 def config_legal(op: int, out_dtype: int, cfg: FoTileCfg) -> tuple[bool, str]:

@@ -132,7 +132,7 @@ class TuneConfig:
 
     kind "simt" is the reference's register-tiled kernel; kind "tcgen05" is this
     package's sm_100a kernel, where block_M is the tcgen05 M (128), block_K one
-    128-byte swizzle row (64), num_warps the fixed role split (6 gemm, 9 conv),
+    128-byte swizzle row (64), num_warps the fixed role split (10 gemm, 13 conv),
     group_size_m the tile raster (0 = row-major) and max_ctas the persistent grid cap
     (0 = one CTA per SM).
     """

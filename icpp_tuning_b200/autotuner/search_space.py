@@ -35,9 +35,9 @@ _TILELANG_CONV2D_PARAMS = {"block_M": [32, 48, 64, 96, 128], "block_N": [32, 64,
 # sm_100a kernels: tcgen05 M = 128 (one CTA) or 256 (a CTA pair, cta_group::2), one
 # 128-byte swizzle row of K, fixed role split.
 _TCGEN05_MATMUL_PARAMS = {"block_M": [128, 256], "block_N": [64, 128, 256], "block_K": [64],
-                          "num_stages": [2, 3, 4, 5, 6, 7, 8], "num_warps": [6], "group_size_m": [0, 8, 16]}
+                          "num_stages": [2, 3, 4, 5, 6, 7, 8], "num_warps": [10], "group_size_m": [0, 8, 16]}
 _TCGEN05_CONV2D_PARAMS = {"block_M": [128, 256], "block_N": [64, 128, 256], "block_K": [64],
-                          "num_stages": [3, 4, 5, 6, 7, 8], "num_warps": [9], "group_size_m": [0]}
+                          "num_stages": [3, 4, 5, 6, 7, 8], "num_warps": [13], "group_size_m": [0]}
 
 MIN_OCCUPANCY_THRESHOLD = 0.2
 _KEYS = ("block_M", "block_N", "block_K", "num_stages", "num_warps", "group_size_m")

@@ -3,8 +3,8 @@
 A raw config is the dict the operator modules pass to the kernel (and that
 `select_best` returns): block_M (tcgen05 M = 128, or 256 for a CTA pair), block_N (64 /
 128 / 256), block_K (64 = one 128-byte swizzle row of 16-bit elements per stage, or 128 =
-two), num_stages, thread_num (6 warps for
-GEMMs, 9 for conv: producer / MMA / 4 epilogue) and group_m (tile raster).  Legality is
+two), num_stages, thread_num (10 warps for
+GEMMs: producer / MMA / 8 epilogue; 13 for conv: 4 producer warps) and group_m (tile raster).  Legality is
 the C ABI's (fo_query_config_legal): shared memory <= 227 KB, TMEM <= 512 columns.
 """
 from __future__ import annotations
@@ -14,8 +14,8 @@ from typing import Any, Dict, List, Sequence
 from .cost_model import TuneConfig
 from .interface import TileLangKernelBase
 
-GEMM_THREADS = 192
-CONV_THREADS = 288
+GEMM_THREADS = 320
+CONV_THREADS = 416
 SMEM_LIMIT = 232448
 
 

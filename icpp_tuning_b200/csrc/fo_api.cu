@@ -212,6 +212,8 @@ int check_cfg(int op, int out_dtype, const FoTileCfg* cfg, char* why, size_t why
   if (cfg->split_k < 0 || cfg->split_k > 16) return say("split_k must be 0 (automatic) .. 16, got %d", cfg->split_k);
   if (cfg->split_mode < 0 || cfg->split_mode > 2)
     return say("split_mode must be 0 (automatic), 1 (workspace) or 2 (cluster), got %d", cfg->split_mode);
+  if (cfg->ln_mode < 0 || cfg->ln_mode > 2)
+    return say("ln_mode must be 0 (automatic), 1 (two kernels) or 2 (one kernel), got %d", cfg->ln_mode);
   // (the direct conv's shared memory depends on the image width: fo_conv2d checks it)
   const int smem = fo::smem_bytes_for(cfg->block_n, cfg->stages, cfg->block_m == 256, cfg->block_k / 64);
   if (cfg->swap_ab != 2 && smem > 232448) return say("shared memory %d B exceeds the 227 KB per-block limit", smem);
@@ -384,14 +386,17 @@ int sm_count_or_default() {
   return 148;
 }
 
-// LayerNorm statistics: one float4 per row per slice, a slice being the column half of
-// an N tile that one epilogue warp covers.
+// LayerNorm workspace: the one-kernel path's counters (arrivals and finished
+// normalisers per 32-row group, zero-filled, left zeroed), then the statistics: one
+// float4 (two kernels) or float2 (one kernel) per row per slice, a slice being the
+// column half of an N tile that one epilogue warp covers.
 int ln_halves(int) { return 2; }
 
+size_t ln_header_bytes(int64_t M) { return round_up(static_cast<size_t>((M + 31) / 32) * 2 * sizeof(int), 256); }
+
 size_t ln_workspace(int64_t M, int64_t N, int bn) {
-  const int64_t tiles_m = (M + 127) / 128;
   const int64_t slices = (N + bn - 1) / bn * ln_halves(bn);
-  return round_up(static_cast<size_t>(tiles_m) * 4, 256) + static_cast<size_t>(slices * M) * 16;
+  return ln_header_bytes(M) + static_cast<size_t>(slices * M) * 16;
 }
 
 void fill_common(fo::KParams& p, const DevInfo& di) {
@@ -409,7 +414,7 @@ void fo::set_last_error(int code, const char* msg) {
 
 extern "C" {
 
-const char* fo_version(void) { return "b200fo 0.1.0 sm_100a abi 1"; }
+const char* fo_version(void) { return "b200fo 0.2.0 sm_100a abi 2"; }
 
 uint64_t fo_launch_count(void) { return g_launches.load(); }
 
@@ -542,8 +547,11 @@ int fo_gemm(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
   p.residual = d->residual;
   p.ldr = d->ldr;
   if (ln) {
-    p.ln_stats = reinterpret_cast<float4*>(static_cast<char*>(d->workspace) +
-                                           round_up(static_cast<size_t>((p.M + 127) / 128) * 4, 256));
+    char* ws = static_cast<char*>(d->workspace);
+    p.ln_cnt = reinterpret_cast<int*>(ws);
+    p.ln_groups = (p.M + 31) / 32;
+    p.ln_stats = reinterpret_cast<float4*>(ws + ln_header_bytes(p.M));
+    p.ln_st2 = reinterpret_cast<float2*>(ws + ln_header_bytes(p.M));
   }
   fill_common(p, di);
 
@@ -622,10 +630,34 @@ int fo_gemm(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
     }
     la.grid = pair ? 2 * pl.grid : pl.grid;
     la.smem = fo::smem_bytes_for(bn, cfg->stages, pair, p.kps);
-    e = launch();
+    if (ln && cfg->ln_mode != 1) {
+      // One kernel when the epilogue stages 128-byte chunks (block_n >= 128) and every
+      // row block's tiles lie within kLnMaxDefer waves of units of the raster.
+      const int span = p.group_m > 0 ? (p.group_m < p.tiles_m ? p.group_m : p.tiles_m) * (p.tiles_n - 1)
+                                     : p.tiles_n - 1;
+      const bool eligible = bn >= 128 && fo::ln_defer_for(span, pl.grid) <= fo::kLnMaxDefer;
+      if (cfg->ln_mode == 2 && !eligible)
+        return fail(FO_EINVAL, "one-kernel LayerNorm needs block_n >= 128 and each row block's %d tiles within %d "
+                    "waves of the tile raster (use group_m 0 or ln_mode 1)", p.tiles_n, fo::kLnMaxDefer);
+      if (eligible) {
+        p.ln_fused = 1;
+        p.ln_span = span;
+        la.coop = true;
+        e = launch();
+        if (e != cudaSuccess && cfg->ln_mode == 2)
+          return fail(FO_ECUDA, "one-kernel LayerNorm launch failed: %s", cudaGetErrorString(e));
+        if (e != cudaSuccess) {  // automatic: the two-kernel path instead
+          cudaGetLastError();
+          p.ln_fused = 0;
+          p.ln_span = 0;
+          la.coop = false;
+        }
+      }
+    }
+    if (!p.ln_fused) e = launch();
   }
   if (e != cudaSuccess) return fail(FO_ECUDA, "kernel launch failed: %s", cudaGetErrorString(e));
-  g_launches.fetch_add(ln || rln ? 2 : 1);  // LayerNorm: GEMM kernel + row kernel
+  g_launches.fetch_add((ln && !p.ln_fused) || rln ? 2 : 1);  // two-kernel LayerNorm: GEMM + row kernel
   return ok();
 }
 

@@ -1,5 +1,7 @@
-// Instantiations of the GEMM + bias + LayerNorm kernels (16-bit outputs): the tcgen05
-// kernel writes the biased rows and per-slice statistics, fo_ln_normalize_kernel follows.
+// Instantiations of the GEMM + bias + LayerNorm kernels (16-bit outputs).  One kernel
+// (p.ln_fused): the tcgen05 kernel normalises its own stored slices once their rows'
+// statistics are complete.  Two kernels: it writes the biased rows and per-slice
+// statistics, and a row pass (fo_ln_normalize_kernel or fo_ln_rows_kernel) follows.
 #include "fo_launch.cuh"
 
 namespace fo {
@@ -60,7 +62,7 @@ static cudaError_t gemm_then_normalize(const LaunchArgs& a) {
   } else {
     e = a.pair ? cudaErrorInvalidValue : launch_tc<BN, ACT_NONE, OUT, true, false, false>(a);
   }
-  if (e != cudaSuccess) return e;
+  if (e != cudaSuccess || a.p.ln_fused) return e;  // one kernel: no row pass
   // The statistics come in slices of half a tile (one per epilogue warp): the row pass
   // merges tiles_n x 2 slices of BN / 2 columns.
   constexpr int kHalves = 2;

@@ -45,6 +45,12 @@ constexpr int kEpiBufBytes = 32 * 128;
 constexpr int kEpiBytes = kEpiWarps * kEpiBufBytes;
 constexpr int kMiscBytes = 1536;
 constexpr int kMaxStages = 8;
+// One-kernel LayerNorm: most units a slice may wait, after its own, for its rows'
+// statistics (the host takes the two-kernel path when the tile raster needs more).
+constexpr int kLnMaxDefer = 3;
+__host__ __device__ constexpr int ln_defer_for(int span, int ncl) {
+  return ncl <= 0 ? 1 << 20 : (span + ncl - 1) / ncl < 1 ? 1 : (span + ncl - 1) / ncl;
+}
 
 // Status codes written into the device status word (first writer wins).
 constexpr int kStatusTimeout = 5;
@@ -101,6 +107,17 @@ struct KParams {
   float* split_ws;
   int* split_cnt;   // [split slot][4 row quarters] arrival counters, self-resetting
                     // (a slot is a split tile's 128 rows: two per tile for CTA pairs)
+  // One-kernel LayerNorm (ln_fused = 1; launched cooperatively, every CTA resident): each
+  // epilogue warp publishes the (mean, M2) of its row slice to ln_st2[slice][row] and
+  // counts itself into ln_cnt[row / 32]; some units later, when every slice of its 32
+  // rows has arrived, the same warp reads its stored slice back and normalises it in
+  // place.  ln_cnt holds 2 x ln_groups int32 (arrivals, then finished normalisers),
+  // zero at launch and reset to zero by the last normaliser of each group.
+  int ln_fused;
+  int ln_span;    // largest unit distance between two tiles of one row block
+  int ln_groups;  // ceil(M / 32)
+  int* ln_cnt;
+  float2* ln_st2;
 };
 
 __host__ __device__ constexpr int b_stage_bytes(int bn) { return bn * kBK * 2; }
@@ -398,6 +415,7 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
   // misc: [0,64) full[8] | [64,128) empty[8] | [128,144) tfull[2] | [144,160) tempty[2]
   //       | [160,168) drain | [168,176) red (cluster split) | [176,240) staged[8] (split
   //       partials, one per epilogue warp) | [248,256) tmem addr + abort flag
+  //       | [256,320) lnld[8] (one-kernel LayerNorm: a stored slice read back, per warp)
   const uint32_t mb = smem_u32(misc);
   const uint32_t bar_full = mb;
   const uint32_t bar_empty = mb + 64;
@@ -406,6 +424,7 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
   const uint32_t bar_drain = mb + 160;
   const uint32_t bar_red = mb + 168;  // cluster split: every partial this CTA receives has landed
   const uint32_t bar_staged = mb + 176;  // + 8 x epilogue warp: the other parts' partials are in smem
+  const uint32_t bar_lnld = mb + 256;    // + 8 x epilogue warp: a stored LayerNorm slice is back in smem
   const int csplit = PAIR || CONV || LN ? 0 : p.csplit;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 248);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 252);
@@ -432,6 +451,8 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
     mbar_init(bar_drain, 1);
     if (csplit > 1) mbar_init(bar_red, 1);
     for (int w = 0; w < kEpiWarps; ++w) mbar_init(bar_staged + 8 * w, 1);
+    if (LN)
+      for (int w = 0; w < kEpiWarps; ++w) mbar_init(bar_lnld + 8 * w, 1);
     *abort_flag = 0;
     fence_mbar_init();
     if (csplit > 1) {
@@ -803,6 +824,124 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
     uint32_t acc_ph = 0;
     uint32_t nstore = 0;
     bool ok = true;
+    // One-kernel LayerNorm (p.ln_fused): the slices this warp has stored centred and whose
+    // statistics it has published, oldest first, normalised ln_defer units later.  A
+    // row block's tiles lie within ln_span consecutive units, so after ln_defer =
+    // ceil(ln_span / ncl) more units of this CTA every slice of the oldest one has been
+    // published by some CTA's earlier (or same) unit, whose epilogue never waits on a later
+    // unit: nothing can wait in a cycle.
+    constexpr int kLnQ = kLnMaxDefer + 1;
+    int h_tm[kLnQ] = {}, h_tn[kLnQ] = {};
+    float h_sh[kLnQ] = {};
+    int nh = 0;
+    uint32_t ln_ph = 0;
+    const int ln_defer = LN ? min(kLnMaxDefer, ln_defer_for(p.ln_span, ncl)) : 0;
+    const uint32_t lnbar = bar_lnld + 8 * ew;
+    // Normalises the slice (rows of this warp's lane quarter, columns of its half) of tile
+    // (tm_, tn_) in place: waits until all 2 x tiles_n slices of its 32 rows are
+    // published, merges their (mean, M2) in slice order (Chan et al.), reads the stored
+    // x - shift back through the staging block with TMA, writes
+    // ((x - shift) + (shift - mean)) * rstd * gamma + beta and stores it.
+    auto ln_normalize = [&](int tm_, int tn_, float sh_) -> bool {
+      const int r0 = tm_ * kTileM + static_cast<int>(rank) * kBM + quarter * 32;
+      if (r0 >= p.M) return true;
+      const int grp = r0 >> 5;
+      const int target = 2 * p.tiles_n;
+      int ready = 1;
+      if (lane == 0) {
+        const int* cp = p.ln_cnt + grp;
+        if (ld_acquire_gpu(cp) < target) {
+          const uint64_t t0 = global_timer_ns();
+          while (ld_acquire_gpu(cp) < target) {
+            if (*abort_flag || global_timer_ns() - t0 > tmo) {
+              ready = 0;
+              break;
+            }
+            __nanosleep(64);
+          }
+        }
+      }
+      ready = __shfl_sync(0xffffffffu, ready, 0);
+      __syncwarp();
+      if (!ready) return false;
+      const int row = r0 + lane;
+      float cnt = 0.f, mean = 0.f, m2 = 0.f;
+      if (row < p.M) {
+        for (int sl = 0; sl < target; ++sl) {
+          const float2 st = __ldcg(p.ln_st2 + static_cast<long long>(sl) * p.M + row);
+          chan_merge(cnt, mean, m2, static_cast<float>(max(0, min(kHalfCols, p.N - sl * kHalfCols))), st.x, st.y);
+        }
+      }
+      const float rs = rsqrtf(m2 / static_cast<float>(p.N) + p.eps);
+      const float off = sh_ - mean;
+      if (lane == 0 && atomicAdd(p.ln_cnt + p.ln_groups + grp, 1) == target - 1) {
+        // every normaliser of these rows has seen the arrivals: reset both counters
+        atomicExch(p.ln_cnt + grp, 0);
+        atomicExch(p.ln_cnt + p.ln_groups + grp, 0);
+      }
+#pragma unroll 1
+      for (int ci = 0; ci < kHalfChunks; ++ci) {
+        const int cbase = tn_ * BN + hcol + ci * kCW;
+        if (lane == 0) {
+          // every store of this warp has completed (the slice among them) and the staging
+          // block is free
+          bulk_wait<0>();
+          fence_proxy_async_global();
+          mbar_arrive_expect_tx(lnbar, kEpiBufBytes);
+          tma_load_2d(buf0, &tmC, lnbar, cbase, r0);
+        }
+        if (!mbar_wait(lnbar, ln_ph, tmo, abort_flag)) return false;
+        ln_ph ^= 1;
+        const uint32_t rowp = buf0 + lane * 128;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int col = cbase + 8 * j;
+          float g[8], b[8];
+          if (col < p.N) {
+            load_vec8(p.gamma, p.vec_dtype, col, g);
+            load_vec8(p.beta, p.vec_dtype, col, b);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) g[e] = b[e] = 0.f;
+          }
+          const uint32_t addr = rowp + ((j ^ (lane & 7)) << 4);
+          uint32_t w[4];
+          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3])
+                       : "r"(addr)
+                       : "memory");
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = unpack2<OUT_DT>(w[e]);
+            w[e] = pack2<OUT_DT>(fmaf((f.x + off) * rs, g[2 * e], b[2 * e]),
+                                 fmaf((f.y + off) * rs, g[2 * e + 1], b[2 * e + 1]));
+          }
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w[0]), "r"(w[1]), "r"(w[2]),
+                       "r"(w[3])
+                       : "memory");
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, buf0, cbase, r0);
+          bulk_commit();
+        }
+        ++nstore;
+      }
+      return true;
+    };
+    // Normalises the oldest held slice and drops it from the queue.
+    auto ln_pop = [&]() -> bool {
+      const bool r = ln_normalize(h_tm[0], h_tn[0], h_sh[0]);
+#pragma unroll
+      for (int i = 0; i + 1 < kLnQ; ++i) {
+        h_tm[i] = h_tm[i + 1];
+        h_tn[i] = h_tn[i + 1];
+        h_sh[i] = h_sh[i + 1];
+      }
+      --nh;
+      return r;
+    };
     for (int u = cid; u < p.num_units; u += ncl) {
       const Unit un = unit_of(p, u);
       const int tm = un.tm, tn = un.tn;
@@ -1331,12 +1470,41 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
       if (acc == 0) acc_ph ^= 1;
 
       if constexpr (LN) {
-        // Per-tile row statistics; the row pass (launched next on the same stream)
-        // merges them and normalises every row in place.
         const int row = row0 + lane;
-        // slice = this warp's column half of the tile (the row pass merges the slices)
-        if (row < p.M)
-          p.ln_stats[static_cast<long long>(tn * kHalves + half) * p.M + row] = make_float4(st_mean, st_m2, shift, 0.f);
+        if (!kNarrow && p.ln_fused) {
+          // Publish this slice's (mean, M2), count it into its 32 rows' arrivals, hold
+          // it, and normalise the oldest held slice once ln_defer newer ones exist.
+          if (row < p.M)
+            p.ln_st2[static_cast<long long>(tn * kHalves + half) * p.M + row] = make_float2(st_mean, st_m2);
+          __threadfence();
+          __syncwarp();
+          if (lane == 0 && row0 < p.M) red_add_release_gpu(p.ln_cnt + (row0 >> 5), 1);
+#pragma unroll
+          for (int i = 0; i < kLnQ; ++i) {
+            if (i == nh) {
+              h_tm[i] = tm;
+              h_tn[i] = tn;
+              h_sh[i] = shift;
+            }
+          }
+          ++nh;
+          if (nh > ln_defer && !ln_pop()) {
+            ok = false;
+            break;
+          }
+        } else {
+          // Per-tile row statistics; the row pass (launched next on the same stream)
+          // merges them and normalises every row in place.  The slice is this warp's
+          // column half of the tile.
+          if (row < p.M)
+            p.ln_stats[static_cast<long long>(tn * kHalves + half) * p.M + row] = make_float4(st_mean, st_m2, shift, 0.f);
+        }
+      }
+    }
+    if constexpr (LN) {
+      // the slices still held after the last unit
+      while (ok && nh > 0) {
+        if (!ln_pop()) ok = false;
       }
     }
     if (!ok) {

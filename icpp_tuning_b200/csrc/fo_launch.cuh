@@ -27,6 +27,8 @@ struct LaunchArgs {
   bool pair;  // launch as clusters of two CTAs (block_m 256, tcgen05 cta_group::2)
   bool swap;  // conv: operand-swapped kernel (M = output channels, N = pixels)
   int csplit;  // gemm: parts of a cluster split (clusters of csplit CTAs), 0 or 1 = none
+  bool coop;   // cooperative launch: every CTA resident at once (one-kernel LayerNorm,
+               // whose CTAs wait on counters other CTAs of the grid increment)
 };
 
 template <int BN, int ACT, int OUT_DT, bool LN, bool CONV, bool PAIR, bool SWAP, int KPS>
@@ -50,18 +52,22 @@ cudaError_t launch_tc_k(const LaunchArgs& a) {
   cudaLaunchAttribute pdl;
   pdl.id = cudaLaunchAttributeProgrammaticStreamSerialization;
   pdl.val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute coop;
+  coop.id = cudaLaunchAttributeCooperative;
+  coop.val.cooperative = 1;
   if constexpr (PAIR) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.grid, 1, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = a.smem;
     cfg.stream = a.stream;
-    cudaLaunchAttribute attr[2];
+    cudaLaunchAttribute attr[3];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     attr[1] = pdl;
+    attr[2] = coop;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     // A persistent grid larger than the number of co-resident pairs would leave a tail
@@ -77,7 +83,10 @@ cudaError_t launch_tc_k(const LaunchArgs& a) {
       max_clusters[dev & 63].store(mc, std::memory_order_relaxed);
     }
     if (mc > 0 && static_cast<int>(cfg.gridDim.x) > 2 * mc) cfg.gridDim.x = 2 * mc;
-    cfg.numAttrs = 2;
+    // the one-kernel LayerNorm's wait depth follows the number of pairs actually launched
+    if (LN && a.p.ln_fused && ln_defer_for(a.p.ln_span, static_cast<int>(cfg.gridDim.x) / 2) > kLnMaxDefer)
+      return cudaErrorCooperativeLaunchTooLarge;
+    cfg.numAttrs = a.coop ? 3 : 2;
     return cudaLaunchKernelEx(&cfg, kern, a.tmA, a.tmB, a.tmC, a.p);
   } else {
     if (a.csplit > 1) {
@@ -117,8 +126,9 @@ cudaError_t launch_tc_k(const LaunchArgs& a) {
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = a.smem;
     cfg.stream = a.stream;
-    cfg.attrs = &pdl;
-    cfg.numAttrs = 1;
+    cudaLaunchAttribute attr[2] = {pdl, coop};
+    cfg.attrs = attr;
+    cfg.numAttrs = a.coop ? 2 : 1;
     return cudaLaunchKernelEx(&cfg, kern, a.tmA, a.tmB, a.tmC, a.p);
   }
 }

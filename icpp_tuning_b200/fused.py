@@ -73,14 +73,14 @@ def default_config(M: int, n: int, K: int, epilogue: str = "none") -> N.FoTileCf
 def as_tile_cfg(cfg) -> N.FoTileCfg:
     """Accepts an FoTileCfg or a raw config dict of the autotuner
     (block_M / block_N / block_K / num_stages / group_m / max_ctas / swap_ab / split_k /
-    split_mode)."""
+    split_mode / ln_mode)."""
     if isinstance(cfg, N.FoTileCfg):
         return cfg
     return N.tile_cfg(block_n=int(cfg["block_N"]), stages=int(cfg["num_stages"]),
                       group_m=int(cfg.get("group_m", 0)), max_ctas=int(cfg.get("max_ctas", 0)),
                       block_m=int(cfg.get("block_M", 128)), block_k=int(cfg.get("block_K", 64)),
                       swap_ab=int(cfg.get("swap_ab", 0)), split_k=int(cfg.get("split_k", 0)),
-                      split_mode=int(cfg.get("split_mode", 0)))
+                      split_mode=int(cfg.get("split_mode", 0)), ln_mode=int(cfg.get("ln_mode", 0)))
 
 
 def workspace_bytes(M: int, N_: int, K: int, epilogue: str, cfg) -> int:

@@ -91,7 +91,7 @@ def build_fused_kernel(M: int, N: int, K: int, gemm_config: Optional[Dict[str, A
                                      out_bytes=torch.empty((), dtype=out_dtype).element_size())
     cfg = fused.as_tile_cfg(gemm_config)
     dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
-    ws = torch.empty(max(16, fused.ln_workspace_bytes(M, N, cfg)), dtype=torch.uint8, device=dev)
+    ws = torch.zeros(max(16, fused.ln_workspace_bytes(M, N, cfg)), dtype=torch.uint8, device=dev)
 
     def fused_kernel(A, B, bias, gamma, beta, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         _check_shape(A, B, M, N, K, b_layout)

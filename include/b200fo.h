@@ -24,7 +24,7 @@
 extern "C" {
 #endif
 
-#define FO_ABI_VERSION 1
+#define FO_ABI_VERSION 2
 
 /* ---- return codes ---------------------------------------------------------------- */
 #define FO_OK 0
@@ -87,14 +87,22 @@ typedef struct FoTileCfg {
                     /*     and reduce-scatter their partials through distributed shared   */
                     /*     memory, no workspace (gemm with block_m 128, s <= 8, one wave, */
                     /*     not with FO_EPI_BIAS_LN)                                       */
+  int32_t ln_mode;  /* FO_EPI_BIAS_LN only: 0 = automatic (one kernel when eligible),      */
+                    /* 1 = two kernels: the GEMM stores biased rows + slice statistics,   */
+                    /*     a row pass normalises them in place,                           */
+                    /* 2 = one kernel: each epilogue warp normalises its own stored slice */
+                    /*     once every slice of its rows has published its statistics     */
+                    /*     (block_n >= 128; a cooperative launch, all CTAs resident)     */
 } FoTileCfg;
 
 /* One GEMM-family call.  A[M,K] row-major (row stride lda elements).  B per b_layout
  * with row stride ldb.  out[M,N] row-major with row stride ldo.  bias/gamma/beta are
  * length-N vectors of type vec_dtype (may be NULL when the epilogue does not read them).
- * For FO_EPI_BIAS_LN the caller provides workspace (fo_gemm_workspace_size bytes, any
- * contents) for the per-row slice statistics; the call then launches two kernels: the
- * GEMM writing biased rows + statistics, and the in-place normalisation pass. */
+ * For FO_EPI_BIAS_LN the caller provides workspace (fo_gemm_workspace_size bytes,
+ * zero-filled before its first use; every call leaves it zeroed) for the per-row slice
+ * statistics and the arrival counters of the one-kernel path (FoTileCfg.ln_mode).  After
+ * a call that reported FO_ETIMEOUT (fo_device_status) the counters may be left non-zero:
+ * zero the workspace again before reusing it. */
 typedef struct FoGemmDesc {
   int64_t M, N, K;
   const void* a;
@@ -147,7 +155,7 @@ typedef struct FoConvDesc {
 int fo_gemm(const FoGemmDesc* desc, const FoTileCfg* cfg, void* stream);
 
 /* Bytes of workspace fo_gemm uses for this (desc, cfg).  FO_EPI_BIAS_LN: required (per-row
- * slice statistics, any contents).  Other epilogues: optional room for fp32 partials of a
+ * slice statistics and arrival counters, zero-filled once).  Other epilogues: optional room for fp32 partials of a
  * split-K tail -- the tiles of a last, less than half-full wave (or of a problem with
  * fewer tiles than SMs) split along K over idle SMs; it must be zero-filled before its
  * first use and is left zeroed.  Without it (or with 0 returned) tiles are never split. */
@@ -199,11 +207,13 @@ int fo_last_error(char* buf, size_t len);
  * instead, and nothing is allocated: no cudaMalloc, no cudaFree.  Problems needing more
  * scratch (fo_gemm_workspace_size > FO_NOALLOC_LN_SCRATCH_BYTES) fail with FO_EINVAL.
  * The first call on a device looks up the array's address (legal under a stream
- * capture too).  All calls share the array: calls that overlap on the GPU race and must
- * be serialised.  Wait timeouts go to a private status word, not fo_device_status. */
+ * capture too).  Each call clears the array's counters on `stream` (cudaMemsetAsync)
+ * and then runs fo_gemm on it, so config checks, the wait limit, fo_device_status and
+ * fo_launch_count behave as for fo_gemm.  All calls share the array: calls that overlap
+ * on the GPU race and must be serialised. */
 int fo_gemm_bias_layernorm_noalloc(const FoGemmDesc* desc, const FoTileCfg* cfg, void* stream);
 
-/* Library version string, e.g. "b200fo 0.1.0 sm_100a abi 1". */
+/* Library version string, e.g. "b200fo 0.2.0 sm_100a abi 2". */
 const char* fo_version(void);
 
 /* Number of kernel launches this library has issued from this process. */

@@ -28,7 +28,7 @@ def _gemm_case(epilogue, M, N_, K, cfg, dt=torch.bfloat16, split=False):
     gamma, beta = randn(g, N_, dtype=dt, scale=0.1, shift=1.0).cuda(), randn(g, N_, dtype=dt, scale=0.1).cuda()
     ws = None
     if epilogue == "bias_layernorm":
-        ws = torch.empty(fused.ln_workspace_bytes(M, N_, cfg), dtype=torch.uint8, device="cuda")
+        ws = torch.zeros(fused.ln_workspace_bytes(M, N_, cfg), dtype=torch.uint8, device="cuda")
     elif split:
         ws = torch.zeros(max(fused.workspace_bytes(M, N_, K, epilogue, cfg), 16), dtype=torch.uint8, device="cuda")
     ln = "layernorm" in epilogue

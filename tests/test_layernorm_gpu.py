@@ -28,13 +28,65 @@ def test_ln_ragged(bn, odt):
     dt = odt
     x, w, bias, gamma, beta = _inputs(10, M, Nn, K, dt)
     cfg = N.tile_cfg(bn, {256: 4, 128: 6, 64: 8}[bn], 0)
-    # arbitrary starting contents: every call writes each statistic before reading it
+    # zero counters, arbitrary statistics: every call writes each statistic before reading it
     ws = torch.full((fused.ln_workspace_bytes(M, Nn, cfg),), 0x7F, dtype=torch.uint8, device="cuda")
+    hdr = _header_bytes(M)
+    ws[:hdr] = 0
     for _ in range(3):
         out = fused.gemm(*cuda(x, w), b_layout="nk", epilogue="bias_layernorm", bias=bias.cuda(),
                          gamma=gamma.cuda(), beta=beta.cuda(), workspace=ws, out_dtype=odt, config=cfg)
         assert_close(out, R.gemm_bias_layernorm(x, w, bias, gamma, beta, b_layout="nk", out_dtype=odt), TOL_LN)
+    assert int(ws[:hdr].count_nonzero()) == 0  # the counters are left zeroed
     status_clean()
+
+
+def _header_bytes(M):
+    """Bytes of arrival counters at the head of the LayerNorm workspace."""
+    return (((M + 31) // 32) * 8 + 255) // 256 * 256
+
+
+def _ln_call(x, w, bias, gamma, beta, cfg, ws=None, odt=torch.bfloat16):
+    M, Nn = x.shape[0], w.shape[0]
+    if ws is None:
+        ws = torch.zeros(fused.ln_workspace_bytes(M, Nn, cfg), dtype=torch.uint8, device="cuda")
+    out = fused.gemm(*cuda(x, w), b_layout="nk", epilogue="bias_layernorm", bias=bias.cuda(), gamma=gamma.cuda(),
+                     beta=beta.cuda(), workspace=ws, out_dtype=odt, config=cfg)
+    return out, ws
+
+
+@pytest.mark.parametrize("bm,bn,bk,st,gm", [(128, 128, 64, 6, 0), (128, 256, 64, 4, 0), (128, 256, 64, 4, 8),
+                                           (256, 256, 128, 3, 0), (256, 256, 128, 3, 8), (256, 128, 128, 4, 16)])
+def test_ln_one_kernel(bm, bn, bk, st, gm):
+    """ln_mode 2 (each epilogue warp normalises its own stored slice once its rows'
+    statistics are all published) against the oracle and against the two-kernel path,
+    on single CTAs and CTA pairs, row-major and grouped rasters (the grouped ones defer
+    a slice by more than one unit), ragged M and N; the counters are left zeroed and a
+    repeated call gives the same bits."""
+    M, Nn, K = 1500, 3000, 320
+    x, w, bias, gamma, beta = _inputs(14, M, Nn, K)
+    one = N.tile_cfg(bn, st, gm, block_m=bm, block_k=bk, ln_mode=N.LN_ONE_KERNEL)
+    two = N.tile_cfg(bn, st, gm, block_m=bm, block_k=bk, ln_mode=N.LN_TWO_KERNELS)
+    n0 = N.launch_count()
+    out1, ws = _ln_call(x, w, bias, gamma, beta, one)
+    assert N.launch_count() - n0 == 1  # one kernel, no row pass
+    ref = R.gemm_bias_layernorm(x, w, bias, gamma, beta, b_layout="nk", out_dtype=torch.bfloat16)
+    assert_close(out1, ref, TOL_LN)
+    assert int(ws[:_header_bytes(M)].count_nonzero()) == 0
+    again, _ = _ln_call(x, w, bias, gamma, beta, one, ws=ws)
+    assert torch.equal(again, out1)
+    out2, _ = _ln_call(x, w, bias, gamma, beta, two)
+    # same statistics and centring: the two paths differ by at most one output rounding
+    assert_close(out1, out2, dict(atol=1e-2, rtol=1e-2))
+    status_clean()
+
+
+def test_ln_one_kernel_rejections():
+    x, w, bias, gamma, beta = _inputs(15, 256, 512, 64)
+    with pytest.raises(N.FoError, match="block_n >= 128"):
+        _ln_call(x, w, bias, gamma, beta, N.tile_cfg(64, 8, 0, ln_mode=N.LN_ONE_KERNEL))
+    # automatic mode takes the two-kernel path for block_n 64
+    out, _ = _ln_call(x, w, bias, gamma, beta, N.tile_cfg(64, 8, 0))
+    assert_close(out, R.gemm_bias_layernorm(x, w, bias, gamma, beta, b_layout="nk", out_dtype=torch.bfloat16), TOL_LN)
 
 
 @pytest.mark.parametrize("M,Nn,bn", [(2000, 1000, 64), (1100, 2304, 256), (3000, 4096, 128), (100, 5000, 256),
@@ -45,7 +97,7 @@ def test_ln_row_pass_variants(M, Nn, bn):
     K = 128
     x, w, bias, gamma, beta = _inputs(13, M, Nn, K)
     cfg = N.tile_cfg(bn, {256: 4, 128: 6, 64: 8}[bn], 0)
-    ws = torch.empty(fused.ln_workspace_bytes(M, Nn, cfg), dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(fused.ln_workspace_bytes(M, Nn, cfg), dtype=torch.uint8, device="cuda")
     out = fused.gemm(*cuda(x, w), b_layout="nk", epilogue="bias_layernorm", bias=bias.cuda(), gamma=gamma.cuda(),
                      beta=beta.cuda(), workspace=ws, out_dtype=torch.bfloat16, config=cfg)
     rows = torch.arange(0, M, max(1, M // 64))
@@ -85,7 +137,9 @@ def test_config4_ln_full():
     M, Nn, K = 16384, 4096, 4096
     x, w, bias, gamma, beta = _inputs(3, M, Nn, K)
     k = gbln.build_fused_kernel(M, Nn, K, out_dtype=torch.bfloat16, b_layout="nk")
+    n0 = N.launch_count()
     out = k(*cuda(x, w, bias, gamma, beta))
+    assert N.launch_count() - n0 == 1  # the tuned config runs the one-kernel LayerNorm
     rows = torch.arange(0, M, 97)
     ref = R.gemm_bias_layernorm(x[rows], w, bias, gamma, beta, b_layout="nk", out_dtype=torch.bfloat16)
     assert_close(out[rows.cuda()], ref, TOL_LN)

@@ -178,7 +178,22 @@ def test_split_mode_field():
     for bad in (-1, 3):
         ok, why = N.config_legal(0, N.FO_DT_BF16, N.tile_cfg(128, 6, 8, split_mode=bad))
         assert not ok and "split_mode" in why
-    assert ctypes.sizeof(N.FoTileCfg) == 9 * 4  # the header's FoTileCfg: nine int32 fields
+    assert ctypes.sizeof(N.FoTileCfg) == 10 * 4  # the header's FoTileCfg: ten int32 fields
+
+
+def test_ln_mode_field_and_workspace():
+    """ln_mode: 0 automatic, 1 two kernels, 2 one kernel.  The LayerNorm workspace holds
+    the 32-row groups' arrival counters (two int32 each, 256-byte padded) and then one
+    16-byte statistic per row per half-tile slice."""
+    for mode in (0, 1, 2):
+        assert N.config_legal(0, N.FO_DT_BF16, N.tile_cfg(128, 6, 8, ln_mode=mode))[0]
+    for bad in (-1, 3):
+        ok, why = N.config_legal(0, N.FO_DT_BF16, N.tile_cfg(128, 6, 8, ln_mode=bad))
+        assert not ok and "ln_mode" in why
+    d = N.FoGemmDesc()
+    d.M, d.N, d.K, d.epilogue = 16384, 4096, 4096, N.FO_EPI_BIAS_LN
+    size = N.lib().fo_gemm_workspace_size(ctypes.byref(d), ctypes.byref(N.tile_cfg(256, 3, 8, block_m=256)))
+    assert size == 512 * 8 + 32 * 16384 * 16
 
 
 def test_timeout_setting():

@@ -63,7 +63,7 @@ def test_pair_layernorm():
     x, w = randn(g, M, K), randn(g, Nn, K, scale=K ** -0.5)
     bias, gamma, beta = randn(g, Nn, scale=0.02), randn(g, Nn, scale=0.02, shift=1.0), randn(g, Nn, scale=0.02)
     cfg = pcfg(256, group_m=0)
-    ws = torch.empty(fused.ln_workspace_bytes(M, Nn, cfg), dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(fused.ln_workspace_bytes(M, Nn, cfg), dtype=torch.uint8, device="cuda")
     out = fused.gemm(*cuda(x, w), b_layout="nk", epilogue="bias_layernorm", bias=bias.cuda(), gamma=gamma.cuda(),
                      beta=beta.cuda(), workspace=ws, config=cfg)
     assert_close(out, R.gemm_bias_layernorm(x, w, bias, gamma, beta, b_layout="nk", out_dtype=torch.bfloat16), TOL_LN)

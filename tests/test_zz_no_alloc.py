@@ -13,6 +13,7 @@ import torch
 
 from icpp_tuning_b200 import _native as N
 from icpp_tuning_b200 import fused
+from oracle import ref_ops as R
 
 pytestmark = pytest.mark.gpu
 
@@ -45,24 +46,45 @@ def test_noalloc_matches_fo_gemm_twice(M, Nn, K, layout, bn):
     ws = torch.zeros(fused.ln_workspace_bytes(M, Nn, cfg), dtype=torch.uint8, device="cuda")
     expect = fused.gemm(x, w, b_layout=layout, epilogue="bias_layernorm", bias=bias, gamma=gamma, beta=beta,
                         workspace=ws, config=cfg)
+    # the reference's own program on sampled rows (the oracle of the other LayerNorm tests)
+    rows = torch.arange(0, M, 37)
+    ref = R.gemm_bias_layernorm(x.cpu()[rows], w.cpu(), bias.cpu(), gamma.cpu(), beta.cpu(), b_layout=layout,
+                                out_dtype=torch.bfloat16)
     stream = torch.cuda.current_stream().cuda_stream
     for call in range(2):
         out = torch.full((M, Nn), float("nan"), dtype=torch.bfloat16, device="cuda")
         d = _desc(x, w, bias, gamma, beta, out, M, Nn, K, layout)
+        n0 = N.launch_count()
         rc = N.lib().fo_gemm_bias_layernorm_noalloc(ctypes.byref(d), ctypes.byref(cfg), stream)
         assert rc == N.FO_OK, N.last_error()
+        assert N.launch_count() > n0  # counted like fo_gemm
         torch.cuda.synchronize()
         torch.testing.assert_close(out.float(), expect.float(), **TOL_LN, msg=f"call {call}")
+        torch.testing.assert_close(out[rows.cuda()].float().cpu(), ref.float(), **TOL_LN, msg=f"call {call}")
+    # a bounded wait that ran out would show here, in fo_device_status's word
+    rc, where = N.device_status(torch.cuda.current_device())
+    assert rc == 0, f"device status {rc} at {where:#x}"
 
 
 def test_noalloc_rejects_oversized_problems():
+    """The size rule rejects the call before anything is enqueued.  The call is made
+    while a side stream is being captured and the capture is discarded unlaunched, so
+    even if the check regressed nothing would run on the (tiny, real) buffers."""
     cfg = N.tile_cfg(64, 8, 0)
+    t = torch.zeros(4096, dtype=torch.bfloat16, device="cuda")
     d = N.FoGemmDesc()
     d.M, d.N, d.K = 1 << 20, 4096, 64  # 64 N-tiles x 1M rows of statistics >> 8 MiB
-    d.a = d.b = d.out = d.bias = d.gamma = d.beta = 1 << 20
+    d.a = d.b = d.out = d.bias = d.gamma = d.beta = t.data_ptr()
     d.lda, d.ldb, d.ldo = 64, 64, 4096
     d.in_dtype = d.vec_dtype = d.out_dtype = N.FO_DT_BF16
     d.b_layout, d.epilogue, d.eps = N.FO_B_NK, N.FO_EPI_BIAS_LN, 1e-5
-    rc = N.lib().fo_gemm_bias_layernorm_noalloc(ctypes.byref(d), ctypes.byref(cfg), None)
+    side = torch.cuda.Stream()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        g.capture_begin()
+        rc = N.lib().fo_gemm_bias_layernorm_noalloc(ctypes.byref(d), ctypes.byref(cfg), side.cuda_stream)
+        msg = N.last_error()
+        g.capture_end()
+    del g  # never replayed
     assert rc == N.FO_EINVAL
-    assert "static scratch holds" in N.last_error()
+    assert "static scratch holds" in msg
