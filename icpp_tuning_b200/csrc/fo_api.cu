@@ -552,6 +552,8 @@ int fo_gemm(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
     p.ln_groups = (p.M + 31) / 32;
     p.ln_stats = reinterpret_cast<float4*>(ws + ln_header_bytes(p.M));
     p.ln_st2 = reinterpret_cast<float2*>(ws + ln_header_bytes(p.M));
+    // after the (mean, M2) slices, in the half of the statistics region they leave free
+    p.ln_fin = p.ln_st2 + static_cast<size_t>(p.tiles_n) * ln_halves(bn) * p.M;
   }
   fill_common(p, di);
 

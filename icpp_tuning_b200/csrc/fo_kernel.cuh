@@ -109,15 +109,16 @@ struct KParams {
                     // (a slot is a split tile's 128 rows: two per tile for CTA pairs)
   // One-kernel LayerNorm (ln_fused = 1; launched cooperatively, every CTA resident): each
   // epilogue warp publishes the (mean, M2) of its row slice to ln_st2[slice][row] and
-  // counts itself into ln_cnt[row / 32]; some units later, when every slice of its 32
-  // rows has arrived, the same warp reads its stored slice back and normalises it in
-  // place.  ln_cnt holds 2 x ln_groups int32 (arrivals, then finished normalisers),
+  // counts itself into ln_cnt[row / 32]; the arrival that completes the 32 rows merges
+  // their statistics into ln_fin; some units later the same warp reads its stored slice
+  // back and normalises it in place.  ln_cnt holds 2 x ln_groups int32 (arrivals, then finished normalisers),
   // zero at launch and reset to zero by the last normaliser of each group.
   int ln_fused;
   int ln_span;    // largest unit distance between two tiles of one row block
   int ln_groups;  // ceil(M / 32)
   int* ln_cnt;
-  float2* ln_st2;
+  float2* ln_st2;  // [2 x tiles_n slices][M] (mean, M2) of each row slice
+  float2* ln_fin;  // [M] (mean, rstd) of each row, written by its group's last arrival
 };
 
 __host__ __device__ constexpr int b_stage_bytes(int bn) { return bn * kBK * 2; }
@@ -838,15 +839,16 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
     const int ln_defer = LN ? min(kLnMaxDefer, ln_defer_for(p.ln_span, ncl)) : 0;
     const uint32_t lnbar = bar_lnld + 8 * ew;
     // Normalises the slice (rows of this warp's lane quarter, columns of its half) of tile
-    // (tm_, tn_) in place: waits until all 2 x tiles_n slices of its 32 rows are
-    // published, merges their (mean, M2) in slice order (Chan et al.), reads the stored
-    // x - shift back through the staging block with TMA, writes
-    // ((x - shift) + (shift - mean)) * rstd * gamma + beta and stores it.
-    auto ln_normalize = [&](int tm_, int tn_, float sh_) -> bool {
+    // (tm_, tn_) in place: waits until the last of the 2 x tiles_n slices of its 32 rows
+    // has merged their statistics into (mean, rstd) (ln_cnt reaches 2 x tiles_n + 1),
+    // reads the stored x - shift back through the staging block with TMA, writes
+    // ((x - shift) + (shift - mean)) * rstd * gamma + beta and stores it.  `tail`: no
+    // newer stores of this warp follow the slice's own, so wait for all of them.
+    auto ln_normalize = [&](int tm_, int tn_, float sh_, bool tail) -> bool {
       const int r0 = tm_ * kTileM + static_cast<int>(rank) * kBM + quarter * 32;
       if (r0 >= p.M) return true;
       const int grp = r0 >> 5;
-      const int target = 2 * p.tiles_n;
+      const int target = 2 * p.tiles_n + 1;
       int ready = 1;
       if (lane == 0) {
         const int* cp = p.ln_cnt + grp;
@@ -865,16 +867,10 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
       __syncwarp();
       if (!ready) return false;
       const int row = r0 + lane;
-      float cnt = 0.f, mean = 0.f, m2 = 0.f;
-      if (row < p.M) {
-        for (int sl = 0; sl < target; ++sl) {
-          const float2 st = __ldcg(p.ln_st2 + static_cast<long long>(sl) * p.M + row);
-          chan_merge(cnt, mean, m2, static_cast<float>(max(0, min(kHalfCols, p.N - sl * kHalfCols))), st.x, st.y);
-        }
-      }
-      const float rs = rsqrtf(m2 / static_cast<float>(p.N) + p.eps);
-      const float off = sh_ - mean;
-      if (lane == 0 && atomicAdd(p.ln_cnt + p.ln_groups + grp, 1) == target - 1) {
+      const float2 fin = row < p.M ? __ldcg(p.ln_fin + row) : make_float2(0.f, 0.f);
+      const float rs = fin.y;
+      const float off = sh_ - fin.x;
+      if (lane == 0 && atomicAdd(p.ln_cnt + p.ln_groups + grp, 1) == target - 2) {
         // every normaliser of these rows has seen the arrivals: reset both counters
         atomicExch(p.ln_cnt + grp, 0);
         atomicExch(p.ln_cnt + p.ln_groups + grp, 0);
@@ -883,9 +879,14 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
       for (int ci = 0; ci < kHalfChunks; ++ci) {
         const int cbase = tn_ * BN + hcol + ci * kCW;
         if (lane == 0) {
-          // every store of this warp has completed (the slice among them) and the staging
-          // block is free
-          bulk_wait<0>();
+          // the slice's stores have completed (only the newer stores of the current unit
+          // may still be in flight) and the staging block is free
+          if (tail) {
+            bulk_wait<0>();
+          } else {
+            bulk_wait<kHalfChunks>();
+            bulk_wait_read<0>();
+          }
           fence_proxy_async_global();
           mbar_arrive_expect_tx(lnbar, kEpiBufBytes);
           tma_load_2d(buf0, &tmC, lnbar, cbase, r0);
@@ -931,8 +932,8 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
       return true;
     };
     // Normalises the oldest held slice and drops it from the queue.
-    auto ln_pop = [&]() -> bool {
-      const bool r = ln_normalize(h_tm[0], h_tn[0], h_sh[0]);
+    auto ln_pop = [&](bool tail) -> bool {
+      const bool r = ln_normalize(h_tm[0], h_tn[0], h_sh[0], tail);
 #pragma unroll
       for (int i = 0; i + 1 < kLnQ; ++i) {
         h_tm[i] = h_tm[i + 1];
@@ -1478,7 +1479,36 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
             p.ln_st2[static_cast<long long>(tn * kHalves + half) * p.M + row] = make_float2(st_mean, st_m2);
           __threadfence();
           __syncwarp();
-          if (lane == 0 && row0 < p.M) red_add_release_gpu(p.ln_cnt + (row0 >> 5), 1);
+          if (row0 < p.M) {
+            // The warp whose arrival completes its 32 rows merges their 2 x tiles_n slices
+            // once (slice order, Chan et al.), publishes (mean, rstd) per row and counts
+            // once more: normalisers wait for 2 x tiles_n + 1.
+            const int nsl = 2 * p.tiles_n;
+            int last = 0;
+            if (lane == 0) last = atomicAdd(p.ln_cnt + (row0 >> 5), 1) == nsl - 1;
+            last = __shfl_sync(0xffffffffu, last, 0);
+            if (last) {
+              __threadfence();
+              float c = 0.f, mean = 0.f, m2 = 0.f;
+              if (row < p.M) {
+                for (int s0 = 0; s0 < nsl; s0 += 8) {
+                  float2 v[8];
+#pragma unroll
+                  for (int i = 0; i < 8; ++i)
+                    v[i] = s0 + i < nsl ? __ldcg(p.ln_st2 + static_cast<long long>(s0 + i) * p.M + row)
+                                        : make_float2(0.f, 0.f);
+#pragma unroll
+                  for (int i = 0; i < 8; ++i)
+                    chan_merge(c, mean, m2, static_cast<float>(max(0, min(kHalfCols, p.N - (s0 + i) * kHalfCols))),
+                               v[i].x, v[i].y);
+                }
+                p.ln_fin[row] = make_float2(mean, rsqrtf(m2 / static_cast<float>(p.N) + p.eps));
+              }
+              __threadfence();
+              __syncwarp();
+              if (lane == 0) red_add_release_gpu(p.ln_cnt + (row0 >> 5), 1);
+            }
+          }
 #pragma unroll
           for (int i = 0; i < kLnQ; ++i) {
             if (i == nh) {
@@ -1488,7 +1518,7 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
             }
           }
           ++nh;
-          if (nh > ln_defer && !ln_pop()) {
+          if (nh > ln_defer && !ln_pop(false)) {
             ok = false;
             break;
           }
@@ -1504,7 +1534,7 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
     if constexpr (LN) {
       // the slices still held after the last unit
       while (ok && nh > 0) {
-        if (!ln_pop()) ok = false;
+        if (!ln_pop(true)) ok = false;
       }
     }
     if (!ok) {

@@ -6,6 +6,10 @@ reference feeds a random [b, s, 3h] tensor instead of a projection), causal atte
 with scores scaled by 1/sqrt(head_size) and a -10000 upper-triangular mask (:56-68),
 output projection + bias + residual + LayerNorm (:76-79), GELU(erf) MLP (:82-83), second
 projection + bias + residual + LayerNorm (:84-87).  fp16 throughout, as the reference.
+Pinned: tests/golden/ref_ops.pt holds the output of the reference's own bert_fwd_std,
+executed from its source on CPU (2 layers, small sizes; tests/golden/make_golden.py
+supplies the util/ helpers the reference does not ship), and tests/test_oracle_golden.py
+checks this restatement against it.
 """
 import math
 
@@ -14,7 +18,9 @@ import torch.nn.functional as F
 
 
 def transpose_for_scores(x, head_num, head_size):
-    """[b, s, h*d] -> [b, s, h, d] (the reference imports this from its missing util/)."""
+    """[b, s, h*d] -> [b, s, h, d].  The reference's helper of this name (imported from
+    its missing util/) also permutes to [b, h, s, d], which its code permutes back before
+    use; this restatement skips both permutes."""
     return x.view(x.size()[:-1] + (head_num, head_size))
 
 

@@ -36,6 +36,5 @@ def test_bert_forward_matches_reference(model, layers, heads, batch, seq):
     with torch.no_grad():
         ours = FusedBert(w, heads, batch * seq)(x)
         ref = bert_forward(w, x, heads, HEAD_SIZE)
-    err = (ours.float() - ref.float()).abs()
-    # fp16 LayerNorm outputs of O(1): per-element agreement within a few fp16 ulps
-    assert err.mean() < 5e-3 and err.max() < 0.1, (err.mean().item(), err.max().item())
+    # the LayerNorm tolerance of the other parity tests
+    torch.testing.assert_close(ours.float(), ref.float(), atol=2e-2, rtol=2e-2)
