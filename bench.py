@@ -8,7 +8,11 @@ same metric through the public API (icpp_tuning_b200.gemm.gemm.build_kernel) wit
 step's inputs copied from pinned host memory and the result read back inside the timed
 region.  At N>1 (torchrun, NCCL) every rank owns one 4096-row shard of a global
 M = 4096*N problem (weak scaling, no collective on the data path); times are the max
-over ranks.  Rank 0 prints one JSON line.
+over ranks.  Rank 0 prints one JSON line.  At N=1 it also carries `per_op` (all five
+BASELINE workloads, device time, each beside the reference's CPU program on a row
+sample); at N>1 `strong` (each fixed global workload split into row / image shards over
+the ranks, global FLOPs over the max per-rank time, plus the NCCL all-gather of the
+output timed separately).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 """
@@ -232,6 +236,10 @@ def run_ours(args):
     e2e = {"value": round(flops * ws / (e2e_ms / 1e3) / 1e12, 2), "unit": UNIT,
            "h2d_bytes_per_step": a_h.numel() * 2 + bt_h.numel() * 2, "d2h_bytes_per_step": out.numel() * 2,
            "ms_per_step": round(e2e_ms, 4), "pipelined": "h2d / compute / d2h on three streams, 2 buffer sets"}
+    # host<->device traffic each rank sustains in that run (the 1 -> N e2e limit: all
+    # ranks' copies share the host's memory system and PCIe root)
+    e2e["host_copy_gbs_per_rank"] = round((e2e["h2d_bytes_per_step"] + e2e["d2h_bytes_per_step"]) / (e2e_ms / 1e3) / 1e9, 2)
+    strong = strong_table(args, ws, rank, dist) if ws > 1 and not args.no_ops else None
 
     if rank != 0:
         if dist is not None:
@@ -250,11 +258,10 @@ def run_ours(args):
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded randn, BASELINE configs[1] shapes)",
-        "config": {"workload": WORKLOAD, "parallelism": f"M-shard x{ws} (weak: 4096 rows per GPU)",
-                   "tile": "BM%d_BN%d_BK%d_S%d_G%d" % (kern.config["block_M"], kern.config["block_N"],
-                                                        kern.config.get("block_K", 64), kern.config["num_stages"],
-                                                        kern.config.get("group_m", 0)),
-                   "l2": "flushed between timed steps (256 MiB write outside the events)"},
+        "config": _config(ws),
+        "tile": "BM%d_BN%d_BK%d_S%d_G%d" % (kern.config["block_M"], kern.config["block_N"],
+                                             kern.config.get("block_K", 64), kern.config["num_stages"],
+                                             kern.config.get("group_m", 0)),
         "e2e": e2e,
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": UNIT,
                      "frac": round(achieved / peak, 4), "peak_kind": f"{kind} bf16 burst (cuBLAS 8192^3)",
@@ -268,31 +275,50 @@ def run_ours(args):
         line["cpu_baseline"] = cpu_baseline(args, budget_s=args.cpu_budget)
     if ws == 1 and not args.no_ops:
         line["per_op"] = per_op_table(args)
+    if strong is not None:
+        line["strong"] = strong
     print(json.dumps(line), flush=True)
     if dist is not None:
         dist.destroy_process_group()
 
 
-def cpu_baseline(args, budget_s: float = 20.0) -> dict:
-    """The reference's CPU program for the workload (oracle port of gemm.py:20-21 with the
-    bf16 output of configs[1]) on all host cores, on a bounded row sample."""
-    from oracle import ref_ops as R
-
+def cpu_rate(run, rows_total: int, flops_per_row: float, budget_s: float, steps: int, warmup: int):
+    """TFLOP/s of `run(rows)` (the reference's CPU program on the first `rows` rows of a
+    workload) on all host threads: one calibration call, then `warmup` untimed and `steps`
+    timed calls on a row sample sized so that all of them fit `budget_s`; the median step.
+    Both bench arms time the CPU path with this one function."""
     torch.set_num_threads(os.cpu_count() or 1)
-    a, bt = _inputs(1, 0)
+    probe = max(1, min(rows_total, 64))
     t0 = time.perf_counter()
-    R.gemm(a[:512], bt, "nk").to(torch.bfloat16)
-    t_full = (time.perf_counter() - t0) * M0 / 512
-    rows = M0 if 3 * t_full <= budget_s else 512
+    run(probe)
+    t_row = (time.perf_counter() - t0) / probe
+    rows = int(max(probe, min(rows_total, budget_s / max(1, steps + warmup) / max(t_row, 1e-9))))
+    for _ in range(warmup):
+        run(rows)
     times = []
-    for _ in range(3):
+    for _ in range(steps):
         t0 = time.perf_counter()
-        R.gemm(a[:rows], bt, "nk").to(torch.bfloat16)
+        run(rows)
         times.append(time.perf_counter() - t0)
     dt = statistics.median(times)
-    return {"value": round(2.0 * rows * N0 * K0 / dt / 1e12, 4), "unit": UNIT, "cores": torch.get_num_threads(),
-            "kind": "port", "sample": f"{rows} of {M0} rows of the 4096^3 bf16 GEMM, median of {len(times)}",
-            "cpu": _cpu_name()}
+    return flops_per_row * rows / dt / 1e12, rows, dt
+
+
+def _cpu_config2(budget_s: float, steps: int, warmup: int) -> dict:
+    """The reference's CPU program for the headline workload (oracle port of gemm.py:20-21
+    with the bf16 output of configs[1])."""
+    from oracle import ref_ops as R
+
+    a, bt = _inputs(1, 0)
+    v, rows, dt = cpu_rate(lambda r: R.gemm(a[:r], bt, "nk").to(torch.bfloat16), M0, 2.0 * N0 * K0,
+                           budget_s, steps, warmup)
+    return {"value": round(v, 4), "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{rows} of {M0} rows of the 4096^3 bf16 GEMM per step, median of {steps} steps "
+                      f"after {warmup} warm-up", "ms_per_step": round(dt * 1e3, 3), "cpu": _cpu_name()}
+
+
+def cpu_baseline(args, budget_s: float = 20.0) -> dict:
+    return _cpu_config2(budget_s, 3, 1)
 
 
 def _cpu_name() -> str:
@@ -305,59 +331,100 @@ def _cpu_name() -> str:
     return "unknown"
 
 
-def workloads(dev) -> dict:
-    """The five BASELINE workloads: name -> (builder, FLOPs).  A builder allocates the
-    seeded inputs on `dev` and returns a zero-argument callable running one step."""
+def _g(seed):
+    return torch.Generator().manual_seed(seed)
+
+
+def host_inputs(key: str):
+    """Seeded CPU inputs of one BASELINE workload, drawn in BASELINE.json's order."""
+    if key == "config1":
+        g = _g(0)
+        a = (torch.rand(1024, 1024, generator=g) * 2 - 1).half()
+        b = (torch.rand(1024, 1024, generator=g) * 2 - 1).half()
+        return {"a": a, "b": b, "bias": (torch.randn(1024, generator=g) * 0.1).half()}
+    if key == "config2":
+        a, bt = _inputs(1, 0)
+        return {"a": a, "b": bt}
+    if key == "config3":
+        g = _g(2)
+        return {"a": torch.randn(8192, 4096, generator=g).bfloat16(),
+                "b": (torch.randn(16384, 4096, generator=g) * 0.02).bfloat16(),
+                "bias": (torch.randn(16384, generator=g) * 0.02).bfloat16()}
+    if key == "config4":
+        g = _g(3)
+        return {"a": torch.randn(16384, 4096, generator=g).bfloat16(),
+                "b": (torch.randn(4096, 4096, generator=g) / 64).bfloat16(),
+                "bias": (torch.randn(4096, generator=g) * 0.02).bfloat16(),
+                "gamma": (1 + torch.randn(4096, generator=g) * 0.02).bfloat16(),
+                "beta": (torch.randn(4096, generator=g) * 0.02).bfloat16()}
+    g = _g(4)
+    return {"x": torch.randn(256, 28, 28, 128, generator=g).bfloat16(),
+            "w": (torch.randn(3, 3, 128, 128, generator=g) / (9 * 128) ** 0.5).bfloat16(),
+            "bias": (torch.randn(128, generator=g) * 0.1).bfloat16()}
+
+
+# name, rows (GEMM M, or conv batch) of the global problem, FLOPs per row, shard alignment
+WORKLOADS = {
+    "config1": ("gemm_bias_relu 1024^3 fp16", 1024, 2.0 * 1024 * 1024, 128),
+    "config2": ("gemm 4096^3 bf16", 4096, 2.0 * 4096 * 4096, 256),
+    "config3": ("gemm_bias_gelu_tanh 8192x16384x4096 bf16", 8192, 2.0 * 16384 * 4096, 256),
+    "config4": ("gemm_bias_layernorm 16384x4096x4096 bf16", 16384, 2.0 * 4096 * 4096, 256),
+    "config5": ("conv2d_bias_relu 256x28x28x128->128 3x3 bf16", 256, 2.0 * 28 * 28 * 128 * 128 * 9, 1),
+}
+
+
+def build_workload(key: str, dev, lo: int = 0, hi: int = None, inputs=None):
+    """Rows [lo, hi) of workload `key` on `dev` through the public operator modules:
+    returns (step, out) where step() runs one call and writes out."""
     from icpp_tuning_b200.conv import conv2d_relu
     from icpp_tuning_b200.gemm import gemm, gemm_bias_act, gemm_bias_layernorm
 
-    def c1():
-        g = torch.Generator().manual_seed(0)
-        a = (torch.rand(1024, 1024, generator=g) * 2 - 1).half().to(dev)
-        b = (torch.rand(1024, 1024, generator=g) * 2 - 1).half().to(dev)
-        bias = (torch.randn(1024, generator=g) * 0.1).half().to(dev)
-        k = gemm_bias_act.build_kernel(1024, 1024, 1024, act="relu", out_dtype=torch.float16)
-        return lambda: k(a, b, bias)
+    t = inputs if inputs is not None else host_inputs(key)
+    hi = WORKLOADS[key][1] if hi is None else hi
+    m = hi - lo
+    if key == "config5":
+        x = t["x"][lo:hi].contiguous().to(dev)
+        wt, bias = t["w"].to(dev), t["bias"].to(dev)
+        y = torch.empty(m, 28, 28, 128, dtype=torch.bfloat16, device=dev)
+        k = conv2d_relu.build_conv2d_relu_kernel(m, 128, 28, 28, 128, 3, 3, 1, 1, 1)
+        return (lambda: k(x, wt, y, bias=bias)), y
+    a = t["a"][lo:hi].contiguous().to(dev)
+    b = t["b"].to(dev)
+    n, kk = (b.shape[1], b.shape[0]) if key == "config1" else (b.shape[0], b.shape[1])
+    if key == "config1":
+        bias = t["bias"].to(dev)
+        k = gemm_bias_act.build_kernel(m, n, kk, act="relu", out_dtype=torch.float16)
+        out = torch.empty(m, n, dtype=torch.float16, device=dev)
+        return (lambda: k(a, b, bias, out=out)), out
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    if key == "config2":
+        k = gemm.build_kernel(m, n, kk, out_dtype=torch.bfloat16, b_layout="nk")
+        return (lambda: k(a, b, out=out)), out
+    if key == "config3":
+        bias = t["bias"].to(dev)
+        k = gemm_bias_act.build_kernel(m, n, kk, act="gelu_tanh", out_dtype=torch.bfloat16, b_layout="nk")
+        return (lambda: k(a, b, bias, out=out)), out
+    bias, gam, bet = (t[x].to(dev) for x in ("bias", "gamma", "beta"))
+    k = gemm_bias_layernorm.build_fused_kernel(m, n, kk, out_dtype=torch.bfloat16, b_layout="nk")
+    return (lambda: k(a, b, bias, gam, bet, out=out)), out
 
-    def c2():
-        a, bt = (t.to(dev) for t in _inputs(1, 0))
-        k = gemm.build_kernel(4096, 4096, 4096, out_dtype=torch.bfloat16, b_layout="nk")
-        return lambda: k(a, bt)
 
-    def c3():
-        g = torch.Generator().manual_seed(2)
-        x = torch.randn(8192, 4096, generator=g).bfloat16().to(dev)
-        w = (torch.randn(16384, 4096, generator=g) * 0.02).bfloat16().to(dev)
-        bias = (torch.randn(16384, generator=g) * 0.02).bfloat16().to(dev)
-        k = gemm_bias_act.build_kernel(8192, 16384, 4096, act="gelu_tanh", out_dtype=torch.bfloat16, b_layout="nk")
-        return lambda: k(x, w, bias)
+def cpu_program(key: str, t: dict):
+    """run(rows): the reference's CPU program (restated in oracle/ref_ops.py) on the first
+    `rows` rows of workload `key`: gemm.py:20-21, gemm_bias_act.py:44-47 (+ GELU-tanh,
+    end2end.py:37-38), gemm_bias_layernorm.py:44-50, conv2d_relu.py:29-60 (+ bias)."""
+    from oracle import ref_ops as R
 
-    def c4():
-        g = torch.Generator().manual_seed(3)
-        x = torch.randn(16384, 4096, generator=g).bfloat16().to(dev)
-        w = (torch.randn(4096, 4096, generator=g) / 64).bfloat16().to(dev)
-        bias = (torch.randn(4096, generator=g) * 0.02).bfloat16().to(dev)
-        gam = (1 + torch.randn(4096, generator=g) * 0.02).bfloat16().to(dev)
-        bet = (torch.randn(4096, generator=g) * 0.02).bfloat16().to(dev)
-        k = gemm_bias_layernorm.build_fused_kernel(16384, 4096, 4096, out_dtype=torch.bfloat16, b_layout="nk")
-        return lambda: k(x, w, bias, gam, bet)
-
-    def c5():
-        g = torch.Generator().manual_seed(4)
-        x = torch.randn(256, 28, 28, 128, generator=g).bfloat16().to(dev)
-        wt = (torch.randn(3, 3, 128, 128, generator=g) / (9 * 128) ** 0.5).bfloat16().to(dev)
-        bias = (torch.randn(128, generator=g) * 0.1).bfloat16().to(dev)
-        y = torch.empty(256, 28, 28, 128, dtype=torch.bfloat16, device=dev)
-        k = conv2d_relu.build_conv2d_relu_kernel(256, 128, 28, 28, 128, 3, 3, 1, 1, 1)
-        return lambda: k(x, wt, y, bias=bias)
-
-    return {
-        "config1": ("gemm_bias_relu 1024^3 fp16", c1, 2.0 * 1024 ** 3),
-        "config2": ("gemm 4096^3 bf16", c2, 2.0 * 4096 ** 3),
-        "config3": ("gemm_bias_gelu_tanh 8192x16384x4096 bf16", c3, 2.0 * 8192 * 16384 * 4096),
-        "config4": ("gemm_bias_layernorm 16384x4096x4096 bf16", c4, 2.0 * 16384 * 4096 * 4096),
-        "config5": ("conv2d_bias_relu 256x28x28x128->128 3x3 bf16", c5, 2.0 * 256 * 28 * 28 * 128 * 128 * 9),
-    }
+    if key == "config1":
+        return lambda r: R.gemm_bias_act(t["a"][:r], t["b"], t["bias"], "relu").to(torch.float16)
+    if key == "config2":
+        return lambda r: R.gemm(t["a"][:r], t["b"], "nk").to(torch.bfloat16)
+    if key == "config3":
+        return lambda r: R.gemm_bias_act(t["a"][:r], t["b"], t["bias"], "gelu_tanh", b_layout="nk").to(torch.bfloat16)
+    if key == "config4":
+        return lambda r: R.gemm_bias_layernorm(t["a"][:r], t["b"], t["bias"], t["gamma"], t["beta"],
+                                               b_layout="nk", out_dtype=torch.bfloat16)
+    return lambda r: R.conv2d_bias_relu(t["x"][:r], t["w"], t["bias"], out_dtype=torch.bfloat16)
 
 
 def time_steps(fn, steps: int, flush) -> float:
@@ -376,22 +443,61 @@ def time_steps(fn, steps: int, flush) -> float:
 
 
 def per_op_table(args) -> list:
-    """Device-timed TFLOP/s of all five BASELINE workloads (config2 is the headline)."""
+    """Device-timed TFLOP/s of all five BASELINE workloads (config2 is the headline), each
+    beside the reference's CPU program on the same inputs (bounded row sample)."""
     dev = torch.device("cuda", torch.cuda.current_device())
     peak = _peaks()[0]
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
     steps = max(5, min(args.steps, 20))
     res = []
-    for key, (name, build, flops) in workloads(dev).items():
-        fn = build()
+    for key, (name, rows, fpr, _) in WORKLOADS.items():
+        t = host_inputs(key)
+        fn, _out = build_workload(key, dev, inputs=t)
         for _ in range(3):
             fn()
         torch.cuda.synchronize()
         ms = time_steps(fn, steps, flush)
-        tf = flops / (ms / 1e3) / 1e12
-        res.append({"op": f"{key} {name}", "ms": round(ms, 5), "tflops": round(tf, 2),
-                    "frac_measured": round(tf / peak, 4), "frac_nominal": round(tf / 2250.0, 4)})
-        del fn
+        tf = fpr * rows / (ms / 1e3) / 1e12
+        row = {"op": f"{key} {name}", "ms": round(ms, 5), "tflops": round(tf, 2),
+               "frac_measured": round(tf / peak, 4), "frac_nominal": round(tf / 2250.0, 4)}
+        if not args.no_cpu:
+            cv, crows, _ = cpu_rate(cpu_program(key, t), rows, fpr, args.cpu_budget / 5, 3, 1)
+            row.update({"cpu_tflops": round(cv, 4), "cpu_sample_rows": crows, "gpu_over_cpu": round(tf / cv, 1)})
+        res.append(row)
+        del fn, _out
+        torch.cuda.empty_cache()
+    return res
+
+
+def strong_table(args, ws: int, rank: int, dist) -> list:
+    """Strong scaling (N > 1): each fixed global workload split into contiguous row (or
+    image) shards, one per rank, weights replicated, no collective on the data path.
+    Throughput = global FLOPs / the max over ranks of the per-shard device time.  The
+    NCCL all-gather that assembles the whole output on every rank (shard.gather_rows) is
+    timed separately."""
+    from icpp_tuning_b200 import shard
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    steps = max(5, min(args.steps, 20))
+    res = []
+    for key, (name, rows, fpr, align) in WORKLOADS.items():
+        lo, hi = shard.row_shard(rows, ws, rank, align)
+        fn, out = build_workload(key, dev, lo, hi)
+        for _ in range(3):
+            fn()
+        _barrier(dist)
+        ms = _max_over_ranks(time_steps(fn, steps, flush), dist)
+        tf = fpr * rows / (ms / 1e3) / 1e12
+        entry = {"op": f"{key} {name}", "global_rows": rows, "rows_per_rank": hi - lo, "ms": round(ms, 5),
+                 "tflops": round(tf, 2)}
+        flat = out.reshape(out.shape[0], -1)
+        _barrier(dist)
+        g_ms = _max_over_ranks(time_steps(lambda: shard.gather_rows(flat, rows), 3, flush), dist)
+        entry["allgather_ms"] = round(g_ms, 4)
+        entry["allgather_bytes"] = rows * flat.shape[1] * flat.element_size()
+        res.append(entry)
+        del fn, out, flat
         torch.cuda.empty_cache()
     return res
 
@@ -400,44 +506,34 @@ def profile_op(args):
     """--profile --op configN: W warm-up steps then K timed steps of one workload, for ncu."""
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    name, build, flops = workloads(dev)[args.op]
-    fn = build()
+    name, rows, fpr, _ = WORKLOADS[args.op]
+    fn, _out = build_workload(args.op, dev)
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
     for _ in range(args.warmup):
         fn()
     torch.cuda.synchronize()
     ms = time_steps(fn, args.steps, flush)
-    print(json.dumps({"profile_run": args.op, "workload": name, "ms": ms, "tflops": flops / (ms / 1e3) / 1e12}))
+    print(json.dumps({"profile_run": args.op, "workload": name, "ms": ms, "tflops": fpr * rows / (ms / 1e3) / 1e12}))
+
+
+def _config(ws: int) -> dict:
+    """The workload description both arms print (the driver compares them)."""
+    return {"workload": WORKLOAD, "parallelism": f"M-shard x{ws} (weak: 4096 rows per GPU)",
+            "l2": "flushed between timed steps (256 MiB write outside the events)"}
 
 
 def run_reference(args):
     """The reference's CPU implementation of the path (its PyTorch program, restated in
     oracle/ref_ops.py) on the host cores, same metric and workload, bounded samples."""
-    from oracle import ref_ops as R
-
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     if int(os.environ.get("RANK", "0")) != 0:
         return
-    torch.set_num_threads(os.cpu_count() or 1)
-    a, bt = _inputs(1, 0)
-    t0 = time.perf_counter()
-    R.gemm(a[:256], bt, "nk").to(torch.bfloat16)
-    t_row = (time.perf_counter() - t0) / 256
-    budget = 120.0
-    rows = int(max(64, min(M0, budget / max(1, args.steps + args.warmup) / max(t_row, 1e-9))))
-    for _ in range(args.warmup):
-        R.gemm(a[:rows], bt, "nk").to(torch.bfloat16)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        R.gemm(a[:rows], bt, "nk").to(torch.bfloat16)
-    dt = (time.perf_counter() - t0) / args.steps
-    v = round(2.0 * rows * N0 * K0 / dt / 1e12, 4)
+    cb = _cpu_config2(min(120.0, 3.0 * (args.steps + args.warmup)), args.steps, args.warmup)
+    v = cb["value"]
     line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "ms_per_step": cb["ms_per_step"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic (seeded randn, BASELINE configs[1] shapes)", "impl": "reference",
-            "config": {"workload": WORKLOAD, "parallelism": "host CPU, rank 0 only"},
-            "cpu_baseline": {"value": v, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-                             "sample": f"{rows} of {M0} rows per step", "cpu": _cpu_name()},
+            "config": _config(ws), "cpu_baseline": cb,
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
