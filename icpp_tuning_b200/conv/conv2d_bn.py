@@ -66,14 +66,14 @@ def build_bn_kernel(desc, N, C, H, W, F_out, KH, KW, S, P, D, config, eps, relu,
     cfg = fused.as_tile_cfg(config)
     OH, OW = calc_oh_ow(H, W, KH, KW, S, P, D)
     ws_bytes = fused.conv_workspace_bytes(N, H, W, C, F_out, KH, KW, S, P, D, config=cfg)
-    # zero-filled once; the kernel leaves its split-K counters zeroed after every call
-    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device="cuda") if ws_bytes > 0 else None
+    # zero-filled once per stream; the kernel leaves its split-K counters zeroed after every call
+    wss = fused.StreamWorkspaces(ws_bytes)
 
     def run(X, Wt, bn, Y, residual=None):
         if tuple(X.shape) != (N, H, W, C) or tuple(Wt.shape) != (KH, KW, C, F_out):
             raise ValueError("input shapes differ from the built shape")
         fused.conv2d_nhwc(X, Wt, bn=bn, bn_eps=eps, relu=relu, residual=residual, stride=S, padding=P, dilation=D,
-                          out=Y, workspace=ws, config=cfg)
+                          out=Y, workspace=wss.get(), config=cfg)
         return Y
 
     if with_residual:
@@ -85,7 +85,7 @@ def build_bn_kernel(desc, N, C, H, W, F_out, KH, KW, S, P, D, config, eps, relu,
 
     kernel.config = config
     kernel.out_shape = (N, OH, OW, F_out)
-    kernel.workspace = ws
+    kernel.workspace = wss.default
     return kernel
 
 

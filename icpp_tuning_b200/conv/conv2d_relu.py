@@ -52,16 +52,16 @@ def build_conv2d_relu_kernel(N, C, H, W, F_out, KH, KW, S=1, P=1, D=1, config=No
     cfg = fused.as_tile_cfg(config)
     OH, OW = calc_oh_ow(H, W, KH, KW, S, P, D)
     ws_bytes = fused.conv_workspace_bytes(N, H, W, C, F_out, KH, KW, S, P, D, config=cfg)
-    # zero-filled once; the kernel leaves its split-K counters zeroed after every call
-    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device="cuda") if ws_bytes > 0 else None
+    # zero-filled once per stream; the kernel leaves its split-K counters zeroed after every call
+    wss = fused.StreamWorkspaces(ws_bytes)
 
     def kernel(X, Wt, Y, bias=None):
         if tuple(X.shape) != (N, H, W, C) or tuple(Wt.shape) != (KH, KW, C, F_out):
             raise ValueError("input shapes differ from the built shape")
-        fused.conv2d_nhwc(X, Wt, bias=bias, relu=True, stride=S, padding=P, dilation=D, out=Y, workspace=ws, config=cfg)
+        fused.conv2d_nhwc(X, Wt, bias=bias, relu=True, stride=S, padding=P, dilation=D, out=Y, workspace=wss.get(), config=cfg)
         return Y
 
     kernel.config = config
     kernel.out_shape = (N, OH, OW, F_out)
-    kernel.workspace = ws
+    kernel.workspace = wss.default
     return kernel

@@ -83,6 +83,33 @@ def as_tile_cfg(cfg) -> N.FoTileCfg:
                       split_mode=int(cfg.get("split_mode", 0)), ln_mode=int(cfg.get("ln_mode", 0)))
 
 
+class StreamWorkspaces:
+    """Zero-filled workspaces of one built operator, one per CUDA stream it runs on.
+
+    The split-K tail and the one-kernel LayerNorm keep counters in their workspace that
+    each call leaves zeroed; two calls that overlap on the GPU (on different streams)
+    must not share one.  The workspace of the stream current at build time is allocated
+    up front; another stream gets its own on its first call (calls on one stream are
+    ordered, so they share it)."""
+
+    def __init__(self, nbytes: int, device: Optional[torch.device] = None):
+        self.nbytes = int(nbytes)
+        self.device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self._by_stream = {}
+        self.default = self.get(torch.cuda.current_stream(self.device))
+
+    def get(self, stream=None) -> Optional[torch.Tensor]:
+        if self.nbytes <= 0:
+            return None
+        s = torch.cuda.current_stream(self.device) if stream is None else stream
+        ws = self._by_stream.get(s.cuda_stream)
+        if ws is None:
+            with torch.cuda.stream(s):
+                ws = torch.zeros(max(16, self.nbytes), dtype=torch.uint8, device=self.device)
+            self._by_stream[s.cuda_stream] = ws
+        return ws
+
+
 def workspace_bytes(M: int, N_: int, K: int, epilogue: str, cfg) -> int:
     """Workspace fo_gemm uses for this problem: LayerNorm statistics (required) or, for
     the other epilogues, fp32 partials of the split-K tail (optional, zero-filled)."""

@@ -51,16 +51,15 @@ def build_kernel(M: int, N: int, K: int, config: Optional[Dict[str, Any]] = None
     if config is None:
         config, _ = select_best(DESCRIPTOR, M=M, N=N, K=K, out_bytes=torch.empty((), dtype=out_dtype).element_size())
     cfg = fused.as_tile_cfg(config)
-    ws_bytes = fused.workspace_bytes(M, N, K, "none", cfg)
-    # zero-filled once; the kernel leaves its split-K counters zeroed after every call
-    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device="cuda") if ws_bytes > 0 else None
+    # split-K workspace: zero-filled once per stream, left zeroed by every call
+    wss = fused.StreamWorkspaces(fused.workspace_bytes(M, N, K, "none", cfg))
 
     def kernel(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         _check_shape(a, b, M, N, K, b_layout)
-        return fused.gemm(a, b, b_layout=b_layout, out=out, out_dtype=out_dtype, workspace=ws, config=cfg)
+        return fused.gemm(a, b, b_layout=b_layout, out=out, out_dtype=out_dtype, workspace=wss.get(), config=cfg)
 
     kernel.config = config
-    kernel.workspace = ws
+    kernel.workspace = wss.default
     return kernel
 
 

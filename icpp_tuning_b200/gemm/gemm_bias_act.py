@@ -62,16 +62,16 @@ def build_kernel(M: int, N: int, K: int, config: Optional[Dict[str, Any]] = None
                                 out_bytes=torch.empty((), dtype=out_dtype).element_size())
     cfg = fused.as_tile_cfg(config)
     ws_bytes = fused.workspace_bytes(M, N, K, "none", cfg)
-    # zero-filled once; the kernel leaves its split-K counters zeroed after every call
-    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device="cuda") if ws_bytes > 0 else None
+    # zero-filled once per stream; the kernel leaves its split-K counters zeroed after every call
+    wss = fused.StreamWorkspaces(ws_bytes)
     epi = _EPI[act]
 
     def kernel(a: torch.Tensor, b: torch.Tensor, bias: torch.Tensor,
                out: Optional[torch.Tensor] = None) -> torch.Tensor:
         _check_shape(a, b, M, N, K, b_layout)
         return fused.gemm(a, b, b_layout=b_layout, epilogue=epi, bias=bias, out=out, out_dtype=out_dtype,
-                          workspace=ws, config=cfg)
+                          workspace=wss.get(), config=cfg)
 
     kernel.config = config
-    kernel.workspace = ws
+    kernel.workspace = wss.default
     return kernel

@@ -82,22 +82,23 @@ def build_fused_kernel(M: int, N: int, K: int, gemm_config: Optional[Dict[str, A
                        eps: float = 1e-5, out_dtype: torch.dtype = torch.float16, b_layout: str = "kn",
                        device: Optional[torch.device] = None):
     """Returns fused_kernel(A, B, bias, gamma, beta) -> Y[M, N] (out_dtype, fp16 default
-    as in the reference).  The statistics workspace is allocated here, once, on `device`
-    (default: the current CUDA device) and reused by every call.  Calls that share one
-    built kernel must not overlap on the GPU."""
+    as in the reference).  The statistics workspace (zero-filled) is allocated here on
+    `device` (default: the current CUDA device) for the current stream, and once more for
+    every other stream the kernel is called on, so calls on different streams never
+    share one."""
     assert N % block_N_ln == 0, f"N={N} must be divisible by block_N_ln={block_N_ln}"
     if gemm_config is None:
         gemm_config, _ = select_best(DESCRIPTOR, M=M, N=N, K=K,
                                      out_bytes=torch.empty((), dtype=out_dtype).element_size())
     cfg = fused.as_tile_cfg(gemm_config)
     dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
-    ws = torch.zeros(max(16, fused.ln_workspace_bytes(M, N, cfg)), dtype=torch.uint8, device=dev)
+    wss = fused.StreamWorkspaces(fused.ln_workspace_bytes(M, N, cfg), dev)
 
     def fused_kernel(A, B, bias, gamma, beta, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         _check_shape(A, B, M, N, K, b_layout)
         return fused.gemm(A, B, b_layout=b_layout, epilogue="bias_layernorm", bias=bias, gamma=gamma,
-                          beta=beta, eps=eps, out=out, out_dtype=out_dtype, workspace=ws, config=cfg)
+                          beta=beta, eps=eps, out=out, out_dtype=out_dtype, workspace=wss.get(), config=cfg)
 
     fused_kernel.config = gemm_config
-    fused_kernel.workspace = ws
+    fused_kernel.workspace = wss.default
     return fused_kernel
