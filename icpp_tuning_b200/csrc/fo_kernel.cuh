@@ -845,19 +845,12 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
     // ((x - shift) + (shift - mean)) * rstd * gamma + beta and stores it.  `tail`: no
     // newer stores of this warp follow the slice's own, so wait for all of them.
     auto ln_normalize = [&](int tm_, int tn_, float sh_, bool tail) -> bool {
-#if FO_LN_EXP == 2
-      return true;
-#endif
       const int r0 = tm_ * kTileM + static_cast<int>(rank) * kBM + quarter * 32;
       if (r0 >= p.M) return true;
       const int grp = r0 >> 5;
       const int target = 2 * p.tiles_n + 1;
       int ready = 1;
-#if FO_LN_EXP == 1
-      if (false) {
-#else
       if (lane == 0) {
-#endif
         const int* cp = p.ln_cnt + grp;
         if (ld_acquire_gpu(cp) < target) {
           const uint64_t t0 = global_timer_ns();
@@ -873,10 +866,11 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
       ready = __shfl_sync(0xffffffffu, ready, 0);
       __syncwarp();
       if (!ready) return false;
+      // lane i holds row r0 + i's rstd and (shift - mean) * rstd
       const int row = r0 + lane;
       const float2 fin = row < p.M ? __ldcg(p.ln_fin + row) : make_float2(0.f, 0.f);
       const float rs = fin.y;
-      const float off = sh_ - fin.x;
+      const float ors = (sh_ - fin.x) * fin.y;
       if (lane == 0 && atomicAdd(p.ln_cnt + p.ln_groups + grp, 1) == target - 2) {
         // every normaliser of these rows has seen the arrivals: reset both counters
         atomicExch(p.ln_cnt + grp, 0);
@@ -885,6 +879,16 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
 #pragma unroll 1
       for (int ci = 0; ci < kHalfChunks; ++ci) {
         const int cbase = tn_ * BN + hcol + ci * kCW;
+        // This lane's two columns of the 64-column chunk and their affine parameters,
+        // loaded once for the chunk's 32 rows.
+        const int col = cbase + 2 * lane;
+        float g0 = 0.f, g1 = 0.f, b0 = 0.f, b1 = 0.f;
+        if (col < p.N) {
+          g0 = load_vec(p.gamma, p.vec_dtype, col);
+          g1 = load_vec(p.gamma, p.vec_dtype, col + 1);
+          b0 = load_vec(p.beta, p.vec_dtype, col);
+          b1 = load_vec(p.beta, p.vec_dtype, col + 1);
+        }
         if (lane == 0) {
           // the slice's stores have completed (only the newer stores of the current unit
           // may still be in flight) and the staging block is free
@@ -900,33 +904,19 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
         }
         if (!mbar_wait(lnbar, ln_ph, tmo, abort_flag)) return false;
         ln_ph ^= 1;
-        const uint32_t rowp = buf0 + lane * 128;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int col = cbase + 8 * j;
-          float g[8], b[8];
-          if (col < p.N) {
-            load_vec8(p.gamma, p.vec_dtype, col, g);
-            load_vec8(p.beta, p.vec_dtype, col, b);
-          } else {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) g[e] = b[e] = 0.f;
-          }
-          const uint32_t addr = rowp + ((j ^ (lane & 7)) << 4);
-          uint32_t w[4];
-          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-                       : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3])
-                       : "r"(addr)
-                       : "memory");
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = unpack2<OUT_DT>(w[e]);
-            w[e] = pack2<OUT_DT>(fmaf((f.x + off) * rs, g[2 * e], b[2 * e]),
-                                 fmaf((f.y + off) * rs, g[2 * e + 1], b[2 * e + 1]));
-          }
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w[0]), "r"(w[1]), "r"(w[2]),
-                       "r"(w[3])
-                       : "memory");
+        // Row i of the staged 32 x 128 B block; this lane's 4 bytes sit in 16-byte chunk
+        // lane / 4, swizzled by the row (32 lanes: 32 distinct banks).
+#pragma unroll 8
+        for (int i = 0; i < 32; ++i) {
+          const float r = __shfl_sync(0xffffffffu, rs, i);
+          const float o = __shfl_sync(0xffffffffu, ors, i);
+          const uint32_t addr = buf0 + i * 128 + ((((lane >> 2) ^ (i & 7)) << 4) | ((lane & 3) << 2));
+          uint32_t w;
+          asm volatile("ld.shared.b32 %0, [%1];" : "=r"(w) : "r"(addr) : "memory");
+          const float2 f = unpack2<OUT_DT>(w);
+          // ((x - shift) + (shift - mean)) * rstd * gamma + beta
+          w = pack2<OUT_DT>(fmaf(fmaf(f.x, r, o), g0, b0), fmaf(fmaf(f.y, r, o), g1, b1));
+          asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(w) : "memory");
         }
         fence_proxy_async_smem();
         __syncwarp();
