@@ -18,7 +18,8 @@ running this design (docs/cost_model.md of the reference describes the factor id
   eff_implicit_conv conv only: rate of the TMA im2col loads relative to tiled loads
   eff_epilogue      overlap of the epilogue (TMEM -> registers -> TMA store) with the
                     next tile's mainloop (two TMEM accumulators)
-  eff_reduction     LayerNorm only: the stream-ordered in-place normalisation pass
+  eff_reduction     LayerNorm only: the normalisation (in the GEMM kernel for block_n >=
+                    128, else a stream-ordered in-place pass)
 
 score = product = (ideal tensor time) / (predicted time).  The constants in CONSTANTS
 are fitted to B200 measurements of these kernels.
@@ -52,6 +53,10 @@ CONSTANTS = {
     # LayerNorm normalisation pass (separate stream-ordered kernel), read + write bytes/s:
     # 16384 x 4096 bf16 measured ~100 us on top of the GEMM
     "ln_pass_bytes_per_s": 2.6e12,
+    # one-kernel LayerNorm (block_n >= 128): the epilogue's statistics and in-place
+    # normalisation, per read + write byte of the output (config4: 58 us over the plain
+    # GEMM + bias kernel for 2 x 128 MiB)
+    "ln_fused_bytes_per_s": 4.6e12,
     # TMA im2col loads (one 128-pixel x 64-channel box per filter tap) run at this share
     # of a tiled load's rate: measured 589 vs 836 TFLOP/s for BN=128 conv vs GEMM tiles
     "im2col_rate": 0.7,
@@ -232,7 +237,8 @@ def _model(op: OpSpec, c: TuneConfig, hw: GPUSpec) -> dict:
     # -- LayerNorm: one normalisation pass (read + write) per 128-row block
     t_ln = 0.0
     if op.has_reduction_epilogue:
-        t_ln = 2.0 * op.M * op.N * ml.output_element_bytes / K["ln_pass_bytes_per_s"]
+        rate = K["ln_fused_bytes_per_s"] if bn >= 128 else K["ln_pass_bytes_per_s"]
+        t_ln = 2.0 * op.M * op.N * ml.output_element_bytes / rate
     # split-K tail (GEMM, CTA pairs included, and single-CTA conv, with a workspace): the
     # last, less than half-full wave is split along K, so it costs 1/split of a wave plus
     # the partials' reduction

@@ -1391,25 +1391,35 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
 #pragma unroll
         for (int i = 0; i < kCW; ++i) v[i] = apply_act<ACT>(v[i]);
         if constexpr (LN) {
+          // Shifted sums: shift = the row's first value of this slice (a sample of the
+          // row, so |mean - shift| is of the order of the row's spread), d = x - shift,
+          // S1 = sum d, S2 = sum d^2; the slice's (mean, M2) = (shift + S1 / n,
+          // S2 - S1^2 / n).  d is also what is stored: the 16-bit rounding then scales
+          // with the row's spread, not with its mean; the normaliser adds
+          // (shift - row mean) back in fp32.
+          if (ci == 0) shift = v[0];
           const int cv = min(kCW, p.N - cbase);
-          if (cv > 0) {
-            float sum = 0.f;
-#pragma unroll
-            for (int i = 0; i < kCW; ++i) sum += (i < cv) ? v[i] : 0.f;
-            const float cm = sum / static_cast<float>(cv);
-            float q = 0.f;
+          float s1[4] = {0.f, 0.f, 0.f, 0.f}, s2[4] = {0.f, 0.f, 0.f, 0.f};
+          if (cv >= kCW) {
 #pragma unroll
             for (int i = 0; i < kCW; ++i) {
-              const float d = v[i] - cm;
-              q += (i < cv) ? d * d : 0.f;
+              const float d = v[i] - shift;
+              s1[i & 3] += d;
+              s2[i & 3] = fmaf(d, d, s2[i & 3]);
+              v[i] = d;
             }
-            chan_merge(st_cnt, st_mean, st_m2, static_cast<float>(cv), cm, q);
-            if (ci == 0) shift = cm;
-          }
-          // Store x - shift: the bf16/fp16 rounding then scales with the row's spread,
-          // not with its mean; the normaliser adds (shift - row mean) back in fp32.
+          } else {
 #pragma unroll
-          for (int i = 0; i < kCW; ++i) v[i] -= shift;
+            for (int i = 0; i < kCW; ++i) {
+              const float d = i < cv ? v[i] - shift : 0.f;
+              s1[i & 3] += d;
+              s2[i & 3] = fmaf(d, d, s2[i & 3]);
+              v[i] = d;
+            }
+          }
+          st_cnt += static_cast<float>(max(cv, 0));
+          st_mean += (s1[0] + s1[1]) + (s1[2] + s1[3]);  // S1 until the slice ends
+          st_m2 += (s2[0] + s2[1]) + (s2[2] + s2[3]);    // S2 until the slice ends
         }
         if constexpr (kNarrow) {
           // 16-bit BN 64: lane l stores row row0 + l of this 32-column half, 64
@@ -1469,6 +1479,14 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
 
       if constexpr (LN) {
         const int row = row0 + lane;
+        // (S1, S2) of the slice's shifted values -> (mean, M2)
+        if (st_cnt > 0.f) {
+          const float s1 = st_mean;
+          st_mean = shift + s1 / st_cnt;
+          st_m2 = fmaxf(0.f, st_m2 - s1 * (s1 / st_cnt));
+        } else {
+          st_mean = st_m2 = 0.f;
+        }
         if (!kNarrow && p.ln_fused) {
           // Publish this slice's (mean, M2), count it into its 32 rows' arrivals, hold
           // it, and normalise the oldest held slice once ln_defer newer ones exist.

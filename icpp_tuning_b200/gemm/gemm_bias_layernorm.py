@@ -38,7 +38,10 @@ def torch_baseline(A, B, bias, gamma, beta):
 
 
 def get_gemm_configs(K: int = 0) -> List[Dict[str, Any]]:
-    return tcgen05_configs()
+    """Row-major tile rasters only: the one-kernel LayerNorm normalises a slice once its
+    row block's tiles are done, which a row-major raster finishes soonest (config4 388 us
+    against 402 us with group_m 8, which also defers slices twice as long)."""
+    return tcgen05_configs(group_ms=(0,))
 
 
 class GemmBiasLayerNormDescriptor(Tcgen05Descriptor):
