@@ -61,13 +61,12 @@ cudaError_t launch_tc_k(const LaunchArgs& a) {
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = a.smem;
     cfg.stream = a.stream;
-    cudaLaunchAttribute attr[3];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     attr[1] = pdl;
-    attr[2] = coop;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     // A persistent grid larger than the number of co-resident pairs would leave a tail
@@ -86,7 +85,8 @@ cudaError_t launch_tc_k(const LaunchArgs& a) {
     // the one-kernel LayerNorm's wait depth follows the number of pairs actually launched
     if (LN && a.p.ln_fused && ln_defer_for(a.p.ln_span, static_cast<int>(cfg.gridDim.x) / 2) > kLnMaxDefer)
       return cudaErrorCooperativeLaunchTooLarge;
-    cfg.numAttrs = a.coop ? 3 : 2;
+    if (a.coop) attr[1] = coop;  // a cooperative grid is not a programmatic dependent
+    cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, kern, a.tmA, a.tmB, a.tmC, a.p);
   } else {
     if (a.csplit > 1) {
@@ -126,9 +126,9 @@ cudaError_t launch_tc_k(const LaunchArgs& a) {
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = a.smem;
     cfg.stream = a.stream;
-    cudaLaunchAttribute attr[2] = {pdl, coop};
+    cudaLaunchAttribute attr[1] = {a.coop ? coop : pdl};  // a cooperative grid is not a programmatic dependent
     cfg.attrs = attr;
-    cfg.numAttrs = a.coop ? 2 : 1;
+    cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kern, a.tmA, a.tmB, a.tmC, a.p);
   }
 }
