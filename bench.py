@@ -373,9 +373,10 @@ WORKLOADS = {
 }
 
 
-def build_workload(key: str, dev, lo: int = 0, hi: int = None, inputs=None):
+def build_workload(key: str, dev, lo: int = 0, hi: int = None, inputs=None, config=None):
     """Rows [lo, hi) of workload `key` on `dev` through the public operator modules:
-    returns (step, out) where step() runs one call and writes out."""
+    returns (step, out) where step() runs one call and writes out.  `config`: a raw tile
+    config replacing the autotuner's pick (profiling runs)."""
     from icpp_tuning_b200.conv import conv2d_relu
     from icpp_tuning_b200.gemm import gemm, gemm_bias_act, gemm_bias_layernorm
 
@@ -386,26 +387,26 @@ def build_workload(key: str, dev, lo: int = 0, hi: int = None, inputs=None):
         x = t["x"][lo:hi].contiguous().to(dev)
         wt, bias = t["w"].to(dev), t["bias"].to(dev)
         y = torch.empty(m, 28, 28, 128, dtype=torch.bfloat16, device=dev)
-        k = conv2d_relu.build_conv2d_relu_kernel(m, 128, 28, 28, 128, 3, 3, 1, 1, 1)
+        k = conv2d_relu.build_conv2d_relu_kernel(m, 128, 28, 28, 128, 3, 3, 1, 1, 1, config=config)
         return (lambda: k(x, wt, y, bias=bias)), y
     a = t["a"][lo:hi].contiguous().to(dev)
     b = t["b"].to(dev)
     n, kk = (b.shape[1], b.shape[0]) if key == "config1" else (b.shape[0], b.shape[1])
     if key == "config1":
         bias = t["bias"].to(dev)
-        k = gemm_bias_act.build_kernel(m, n, kk, act="relu", out_dtype=torch.float16)
+        k = gemm_bias_act.build_kernel(m, n, kk, config=config, act="relu", out_dtype=torch.float16)
         out = torch.empty(m, n, dtype=torch.float16, device=dev)
         return (lambda: k(a, b, bias, out=out)), out
     out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
     if key == "config2":
-        k = gemm.build_kernel(m, n, kk, out_dtype=torch.bfloat16, b_layout="nk")
+        k = gemm.build_kernel(m, n, kk, config=config, out_dtype=torch.bfloat16, b_layout="nk")
         return (lambda: k(a, b, out=out)), out
     if key == "config3":
         bias = t["bias"].to(dev)
-        k = gemm_bias_act.build_kernel(m, n, kk, act="gelu_tanh", out_dtype=torch.bfloat16, b_layout="nk")
+        k = gemm_bias_act.build_kernel(m, n, kk, config=config, act="gelu_tanh", out_dtype=torch.bfloat16, b_layout="nk")
         return (lambda: k(a, b, bias, out=out)), out
     bias, gam, bet = (t[x].to(dev) for x in ("bias", "gamma", "beta"))
-    k = gemm_bias_layernorm.build_fused_kernel(m, n, kk, out_dtype=torch.bfloat16, b_layout="nk")
+    k = gemm_bias_layernorm.build_fused_kernel(m, n, kk, gemm_config=config, out_dtype=torch.bfloat16, b_layout="nk")
     return (lambda: k(a, b, bias, gam, bet, out=out)), out
 
 
@@ -502,12 +503,25 @@ def strong_table(args, ws: int, rank: int, dist) -> list:
     return res
 
 
+def _tile_arg(args):
+    """--tile BM,BN,BK,STAGES,GROUP[,key=value...] -> a raw config dict (None: autotuner)."""
+    if not args.tile:
+        return None
+    f = args.tile.split(",")
+    c = {"block_M": int(f[0]), "block_N": int(f[1]), "block_K": int(f[2]), "num_stages": int(f[3]),
+         "group_m": int(f[4]), "thread_num": 320}
+    for kv in f[5:]:
+        k, v = kv.split("=")
+        c[k] = int(v)
+    return c
+
+
 def profile_op(args):
     """--profile --op configN: W warm-up steps then K timed steps of one workload, for ncu."""
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     name, rows, fpr, _ = WORKLOADS[args.op]
-    fn, _out = build_workload(args.op, dev)
+    fn, _out = build_workload(args.op, dev, config=_tile_arg(args))
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
     for _ in range(args.warmup):
         fn()
@@ -549,6 +563,7 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--op", default="config2", choices=["config1", "config2", "config3", "config4", "config5"],
                     help="with --profile: the workload to run")
+    ap.add_argument("--tile", default="", help="with --profile: BM,BN,BK,STAGES,GROUP[,ln_mode=1,swap_ab=2,...]")
     ap.add_argument("--profile", action="store_true",
                     help="timed steps only (no e2e, CPU baseline, per-op table or clock hold): for ncu")
     args = ap.parse_args()

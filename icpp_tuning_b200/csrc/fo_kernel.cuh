@@ -921,7 +921,8 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(&tmC, buf0, cbase, r0);
+          // final values: written back first, before the slices still to be read back
+          tma_store_2d_hint(&tmC, buf0, cbase, r0, l2_policy_evict_first());
           bulk_commit();
         }
         ++nstore;
@@ -1468,7 +1469,12 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&tmC, buf, cbase, row0);
+            if (LN && p.ln_fused) {
+              // the centred slice is read back a unit later: keep it in L2
+              tma_store_2d_hint(&tmC, buf, cbase, row0, l2_policy_evict_last());
+            } else {
+              tma_store_2d(&tmC, buf, cbase, row0);
+            }
             bulk_commit();
           }
           ++nstore;
