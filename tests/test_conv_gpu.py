@@ -61,9 +61,9 @@ def test_config5_conv_full():
     kern = conv2d_relu.build_conv2d_relu_kernel(256, 128, 28, 28, 128, 3, 3, 1, 1, 1)
     y = torch.empty(256, 28, 28, 128, dtype=torch.bfloat16, device="cuda")
     kern(*cuda(x, wt), y, bias=bias.cuda())
-    sl = slice(0, 256, 17)
-    ref = R.conv2d_bias_relu(x[sl], wt, bias, True, 1, 1, 1, out_dtype=torch.bfloat16)
-    assert_close(y[sl], ref, TOL)
+    # every image (the CPU oracle takes well under a second for all 256)
+    ref = R.conv2d_bias_relu(x, wt, bias, True, 1, 1, 1, out_dtype=torch.bfloat16)
+    assert_close(y, ref, TOL)
     status_clean()
 
 

@@ -172,9 +172,8 @@ def test_config3_gemm_bias_gelu_mlp():
     from icpp_tuning_b200.gemm import gemm_bias_act
     k = gemm_bias_act.build_kernel(8192, 16384, 4096, act="gelu_tanh", out_dtype=torch.bfloat16, b_layout="nk")
     out = k(*cuda(x, w, bias))
-    # full-size check on a row sample (the CPU oracle of all 8192 rows takes ~minutes)
-    rows = torch.arange(0, 8192, 61)
-    assert_close(out[rows.cuda()], R.gemm_bias_act(x[rows], w, bias, "gelu_tanh", "nk"), TOL)
+    # every row (the CPU oracle takes ~10 s on a 16-core host)
+    assert_close(out, R.gemm_bias_act(x, w, bias, "gelu_tanh", "nk"), TOL)
     status_clean()
 
 

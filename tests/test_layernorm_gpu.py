@@ -140,9 +140,9 @@ def test_config4_ln_full():
     n0 = N.launch_count()
     out = k(*cuda(x, w, bias, gamma, beta))
     assert N.launch_count() - n0 == 1  # the tuned config runs the one-kernel LayerNorm
-    rows = torch.arange(0, M, 97)
-    ref = R.gemm_bias_layernorm(x[rows], w, bias, gamma, beta, b_layout="nk", out_dtype=torch.bfloat16)
-    assert_close(out[rows.cuda()], ref, TOL_LN)
+    # every row (the CPU oracle takes ~2 s)
+    ref = R.gemm_bias_layernorm(x, w, bias, gamma, beta, b_layout="nk", out_dtype=torch.bfloat16)
+    assert_close(out, ref, TOL_LN)
     # every row normalised: mean ~ beta-mean, unit variance before the affine transform
     y = (out.float() - beta.cuda().float()) / gamma.cuda().float()
     assert y.mean(dim=1).abs().max() < 0.05 and (y.var(dim=1, unbiased=False) - 1).abs().max() < 0.05
