@@ -493,6 +493,7 @@ def strong_table(args, ws: int, rank: int, dist) -> list:
         entry = {"op": f"{key} {name}", "global_rows": rows, "rows_per_rank": hi - lo, "ms": round(ms, 5),
                  "tflops": round(tf, 2)}
         flat = out.reshape(out.shape[0], -1)
+        shard.gather_rows(flat, rows)  # NCCL communicator set-up outside the timing
         _barrier(dist)
         g_ms = _max_over_ranks(time_steps(lambda: shard.gather_rows(flat, rows), 3, flush), dist)
         entry["allgather_ms"] = round(g_ms, 4)

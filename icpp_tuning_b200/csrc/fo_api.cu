@@ -698,7 +698,7 @@ struct DirectPlan {
   int P, Hp, nR, pslots, smem;
 };
 
-bool plan_direct(const FoConvDesc* d, int stages, DirectPlan* pl, char* why, size_t n) {
+bool plan_direct(const FoConvDesc* d, int stages, int kps, DirectPlan* pl, char* why, size_t n) {
   auto no = [&](const char* msg) {
     snprintf(why, n, "%s", msg);
     return false;
@@ -714,7 +714,7 @@ bool plan_direct(const FoConvDesc* d, int stages, DirectPlan* pl, char* why, siz
   pl->nR = (fo::kDirectBN - 1 + (d->kh - 1) * P + d->kw - 1) / P + 1;
   const int slot = pl->nR * P * 128;
   for (int slots = 2; slots >= 1; --slots) {
-    const int smem = fo::direct_smem_bytes(stages, slots, slot);
+    const int smem = fo::direct_smem_bytes(stages, slots, slot, kps);
     if (smem <= 232448) {
       pl->pslots = slots;
       pl->smem = smem;
@@ -833,7 +833,8 @@ int fo_conv2d(const FoConvDesc* d, const FoTileCfg* cfg, void* stream) {
     // direct conv: one 4-D box per padded input row, 4-D output boxes of 32 x 32
     DirectPlan dp;
     char why[160];
-    if (!plan_direct(d, cfg->stages, &dp, why, sizeof(why))) return fail(FO_EINVAL, "%s", why);
+    if (!plan_direct(d, cfg->stages, cfg->block_k / 64, &dp, why, sizeof(why))) return fail(FO_EINVAL, "%s", why);
+    p.kps = cfg->block_k / 64;  // filter taps per weight stage
     p.P = dp.P;
     p.Hp = dp.Hp;
     p.nR = dp.nR;

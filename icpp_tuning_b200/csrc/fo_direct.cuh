@@ -32,11 +32,13 @@ namespace fo {
 constexpr int kDirectBN = 256;          // positions per tile
 constexpr int kDirectWStage = 128 * 64 * 2;  // 128 channels x 64 K of weights
 
-__host__ __device__ constexpr int direct_smem_bytes(int stages, int pslots, int slot_bytes) {
-  return 1024 + pslots * slot_bytes + stages * kDirectWStage + kEpiBytes + kMiscBytes;
+// kps: filter taps per weight stage (1, or 2 = block_k 128: one barrier wait and one
+// commit per 8 MMAs instead of 4, for the single MMA-issuing thread).
+__host__ __device__ constexpr int direct_smem_bytes(int stages, int pslots, int slot_bytes, int kps = 1) {
+  return 1024 + pslots * slot_bytes + stages * kps * kDirectWStage + kEpiBytes + kMiscBytes;
 }
 
-template <int ACT, int OUT_DT>
+template <int ACT, int OUT_DT, int KPS = 1>
 __global__ void __launch_bounds__(320, 1)
     fo_direct_conv_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                           const __grid_constant__ CUtensorMap tmY, const KParams p) {
@@ -52,7 +54,7 @@ __global__ void __launch_bounds__(320, 1)
   const int slot_bytes = p.nR * p.P * 128;
   const uint32_t sPix = smem_u32(smem);
   const uint32_t sW = sPix + p.pslots * slot_bytes;
-  const uint32_t sEpi = sW + stages * kDirectWStage;
+  const uint32_t sEpi = sW + stages * KPS * kDirectWStage;
   uint8_t* misc = smem + (sEpi - sPix) + kEpiBytes;
   // misc: [0,64) full[8] | [64,128) empty[8] | [128,144) pfull[2] | [144,160) pempty[2]
   //       | [160,176) tfull[2] | [176,192) tempty[2] | [192,200) drain | [248,256) tmem addr + abort
@@ -126,16 +128,20 @@ __global__ void __launch_bounds__(320, 1)
             ps = 0;
             pph ^= 1;
           }
-          for (int t = 0; t < taps; ++t) {
+          for (int t = 0; t < taps; t += KPS) {
+            const int nk = KPS == 1 ? 1 : min(KPS, taps - t);  // taps in this stage
             if (!mbar_wait(bar_empty + 8 * s, ph ^ 1, tmo, abort_flag)) {
               ok = false;
               break;
             }
             const uint32_t fb = bar_full + 8 * s;
-            mbar_arrive_expect_tx(fb, kDirectWStage);
+            mbar_arrive_expect_tx(fb, nk * kDirectWStage);
+            for (int i = 0; i < nk; ++i) {
 #pragma unroll
-            for (int j = 0; j < 2; ++j)  // 128 output channels x 64 K, MN-major
-              tma_load_2d(sW + s * kDirectWStage + j * 64 * 128, &tmW, fb, tm * 128 + j * 64, t * p.C + cb * 64);
+              for (int j = 0; j < 2; ++j)  // 128 output channels x 64 K, MN-major
+                tma_load_2d(sW + (s * KPS + i) * kDirectWStage + j * 64 * 128, &tmW, fb, tm * 128 + j * 64,
+                            (t + i) * p.C + cb * 64);
+            }
             ++issued;
             if (++s == stages) {
               s = 0;
@@ -183,30 +189,36 @@ __global__ void __launch_bounds__(320, 1)
           tc_fence_after();
           uint64_t bd = b_desc0 + static_cast<uint64_t>(ps * slot_units);
           int dx = 0;
-          for (int t = 0; t < taps; ++t) {
+          for (int t = 0; t < taps; t += KPS) {
+            const int nk = KPS == 1 ? 1 : min(KPS, taps - t);
             if (!mbar_wait(bar_full + 8 * s, ph, tmo, abort_flag)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            tc_mma_f16(d, ad, bd, idesc, accum);
-            tc_mma_f16(d, ad + (2048 >> 4), bd + (32 >> 4), idesc, 1u);
-            tc_mma_f16(d, ad + 2 * (2048 >> 4), bd + 2 * (32 >> 4), idesc, 1u);
-            tc_mma_f16(d, ad + 3 * (2048 >> 4), bd + 3 * (32 >> 4), idesc, 1u);
-            accum = 1u;
+#pragma unroll
+            for (int i = 0; i < KPS; ++i) {
+              if (KPS > 1 && i >= nk) break;
+              const uint64_t a = ad + static_cast<uint64_t>(i * (kDirectWStage >> 4));
+              tc_mma_f16(d, a, bd, idesc, accum);
+              tc_mma_f16(d, a + (2048 >> 4), bd + (32 >> 4), idesc, 1u);
+              tc_mma_f16(d, a + 2 * (2048 >> 4), bd + 2 * (32 >> 4), idesc, 1u);
+              tc_mma_f16(d, a + 3 * (2048 >> 4), bd + 3 * (32 >> 4), idesc, 1u);
+              accum = 1u;
+              if (++dx == p.KW) {
+                dx = 0;
+                bd += wrap_units;
+              } else {
+                bd += 8;
+              }
+            }
             tc_commit(bar_empty + 8 * s);
             if (++s == stages) {
               s = 0;
               ph ^= 1;
               ad = a_desc0;
             } else {
-              ad += kDirectWStage >> 4;
-            }
-            if (++dx == p.KW) {
-              dx = 0;
-              bd += wrap_units;
-            } else {
-              bd += 8;
+              ad += KPS * (kDirectWStage >> 4);
             }
           }
           tc_commit(bar_pempty + 8 * ps);

@@ -4,9 +4,9 @@
 
 namespace fo {
 
-template <int ACT, int OUT>
-static cudaError_t launch_direct(const LaunchArgs& a) {
-  auto kern = fo_direct_conv_kernel<ACT, OUT>;
+template <int ACT, int OUT, int KPS>
+static cudaError_t launch_direct_k(const LaunchArgs& a) {
+  auto kern = fo_direct_conv_kernel<ACT, OUT, KPS>;
   static std::atomic<uint64_t> opted{0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -19,6 +19,12 @@ static cudaError_t launch_direct(const LaunchArgs& a) {
   }
   kern<<<a.grid, 320, a.smem, a.stream>>>(a.tmA, a.tmB, a.tmC, a.p);
   return cudaGetLastError();
+}
+
+// One filter tap per weight stage, or two (block_k 128).
+template <int ACT, int OUT>
+static cudaError_t launch_direct(const LaunchArgs& a) {
+  return a.p.kps == 2 ? launch_direct_k<ACT, OUT, 2>(a) : launch_direct_k<ACT, OUT, 1>(a);
 }
 
 cudaError_t launch_direct_conv(int act, int out_dt, const LaunchArgs& a) {

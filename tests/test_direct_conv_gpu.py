@@ -11,8 +11,8 @@ from tests.gpu_util import TOL, assert_close, cuda, gen, randn, status_clean
 pytestmark = pytest.mark.gpu
 
 
-def dcfg(stages=4):
-    return N.tile_cfg(block_n=256, stages=stages, group_m=0, swap_ab=2)
+def dcfg(stages=4, block_k=64):
+    return N.tile_cfg(block_n=256, stages=stages, group_m=0, swap_ab=2, block_k=block_k)
 
 
 SHAPES = [  # n, h, w, c, f, k, pad
@@ -27,14 +27,16 @@ SHAPES = [  # n, h, w, c, f, k, pad
 
 
 @pytest.mark.parametrize("shape", SHAPES, ids=str)
-@pytest.mark.parametrize("odt", [torch.bfloat16, torch.float32])
-def test_direct_conv_bias_relu(shape, odt):
+@pytest.mark.parametrize("odt,bk", [(torch.bfloat16, 64), (torch.float32, 64), (torch.bfloat16, 128)])
+def test_direct_conv_bias_relu(shape, odt, bk):
+    """block_k 128: two filter taps per weight stage (5x5: an odd tap count, 1x1: one)."""
     n, h, w, c, f, k, p = shape
     g = gen(70)
     x = randn(g, n, h, w, c)
     wt = randn(g, k, k, c, f, scale=(k * k * c) ** -0.5)
     bias = randn(g, f, scale=0.1)
-    out = fused.conv2d_nhwc(*cuda(x, wt), bias=bias.cuda(), relu=True, padding=p, out_dtype=odt, config=dcfg())
+    out = fused.conv2d_nhwc(*cuda(x, wt), bias=bias.cuda(), relu=True, padding=p, out_dtype=odt,
+                            config=dcfg(3 if bk == 128 else 4, bk))
     ref = R.conv2d_bias_relu(x, wt, bias, True, 1, p, 1, out_dtype=odt)
     assert_close(out, ref, TOL)
     status_clean()
