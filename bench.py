@@ -493,13 +493,15 @@ def strong_table(args, ws: int, rank: int, dist) -> list:
         entry = {"op": f"{key} {name}", "global_rows": rows, "rows_per_rank": hi - lo, "ms": round(ms, 5),
                  "tflops": round(tf, 2)}
         flat = out.reshape(out.shape[0], -1)
-        shard.gather_rows(flat, rows)  # NCCL communicator set-up outside the timing
+        whole = torch.empty((rows, flat.shape[1]), dtype=flat.dtype, device=dev)
+        shard.gather_rows(flat, rows, out=whole)  # NCCL communicator set-up outside the timing
         _barrier(dist)
-        g_ms = _max_over_ranks(time_steps(lambda: shard.gather_rows(flat, rows), 3, flush), dist)
+        g_ms = _max_over_ranks(time_steps(lambda: shard.gather_rows(flat, rows, out=whole), 5, flush), dist)
         entry["allgather_ms"] = round(g_ms, 4)
         entry["allgather_bytes"] = rows * flat.shape[1] * flat.element_size()
+        entry["allgather_gbs"] = round(entry["allgather_bytes"] / (g_ms / 1e3) / 1e9, 1)
         res.append(entry)
-        del fn, out, flat
+        del fn, out, flat, whole
         torch.cuda.empty_cache()
     return res
 

@@ -26,18 +26,28 @@ def row_shard(M: int, world: int, rank: int, align: int = 128) -> Tuple[int, int
     return min(M, lo_b * align), min(M, hi_b * align)
 
 
-def gather_rows(shard: torch.Tensor, M: int, group=None) -> torch.Tensor:
+def gather_rows(shard: torch.Tensor, M: int, group=None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Concatenate every rank's row shard (as produced by row_shard) into [M, ...] on
-    every rank.  Shards may differ in length; they are padded to the longest for the
-    collective and trimmed after."""
+    every rank (into `out` when given).  Equal shards are gathered straight into the
+    output with one all-gather; shards of different lengths are padded to the longest
+    for the collective and trimmed after."""
     world = dist.get_world_size(group)
     sizes = [row_shard(M, world, r) for r in range(world)]
     longest = max(hi - lo for lo, hi in sizes)
+    if all(hi - lo == longest for lo, hi in sizes) and shard.is_contiguous():
+        if out is None:
+            out = torch.empty((M,) + tuple(shard.shape[1:]), dtype=shard.dtype, device=shard.device)
+        dist.all_gather_into_tensor(out, shard, group=group)
+        return out
     pad = torch.zeros((longest,) + tuple(shard.shape[1:]), dtype=shard.dtype, device=shard.device)
     pad[: shard.shape[0]] = shard
-    out = torch.empty((world * longest,) + tuple(shard.shape[1:]), dtype=shard.dtype, device=shard.device)
-    dist.all_gather_into_tensor(out, pad, group=group)
-    return torch.cat([out[r * longest: r * longest + (hi - lo)] for r, (lo, hi) in enumerate(sizes)])
+    buf = torch.empty((world * longest,) + tuple(shard.shape[1:]), dtype=shard.dtype, device=shard.device)
+    dist.all_gather_into_tensor(buf, pad, group=group)
+    rows = torch.cat([buf[r * longest: r * longest + (hi - lo)] for r, (lo, hi) in enumerate(sizes)])
+    if out is not None:
+        out.copy_(rows)
+        return out
+    return rows
 
 
 class PeerLost(RuntimeError):

@@ -35,8 +35,9 @@ def _worker_gather(rank, world, port, M, q):
         bias = torch.randn(96, generator=g).bfloat16()
         out, lo, hi = sharded_apply(lambda x: R.gemm_bias_act(x, b, bias, "gelu_tanh"), a, world, rank)
         full = gather_rows(out.contiguous(), M)
+        into = gather_rows(out.contiguous(), M, out=torch.empty_like(full))  # caller-provided output
         ref = R.gemm_bias_act(a, b, bias, "gelu_tanh")
-        q.put((rank, bool(torch.equal(full, ref)), lo, hi))
+        q.put((rank, bool(torch.equal(full, ref) and torch.equal(into, ref)), lo, hi))
         dist.destroy_process_group()
     except Exception as e:  # pragma: no cover - reported through the queue
         q.put((rank, repr(e), -1, -1))
