@@ -57,6 +57,7 @@ CONSTANTS = {
     # normalisation, per read + write byte of the output (config4: 58 us over the plain
     # GEMM + bias kernel for 2 x 128 MiB)
     "ln_fused_bytes_per_s": 4.6e12,
+    "ln_fused_tail_s": 7.4e-6,  # its normalisation after the last unit (2048 x 4096: +2.7 us)
     # TMA im2col loads (one 128-pixel x 64-channel box per filter tap) run at this share
     # of a tiled load's rate: measured 589 vs 836 TFLOP/s for BN=128 conv vs GEMM tiles
     "im2col_rate": 0.7,
@@ -237,8 +238,11 @@ def _model(op: OpSpec, c: TuneConfig, hw: GPUSpec) -> dict:
     # -- LayerNorm: one normalisation pass (read + write) per 128-row block
     t_ln = 0.0
     if op.has_reduction_epilogue:
-        rate = K["ln_fused_bytes_per_s"] if bn >= 128 else K["ln_pass_bytes_per_s"]
-        t_ln = 2.0 * op.M * op.N * ml.output_element_bytes / rate
+        ln_bytes = 2.0 * op.M * op.N * ml.output_element_bytes
+        if bn >= 128 and op.M * op.N >= (1 << 24):  # the C ABI runs these as one kernel
+            t_ln = ln_bytes / K["ln_fused_bytes_per_s"] + K["ln_fused_tail_s"]
+        else:
+            t_ln = ln_bytes / K["ln_pass_bytes_per_s"]
     # split-K tail (GEMM, CTA pairs included, and single-CTA conv, with a workspace): the
     # last, less than half-full wave is split along K, so it costs 1/split of a wave plus
     # the partials' reduction

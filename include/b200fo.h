@@ -87,7 +87,8 @@ typedef struct FoTileCfg {
                     /*     and reduce-scatter their partials through distributed shared   */
                     /*     memory, no workspace (gemm with block_m 128, s <= 8, one wave, */
                     /*     not with FO_EPI_BIAS_LN)                                       */
-  int32_t ln_mode;  /* FO_EPI_BIAS_LN only: 0 = automatic (one kernel when eligible),      */
+  int32_t ln_mode;  /* FO_EPI_BIAS_LN only: 0 = automatic (one kernel when eligible and  */
+                    /*     M x N >= 2^24, where it measured faster),                      */
                     /* 1 = two kernels: the GEMM stores biased rows + slice statistics,   */
                     /*     a row pass normalises them in place,                           */
                     /* 2 = one kernel: each epilogue warp normalises its own stored slice */
