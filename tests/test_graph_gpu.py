@@ -68,6 +68,10 @@ CASES = {
     "gemm_pair_gelu": lambda: _gemm_case("bias_gelu_erf", 2048, 3072, 768, N.tile_cfg(256, 4, 8, block_m=256)),
     "gemm_bk128_relu": lambda: _gemm_case("bias_relu", 1536, 1024, 1024, N.tile_cfg(128, 3, 8, block_k=128)),
     "bias_layernorm": lambda: _gemm_case("bias_layernorm", 700, 1024, 512, N.tile_cfg(128, 6, 8)),
+    # the one-kernel LayerNorm: a cooperative launch inside the captured graph
+    "bias_layernorm_one_kernel": lambda: _gemm_case("bias_layernorm", 1500, 2048, 256,
+                                                    N.tile_cfg(256, 3, 0, block_m=256, block_k=128,
+                                                               ln_mode=N.LN_ONE_KERNEL)),
     "residual_layernorm": lambda: _gemm_case("bias_residual_layernorm", 384, 768, 768, N.tile_cfg(128, 6, 8),
                                              dt=torch.float16),
     "conv_bn_add_relu": lambda: _conv_case(N.tile_cfg(128, 6, 0), True, True),
