@@ -73,6 +73,9 @@ class MainloopSpec:
     weight_reuse_hint: float = 1.0
     spatial_reuse_hint: float = 1.0
     preferred_group_m: int = 8
+    # conv only: (N, C, H, W, OC, KH, KW, stride, padding), for models that need the image
+    # geometry (the tcgen05 model's direct conv); the reference's factors do not read it
+    conv_geometry: Optional[Tuple[int, ...]] = None
 
     @property
     def mainloop_flops(self) -> int:
@@ -272,7 +275,8 @@ def make_conv2d_spec(N: int, C: int, H: int, W: int, OC: int, KH: int, KW: int, 
                       output_element_bytes=output_element_bytes,
                       input_reuse_hint=math.sqrt(overlap),
                       weight_reuse_hint=math.sqrt(max(1.0, overlap)),
-                      spatial_reuse_hint=overlap)
+                      spatial_reuse_hint=overlap,
+                      conv_geometry=(N, C, H, W, OC, KH, KW, stride, padding))
     return OpSpec(name=name or "conv2d", mainloop=ml, epilogue=resolve_primitives(primitives))
 
 

@@ -61,6 +61,13 @@ CONSTANTS = {
     # TMA im2col loads (one 128-pixel x 64-channel box per filter tap) run at this share
     # of a tiled load's rate: measured 589 vs 836 TFLOP/s for BN=128 conv vs GEMM tiles
     "im2col_rate": 0.7,
+    # direct conv: mainloop rate of a 128 x (rows x pitch) tile per taps-per-weight-stage
+    # (one MMA issue wait per stage; config5 224-position tiles measured 7.4 / 6.7 / 6.4
+    # us per tile for 1 / 2 / 3 taps per stage), and the factor when only one pixel slot
+    # fits (its reload is then not overlapped)
+    "direct_rate_kps": {1: 0.79, 2: 0.87, 3: 0.90},
+    "direct_one_slot": 0.7,
+    "mma_issue_cycles": 130,  # one thread issuing back-to-back MMAs with a wait per stage
     "fixed_s": 6.0e-6,  # launch + TMEM alloc + pipeline fill + last epilogue
     "pair_fixed_s": 1.0e-6,  # extra fixed cost of a CTA-pair launch (cluster start and exit)
     "split_overhead_s": 2.0e-6,  # partial write -> fence -> atomic -> reduce chain
@@ -196,8 +203,90 @@ def _traffic_bytes(op: OpSpec, c: TuneConfig, hw: GPUSpec, ctas: int) -> float:
     return max(a_total + b_total, waves * per_wave) + out
 
 
+def direct_plan(geo, block_n: int, sms: int, kps: int, stages: int):
+    """The direct conv's geometry as fo_api.cu plan_direct computes it: (P, rows per tile,
+    tiles per image, positions per tile, pixel slots, shared bytes), or None when the
+    shape does not qualify or nothing fits in shared memory."""
+    n, c, h, w, oc, kh, kw, stride, pad = geo
+    if stride != 1 or c % 64 != 0:
+        return None
+    P = _cdiv(w + 2 * pad, 32) * 32
+    oh = h + 2 * pad - kh + 1
+    if P > block_n or kw - 1 >= P or oh <= 0:
+        return None
+    tiles_m = _cdiv(oc, 128)
+    best, rpt = -1, 1
+    for r in range(1, block_n // P + 1):
+        cost = _cdiv(n * _cdiv(oh, r) * tiles_m, sms) * (max(r * P, 240) + 32)
+        if best < 0 or cost <= best:
+            best, rpt = cost, r
+    bn = rpt * P
+    nr = (bn - 1 + (kh - 1) * P + kw - 1) // P + 1
+    slot = nr * P * 128
+    for slots in (2, 1):
+        smem = 1024 + slots * slot + stages * kps * 128 * 64 * 2 + 32768 + 1536
+        if smem <= 232448:
+            return P, rpt, _cdiv(oh, rpt), bn, slots, smem
+    return None
+
+
+def _model_direct(op: OpSpec, c: TuneConfig, hw: GPUSpec) -> dict:
+    """Direct conv (swap_ab 2): tiles of rpt padded rows x 128 channels, each input row
+    loaded once per channel block and every filter tap a shifted view of it, so the
+    mainloop runs near the tensor rate; the padding positions of each row (P - OW) and of
+    the last tile of an image are computed and discarded."""
+    K = CONSTANTS
+    ml = op.mainloop
+    geo = ml.conv_geometry
+    kps = c.block_K // 64
+    pl = direct_plan(geo, c.block_N, hw.num_sm, kps, c.num_stages) if geo else None
+    if pl is None or c.block_M != 128:
+        return {"score": 0.0, **{f: 0.0 for f in ("eff_mainloop", "eff_memory", "eff_parallel", "eff_pipeline",
+                                                   "eff_implicit_conv", "eff_epilogue", "eff_reduction")},
+                "projection": {"predicted_s": float("inf"), "predicted_tflops": 0.0}}
+    P, rpt, tpi, bn, slots, _ = pl
+    n, cin, h, w, oc, kh, kw, _, pad = geo
+    tiles = n * tpi * _cdiv(oc, 128)
+    ctas = min(tiles, hw.num_sm)
+    waves = _cdiv(tiles, ctas)
+    rate = _sm_rate(hw)
+    e_kps = K["direct_rate_kps"][kps] * (1.0 if slots == 2 else K["direct_one_slot"])
+    # one 128 x bn x 16 MMA: bn / 2 tensor cycles at the kps-dependent rate, but no fewer
+    # than the issuing thread's cycles per MMA (narrow tiles are issue-bound)
+    clk = rate / 8192.0  # the tensor clock implied by the achievable rate (8192 FLOP / cycle)
+    n_mma = cin // 16 * kh * kw
+    t_tile_mma = n_mma * max(bn / 2.0 / e_kps, K["mma_issue_cycles"]) / clk
+    t_epi = 128 * bn * ml.output_element_bytes / K["epi_bytes_per_s_sm"]
+    t_tile = max(t_tile_mma, t_epi)
+    t_comp = waves * t_tile + t_epi + K["fixed_s"]
+    traffic = (ml.input_elements * ml.input_element_bytes + ml.weight_elements * ml.weight_element_bytes
+               + ml.output_elements * ml.output_element_bytes)
+    t_mem = traffic / (hw.mem_bandwidth_gbps * 1e9 * K["hbm_efficiency"])
+    t_pred = max(t_comp, t_mem) + K["mem_overlap"] * min(t_comp, t_mem)
+    t_ideal = ml.mainloop_flops / (_sm_rate(hw) * hw.num_sm)
+    score = min(1.0, t_ideal / t_pred)
+    oh = h + 2 * pad - kh + 1
+    e_main = min(1.0, (oh * (w + 2 * pad - kw + 1)) / float(tpi * rpt * P) * e_kps)
+    e_mem = t_comp / t_pred
+    e_epi = t_tile_mma / t_tile
+    e_par = score / max(1e-12, e_main * e_mem * e_epi)
+    return {
+        "score": score, "eff_mainloop": e_main, "eff_memory": e_mem, "eff_parallel": e_par,
+        "eff_pipeline": 1.0, "eff_implicit_conv": 1.0, "eff_epilogue": e_epi, "eff_reduction": 1.0,
+        "projection": {
+            "tiles_M": _cdiv(oc, 128), "tiles_N": n * tpi, "tiles_K": cin // 64 * kh * kw, "grid_size": ctas,
+            "num_tiles": tiles, "waves": waves, "wave_fill": tiles / float(waves * ctas),
+            "predicted_s": t_pred, "predicted_tflops": ml.mainloop_flops / t_pred / 1e12,
+            "hbm_bytes": traffic, "t_tile_s": t_tile, "t_epilogue_s": t_epi, "pitch": P, "rows_per_tile": rpt,
+            "positions_per_tile": bn, "pixel_slots": slots,
+        },
+    }
+
+
 def _model(op: OpSpec, c: TuneConfig, hw: GPUSpec) -> dict:
     K = CONSTANTS
+    if c.swap_ab == 2:
+        return _model_direct(op, c, hw)
     ml = op.mainloop
     bm, bn, bk = c.block_M, c.block_N, c.block_K
     pair = bm == 256

@@ -3,9 +3,12 @@
 A raw config is the dict the operator modules pass to the kernel (and that
 `select_best` returns): block_M (tcgen05 M = 128, or 256 for a CTA pair), block_N (64 /
 128 / 256), block_K (64 = one 128-byte swizzle row of 16-bit elements per stage, or 128 =
-two), num_stages, thread_num (10 warps for
-GEMMs: producer / MMA / 8 epilogue; 13 for conv: 4 producer warps) and group_m (tile raster).  Legality is
-the C ABI's (fo_query_config_legal): shared memory <= 227 KB, TMEM <= 512 columns.
+two; 192 = three filter taps per stage in the direct conv), num_stages, thread_num (10
+warps for GEMMs: producer / MMA / 8 epilogue; 13 for conv: 4 producer warps; 11 for the
+direct conv: weight producer / MMA / 8 epilogue / pixel-slot producer), group_m (tile
+raster) and swap_ab (conv: 1 = operand-swapped im2col kernel, 2 = direct conv).  Legality
+is the C ABI's (fo_query_config_legal): shared memory <= 227 KB, TMEM <= 512 columns; the
+direct conv's shared memory depends on the image width and is checked per shape.
 """
 from __future__ import annotations
 
@@ -16,6 +19,7 @@ from .interface import TileLangKernelBase
 
 GEMM_THREADS = 320
 CONV_THREADS = 416
+DIRECT_THREADS = 352  # direct conv: weight producer, MMA, 8 epilogue, slot producer
 SMEM_LIMIT = 232448
 
 
@@ -66,6 +70,12 @@ def tcgen05_configs(block_ns: Sequence[int] = (64, 128, 256), group_ms: Sequence
             for s in sorted({x for x in (stages or (3, 4)) if 3 <= x <= max_stages(bn)}, reverse=True):
                 out.append({"block_M": 128, "block_N": bn, "block_K": 64, "num_stages": s,
                             "thread_num": CONV_THREADS, "group_m": 0, "swap_ab": 1})
+        # direct conv (stride 1, C % 64 == 0, padded row <= 256 positions; the model scores
+        # other shapes 0): up to 256 positions x 128 channels per tile, one to three filter
+        # taps per weight stage, as many stages as fit beside two 224-position pixel slots
+        for bk, s in ((64, 6), (128, 3), (192, 2)):
+            out.append({"block_M": 128, "block_N": 256, "block_K": bk, "num_stages": s,
+                        "thread_num": DIRECT_THREADS, "group_m": 0, "swap_ab": 2})
     return out
 
 
@@ -80,4 +90,5 @@ class Tcgen05Descriptor(TileLangKernelBase):
 
     def format_config(self, raw: Dict[str, Any]) -> str:
         base = super().format_config(raw)
-        return base + "_SW" if raw.get("swap_ab") else base
+        sw = raw.get("swap_ab", 0)
+        return base + ("_DC" if sw == 2 else "_SW" if sw else "")

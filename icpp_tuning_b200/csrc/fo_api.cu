@@ -197,17 +197,16 @@ int check_cfg(int op, int out_dtype, const FoTileCfg* cfg, char* why, size_t why
   if (cfg->block_m == 256 && cfg->block_n < 128) return say("CTA pairs (block_m 256) need block_n >= 128, got %d", cfg->block_n);
   if (cfg->block_n != 64 && cfg->block_n != 128 && cfg->block_n != 256)
     return say("block_n must be 64, 128 or 256, got %d", cfg->block_n);
-  if (cfg->block_k != 64 && cfg->block_k != 128)
-    return say("block_k must be 64 or 128 (one or two 128-byte swizzle rows per stage), got %d", cfg->block_k);
-  const int min_stages = op == 1 ? 3 : 2;
+  if (cfg->block_k != 64 && cfg->block_k != 128 && !(cfg->block_k == 192 && cfg->swap_ab == 2))
+    return say("block_k must be 64 or 128 (one or two 128-byte swizzle rows per stage; 192, three filter taps "
+               "per weight stage, for the direct conv), got %d", cfg->block_k);
+  const int min_stages = op == 1 && cfg->swap_ab != 2 ? 3 : 2;
   if (cfg->stages < min_stages || cfg->stages > fo::kMaxStages)
     return say("stages out of range: %d", cfg->stages);
   if (cfg->group_m < 0) return say("group_m must be >= 0, got %d", cfg->group_m);
   if (cfg->swap_ab < 0 || cfg->swap_ab > 2) return say("swap_ab must be 0, 1 or 2 (direct conv), got %d", cfg->swap_ab);
   if (cfg->swap_ab && (op != 1 || cfg->block_m != 128 || cfg->block_n < 128))
     return say("swap_ab is a conv2d mode with block_m 128 and block_n >= 128 (block_n %d)", cfg->block_n);
-  if (cfg->swap_ab == 2 && cfg->block_n != 256)
-    return say("the direct conv (swap_ab 2) computes 256-position tiles: block_n must be 256, got %d", cfg->block_n);
   if (cfg->max_ctas < 0) return say("max_ctas must be >= 0, got %d", cfg->max_ctas);
   if (cfg->split_k < 0 || cfg->split_k > 16) return say("split_k must be 0 (automatic) .. 16, got %d", cfg->split_k);
   if (cfg->split_mode < 0 || cfg->split_mode > 2)
@@ -696,13 +695,20 @@ extern "C" size_t fo_conv2d_workspace_size(const FoConvDesc* d, const FoTileCfg*
 }
 
 // Geometry of the direct conv (swap_ab 2): pitch P of the padded rows (W + 2 pad rounded
-// up to 32, dividing 256), rows per pixel slot, and how many slots fit beside `stages`
-// weight stages.  Returns false (with the reason) when the shape does not qualify.
+// up to 32), output rows per tile (rpt: BN = rpt * P <= block_n positions), rows per pixel
+// slot, and how many slots fit beside `stages` weight stages.  rpt minimises the time of
+// the busiest SM, ceil(tiles / sms) x (max(BN, 240) + 32) in positions: a tile's MMAs
+// (128 x BN x 16) cost BN / 2 tensor cycles each, but no less than the ~130 cycles the
+// issuing thread needs per MMA, and 32 is a tile's fixed cost.  Ties go to taller tiles;
+// e.g. 28 x 28 with P = 32 takes 7-row tiles (4 per image, 224 positions) over 8-row
+// ones that would compute 32 rows per 28.  Returns false (with the reason) when the
+// shape does not qualify.
 struct DirectPlan {
-  int P, Hp, nR, pslots, smem;
+  int P, Hp, nR, pslots, smem, rpt, tpi;
 };
 
-bool plan_direct(const FoConvDesc* d, int stages, int kps, DirectPlan* pl, char* why, size_t n) {
+bool plan_direct(const FoConvDesc* d, int stages, int kps, int block_n, int sms, DirectPlan* pl, char* why,
+                 size_t n) {
   auto no = [&](const char* msg) {
     snprintf(why, n, "%s", msg);
     return false;
@@ -711,11 +717,28 @@ bool plan_direct(const FoConvDesc* d, int stages, int kps, DirectPlan* pl, char*
   if (d->c % 64 != 0) return no("the direct conv needs C % 64 == 0");
   const int wp = d->w + 2 * d->pad;
   const int P = (wp + 31) / 32 * 32;
-  if (P > 256 || 256 % P != 0) return no("the direct conv needs W + 2 pad <= 256 with its 32-rounded pitch dividing 256");
+  if (P > block_n) {
+    snprintf(why, n, "the direct conv needs W + 2 pad, rounded up to 32, <= %d (block_n)", block_n);
+    return false;
+  }
   if (d->kw - 1 >= P) return no("filter wider than the padded row");
+  const int oh = d->h + 2 * d->pad - d->kh + 1;
+  if (oh <= 0) return no("the filter is taller than the padded image");
   pl->P = P;
   pl->Hp = d->h + 2 * d->pad;
-  pl->nR = (fo::kDirectBN - 1 + (d->kh - 1) * P + d->kw - 1) / P + 1;
+  const long long tiles_m = (d->f + 127) / 128;
+  long long best = -1;
+  for (int rpt = 1; rpt * P <= block_n; ++rpt) {
+    const long long tiles = static_cast<long long>(d->n) * ((oh + rpt - 1) / rpt) * tiles_m;
+    const long long cost = (tiles + sms - 1) / sms * ((rpt * P > 240 ? rpt * P : 240) + 32);
+    if (best < 0 || cost <= best) {
+      best = cost;
+      pl->rpt = rpt;
+    }
+  }
+  pl->tpi = (oh + pl->rpt - 1) / pl->rpt;
+  const int bn = pl->rpt * P;
+  pl->nR = (bn - 1 + (d->kh - 1) * P + d->kw - 1) / P + 1;
   const int slot = pl->nR * P * 128;
   for (int slots = 2; slots >= 1; --slots) {
     const int smem = fo::direct_smem_bytes(stages, slots, slot, kps);
@@ -837,17 +860,20 @@ int fo_conv2d(const FoConvDesc* d, const FoTileCfg* cfg, void* stream) {
     // direct conv: one 4-D box per padded input row, 4-D output boxes of 32 x 32
     DirectPlan dp;
     char why[160];
-    if (!plan_direct(d, cfg->stages, cfg->block_k / 64, &dp, why, sizeof(why))) return fail(FO_EINVAL, "%s", why);
+    const int ctas = cfg->max_ctas > 0 && cfg->max_ctas < di.sms ? cfg->max_ctas : di.sms;
+    if (!plan_direct(d, cfg->stages, cfg->block_k / 64, cfg->block_n, ctas, &dp, why, sizeof(why)))
+      return fail(FO_EINVAL, "%s", why);
     p.kps = cfg->block_k / 64;  // filter taps per weight stage
     p.P = dp.P;
     p.Hp = dp.Hp;
     p.nR = dp.nR;
     p.pslots = dp.pslots;
     p.nimg = d->n;
+    p.rpt = dp.rpt;
+    p.tpi = dp.tpi;
     p.c_blocks = d->c / 64;
-    const long long positions = static_cast<long long>(d->n) * dp.Hp * dp.P;
     p.tiles_m = (p.N + 127) / 128;
-    p.tiles_n = static_cast<int>((positions + fo::kDirectBN - 1) / fo::kDirectBN);
+    p.tiles_n = d->n * dp.tpi;
     p.num_tiles = p.tiles_m * p.tiles_n;
     p.num_units = p.num_tiles;
     p.dp_units = p.num_tiles;

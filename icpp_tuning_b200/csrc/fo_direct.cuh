@@ -6,46 +6,54 @@
 // once per 128-channel output tile and every tap is a shifted view of the same rows:
 //
 //   * The image is viewed with padded rows of P positions (P = W + 2*pad rounded up to
-//     32, P dividing 256) and Hp = H + 2*pad padded rows per image.  Output position
-//     o = (n * Hp + oh) * P + ow; tap (dy, dx) reads input position o + dy * P + dx, a
-//     constant shift.  Positions with ow >= OW or oh >= OH are computed and discarded.
-//   * A tile is BN = 256 consecutive positions (256 / P whole padded rows) x 128 output
-//     channels (operand-swapped: M = channels from the weights, N = positions).  The
-//     producer loads the nR padded rows the tile's taps touch, one 4-D TMA box of
-//     (64 channels, P positions) per row starting at w = -pad (the padding is the
-//     hardware's out-of-range zero fill; every box lands 1024-byte aligned because
-//     P * 128 B is a multiple of 4 KB).
+//     32).  Inside a tile, output position q = r * P + ow (r = output row of the tile)
+//     and tap (dy, dx) reads padded-input position q + dy * P + dx, a constant shift.
+//     Positions with ow >= OW or with an output row past OH are computed and discarded.
+//   * A tile is rpt whole output rows of one image (BN = rpt * P <= 256 positions, rpt
+//     chosen by the host so that the tiles cover OH with little waste and fill the
+//     waves evenly) x 128 output channels (operand-swapped: M = channels from the
+//     weights, N = positions).  The slot producer loads the nR padded rows the tile's
+//     taps touch, one 4-D TMA box of (64 channels, P positions) per row starting at
+//     w = -pad (the padding, and rows past the image, are the hardware's out-of-range
+//     zero fill; every box lands 1024-byte aligned because P * 128 B is a multiple of
+//     4 KB).
 //   * For each channel block and tap the MMA issuer points the B descriptor at the rows
 //     shifted by dy * P + dx positions (128 B each); the swizzle is anchored on absolute
 //     shared-memory addresses, so any row shift is a plain start-address offset.
-//   * The weights stream through a ring of 128 x 64 stages as in the im2col kernel.
+//   * The weights stream through a ring of 128 x 64 stages (one or two taps per stage)
+//     from their own producer thread; the pixel slots have a producer thread of their
+//     own (the last warp), so a slot is refilled as soon as it frees instead of after the
+//     weight loads queued before it.
 //   * Eight epilogue warps (two per TMEM lane quarter) take 32-position chunks: with
 //     P % 32 == 0 each chunk is part of one padded row, stored with one 4-D TMA box
 //     (32 channels x 32 columns) whose out-of-range columns the hardware clips.
-// Per 128 x 256 x 64 MMA step an SM now loads 16 KB of weights plus 1/(KH*KW) of the
-// rows instead of 48 KB.  Every wait is bounded as in fo_tc_kernel.
+// Per 128 x BN x 64 MMA step an SM loads 16 KB of weights plus 1/(KH*KW) of the rows
+// instead of 16 KB + BN * 128 B.  Every wait is bounded as in fo_tc_kernel.
 #pragma once
 #include "fo_kernel.cuh"
 
 namespace fo {
 
-constexpr int kDirectBN = 256;          // positions per tile
+constexpr int kDirectMaxBN = 256;       // positions per tile, at most
+constexpr int kDirectThreads = 352;     // weight producer, MMA, 8 epilogue, slot producer
 constexpr int kDirectWStage = 128 * 64 * 2;  // 128 channels x 64 K of weights
 
-// kps: filter taps per weight stage (1, or 2 = block_k 128: one barrier wait and one
-// commit per 8 MMAs instead of 4, for the single MMA-issuing thread).
+// kps: filter taps per weight stage (1; 2 = block_k 128; 3 = block_k 192).  The single
+// MMA-issuing thread loses a few hundred cycles at every barrier wait (the tensor pipe's
+// queue of issued MMAs is too short to cover it), so more MMAs per wait -- 8 or 12
+// instead of 4 -- keep the pipe fuller, at the price of fewer, larger stages.
 __host__ __device__ constexpr int direct_smem_bytes(int stages, int pslots, int slot_bytes, int kps = 1) {
   return 1024 + pslots * slot_bytes + stages * kps * kDirectWStage + kEpiBytes + kMiscBytes;
 }
 
 template <int ACT, int OUT_DT, int KPS = 1>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(kDirectThreads, 1)
     fo_direct_conv_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                           const __grid_constant__ CUtensorMap tmY, const KParams p) {
-  constexpr int BN = kDirectBN;
-  constexpr int kMmaWarp = 1, kFirstEpiWarp = 2;
+  constexpr int kMmaWarp = 1, kFirstEpiWarp = 2, kSlotWarp = kFirstEpiWarp + kEpiWarps;
+  const int BN = p.rpt * p.P;  // positions per tile
   constexpr int kOutBytes = OUT_DT == DT_F32 ? 4 : 2;
-  constexpr uint32_t kTmemCols = 2 * BN;
+  constexpr uint32_t kTmemCols = 2 * kDirectMaxBN;  // two accumulators, 256 columns apart
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -100,34 +108,15 @@ __global__ void __launch_bounds__(320, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
-    // ------------------------------------------------------------------ producer
+    // ------------------------------------------------------------------ weight producer
     if (lane == 0) {
-      int s = 0, ps = 0;
-      uint32_t ph = 0, pph = 0;
-      int issued = 0, pissued = 0;
+      int s = 0;
+      uint32_t ph = 0;
+      int issued = 0;
       bool ok = true;
-      const uint32_t row_bytes = static_cast<uint32_t>(p.P) * 128;
       for (int u = cid; u < p.num_units && ok; u += ncl) {
-        const int tm = u % p.tiles_m, tn = u / p.tiles_m;
-        const int r0 = tn * (BN / p.P);  // first padded row of the tile (BN % P == 0)
+        const int tm = u % p.tiles_m;
         for (int cb = 0; cb < p.c_blocks && ok; ++cb) {
-          if (!mbar_wait(bar_pempty + 8 * ps, pph ^ 1, tmo, abort_flag)) {
-            ok = false;
-            break;
-          }
-          const uint32_t pb = bar_pfull + 8 * ps;
-          mbar_arrive_expect_tx(pb, static_cast<uint32_t>(p.nR) * row_bytes);
-          for (int r = 0; r < p.nR; ++r) {
-            const int R = r0 + r;
-            const int n = R / p.Hp;
-            const int hp = R - n * p.Hp;
-            tma_load_4d(sPix + ps * slot_bytes + r * row_bytes, &tmX, pb, cb * 64, -p.pad, hp - p.pad, n);
-          }
-          ++pissued;
-          if (++ps == p.pslots) {
-            ps = 0;
-            pph ^= 1;
-          }
           for (int t = 0; t < taps; t += KPS) {
             const int nk = KPS == 1 ? 1 : min(KPS, taps - t);  // taps in this stage
             if (!mbar_wait(bar_empty + 8 * s, ph ^ 1, tmo, abort_flag)) {
@@ -155,6 +144,39 @@ __global__ void __launch_bounds__(320, 1)
         *abort_flag = 1;
       }
       drain_loads(bar_full, stages, issued);
+    }
+  } else if (warp == kSlotWarp) {
+    // ------------------------------------------------------------------ slot producer
+    if (lane == 0) {
+      int ps = 0;
+      uint32_t pph = 0;
+      int pissued = 0;
+      bool ok = true;
+      const uint32_t row_bytes = static_cast<uint32_t>(p.P) * 128;
+      for (int u = cid; u < p.num_units && ok; u += ncl) {
+        const int tn = u / p.tiles_m;
+        const int n = tn / p.tpi;
+        const int hp0 = (tn - n * p.tpi) * p.rpt;  // first padded input row = first output row
+        for (int cb = 0; cb < p.c_blocks; ++cb) {
+          if (!mbar_wait(bar_pempty + 8 * ps, pph ^ 1, tmo, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t pb = bar_pfull + 8 * ps;
+          mbar_arrive_expect_tx(pb, static_cast<uint32_t>(p.nR) * row_bytes);
+          for (int r = 0; r < p.nR; ++r)  // rows past the image are zero-filled
+            tma_load_4d(sPix + ps * slot_bytes + r * row_bytes, &tmX, pb, cb * 64, -p.pad, hp0 + r - p.pad, n);
+          ++pissued;
+          if (++ps == p.pslots) {
+            ps = 0;
+            pph ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        record_error(p, kStatusTimeout, 0x43);
+        *abort_flag = 1;
+      }
       drain_loads(bar_pfull, p.pslots, pissued);
     }
   } else if (warp == kMmaWarp) {
@@ -179,7 +201,7 @@ __global__ void __launch_bounds__(320, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t d = tmem_base + acc * BN;
+        const uint32_t d = tmem_base + acc * kDirectMaxBN;
         uint32_t accum = 0;
         for (int cb = 0; cb < p.c_blocks && ok; ++cb) {
           if (!mbar_wait(bar_pfull + 8 * ps, pph, tmo, abort_flag)) {
@@ -263,23 +285,32 @@ __global__ void __launch_bounds__(320, 1)
       const int f = f0 + lane;
       const float2 aff = channel_affine(p, f);
       const bool has_add = OUT_DT != DT_F32 && p.add_src != nullptr && f0 < p.N;
+      const int n = tn / p.tpi;
+      const int oh0 = (tn - n * p.tpi) * p.rpt;
+      // the tile's BN / 32 chunks: the first half of the warps takes chunks 0-3, the second
+      // half the rest (none when BN <= 128: those warps only release the accumulator)
+      const int mine = min(4, max(0, BN / 32 - half * 4));
+      if (mine == 0) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_tempty + 8 * acc);
+      }
 #pragma unroll 1
-      for (int ci = 0; ci < 4; ++ci) {
+      for (int ci = 0; ci < mine; ++ci) {
         const int c = half * 4 + ci;
         uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + lane_off + acc * BN + c * 32, r);
+        tmem_ld_32x32b_x32(tmem_base + lane_off + acc * kDirectMaxBN + c * 32, r);
         tc_wait_ld_regs(r);
-        if (ci == 3) {
+        if (ci == mine - 1) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(bar_tempty + 8 * acc);
         }
-        const int pos0 = tn * BN + c * 32;  // 32 positions inside one padded row
-        const int R = pos0 / p.P;
-        const int n = R / p.Hp;
-        const int oh = R - n * p.Hp;
-        const int ow0 = pos0 - R * p.P;
-        if (n >= p.nimg || oh >= p.OH || ow0 >= p.OW || f0 >= p.N) continue;  // padding positions
+        const int pos0 = c * 32;  // 32 positions inside one padded row of the tile
+        const int rr = pos0 / p.P;
+        const int oh = oh0 + rr;
+        const int ow0 = pos0 - rr * p.P;
+        if (oh >= p.OH || ow0 >= p.OW || f0 >= p.N) continue;  // padding positions
         float acc_v[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) acc_v[i] = __uint_as_float(r[i]);

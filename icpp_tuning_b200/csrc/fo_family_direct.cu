@@ -17,14 +17,19 @@ static cudaError_t launch_direct_k(const LaunchArgs& a) {
     if (e != cudaSuccess) return e;
     opted.fetch_or(bit, std::memory_order_acq_rel);
   }
-  kern<<<a.grid, 320, a.smem, a.stream>>>(a.tmA, a.tmB, a.tmC, a.p);
+  kern<<<a.grid, kDirectThreads, a.smem, a.stream>>>(a.tmA, a.tmB, a.tmC, a.p);
   return cudaGetLastError();
 }
 
-// One filter tap per weight stage, or two (block_k 128).
+// One filter tap per weight stage, two (block_k 128) or three (block_k 192).
 template <int ACT, int OUT>
 static cudaError_t launch_direct(const LaunchArgs& a) {
-  return a.p.kps == 2 ? launch_direct_k<ACT, OUT, 2>(a) : launch_direct_k<ACT, OUT, 1>(a);
+  switch (a.p.kps) {
+    case 1: return launch_direct_k<ACT, OUT, 1>(a);
+    case 2: return launch_direct_k<ACT, OUT, 2>(a);
+    case 3: return launch_direct_k<ACT, OUT, 3>(a);
+  }
+  return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_direct_conv(int act, int out_dt, const LaunchArgs& a) {

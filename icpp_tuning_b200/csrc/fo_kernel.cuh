@@ -80,8 +80,9 @@ struct KParams {
   int H, W, C, OH, OW, KH, KW, stride, pad, dil, c_blocks;
   int conv_tma;  // 1: A tiles by TMA im2col loads (tmA); 0: cp.async gather
   // direct conv (fo_direct_conv_kernel): input rows padded to pitch P positions, Hp padded
-  // rows per image, nR rows per pixel slot, pslots slots, nimg images
-  int P, Hp, nR, pslots, nimg;
+  // rows per image, nR rows per pixel slot, pslots slots, nimg images; a tile is rpt
+  // output rows (rpt * P positions) of one image, tpi tiles per image
+  int P, Hp, nR, pslots, nimg, rpt, tpi;
   // k-blocks (64-wide K slices) per pipeline stage: 1 or 2 (block_k 128).  Two per stage
   // halve the barrier waits, fences and commits the single MMA-issuing thread spends per
   // MMA (8 MMAs per wait / commit instead of 4).

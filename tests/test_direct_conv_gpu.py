@@ -11,12 +11,14 @@ from tests.gpu_util import TOL, assert_close, cuda, gen, randn, status_clean
 pytestmark = pytest.mark.gpu
 
 
-def dcfg(stages=4, block_k=64):
-    return N.tile_cfg(block_n=256, stages=stages, group_m=0, swap_ab=2, block_k=block_k)
+def dcfg(stages=4, block_k=64, block_n=256):
+    """block_n caps the tile's positions (rows of P padded positions); the host picks the
+    rows per tile."""
+    return N.tile_cfg(block_n=block_n, stages=stages, group_m=0, swap_ab=2, block_k=block_k)
 
 
 SHAPES = [  # n, h, w, c, f, k, pad
-    (2, 28, 28, 128, 128, 3, 1),   # P = 32: 8 padded rows per tile
+    (2, 28, 28, 128, 128, 3, 1),   # P = 32: 7-row tiles, 4 per image
     (3, 30, 30, 64, 192, 3, 1),    # W + 2 pad = 32 exactly; two channel tiles
     (2, 56, 56, 64, 72, 3, 1),     # P = 64; a partial channel tile (72)
     (1, 28, 28, 64, 64, 5, 2),     # 5x5
@@ -27,18 +29,36 @@ SHAPES = [  # n, h, w, c, f, k, pad
 
 
 @pytest.mark.parametrize("shape", SHAPES, ids=str)
-@pytest.mark.parametrize("odt,bk", [(torch.bfloat16, 64), (torch.float32, 64), (torch.bfloat16, 128)])
+@pytest.mark.parametrize("odt,bk", [(torch.bfloat16, 64), (torch.float32, 64), (torch.bfloat16, 128), (torch.bfloat16, 192)])
 def test_direct_conv_bias_relu(shape, odt, bk):
-    """block_k 128: two filter taps per weight stage (5x5: an odd tap count, 1x1: one)."""
+    """block_k 128 / 192: two / three filter taps per weight stage (5x5: a tap count that
+    neither divides, 1x1: one)."""
     n, h, w, c, f, k, p = shape
     g = gen(70)
     x = randn(g, n, h, w, c)
     wt = randn(g, k, k, c, f, scale=(k * k * c) ** -0.5)
     bias = randn(g, f, scale=0.1)
     out = fused.conv2d_nhwc(*cuda(x, wt), bias=bias.cuda(), relu=True, padding=p, out_dtype=odt,
-                            config=dcfg(3 if bk == 128 else 4, bk))
+                            config=dcfg({64: 4, 128: 3, 192: 2}[bk], bk))
     ref = R.conv2d_bias_relu(x, wt, bias, True, 1, p, 1, out_dtype=odt)
     assert_close(out, ref, TOL)
+    status_clean()
+
+
+@pytest.mark.parametrize("shape", [(2, 28, 28, 128, 128, 3, 1), (1, 17, 13, 192, 128, 3, 1), (3, 30, 30, 64, 64, 5, 2),
+                                   (2, 9, 20, 64, 96, 3, 1)], ids=str)
+def test_direct_conv_narrow_tiles(shape):
+    """block_n 128: at most 128 positions (4 rows of 32) per tile, half of the epilogue
+    warps idle; 9 x 20: P = 32 with OH = 9 (tiles of 3 rows, or 4 + 4 + 1)."""
+    n, h, w, c, f, k, p = shape
+    g = gen(74)
+    x = randn(g, n, h, w, c)
+    wt = randn(g, k, k, c, f, scale=(k * k * c) ** -0.5)
+    bias = randn(g, f, scale=0.1)
+    for bn in (128, 256):
+        out = fused.conv2d_nhwc(*cuda(x, wt), bias=bias.cuda(), relu=True, padding=p, config=dcfg(4, 64, bn))
+        ref = R.conv2d_bias_relu(x, wt, bias, True, 1, p, 1, out_dtype=torch.bfloat16)
+        assert_close(out, ref, TOL)
     status_clean()
 
 

@@ -3,6 +3,7 @@ memory / TMEM model equals the library's, and the BASELINE shapes get a config."
 import pytest
 
 from icpp_tuning_b200 import _native as N
+from icpp_tuning_b200 import fused
 from icpp_tuning_b200.autotuner.cost_model import TuneConfig
 from icpp_tuning_b200.autotuner.gpu_spec import known_gpu
 from icpp_tuning_b200.autotuner.interface import rank_all, select_best
@@ -25,9 +26,11 @@ SHAPES = [
 def test_every_config_legal_for_the_library(conv):
     for raw in tcgen05_configs(conv=conv, stages=range(2, 9)):
         cfg = N.tile_cfg(block_n=raw["block_N"], stages=raw["num_stages"], group_m=raw["group_m"],
-                         block_m=raw["block_M"])
+                         block_m=raw["block_M"], block_k=raw["block_K"], swap_ab=raw.get("swap_ab", 0))
         ok, why = N.config_legal(1 if conv else 0, N.FO_DT_BF16, cfg)
         assert ok, why
+        if raw.get("swap_ab") == 2 or raw["block_K"] != 64:
+            continue  # the direct conv's shared memory depends on the image width
         want = smem_bytes(raw["block_N"], raw["num_stages"], raw["block_M"])
         assert N.config_smem_bytes(1 if conv else 0, N.FO_DT_BF16, cfg) == want
         tc = TuneConfig(raw["block_M"], raw["block_N"], 64, raw["num_stages"], raw["thread_num"] // 32, kind="tcgen05")
@@ -54,8 +57,7 @@ def test_baseline_shapes_select_legal(desc, shape):
     raw, score = select_best(desc, hw=B200, **shape)
     assert 0.0 < score <= 1.0
     op = 1 if "conv" in desc.name else 0
-    ok, why = N.config_legal(op, N.FO_DT_BF16, N.tile_cfg(block_n=raw["block_N"], stages=raw["num_stages"],
-                                                          group_m=raw["group_m"], block_m=raw["block_M"]))
+    ok, why = N.config_legal(op, N.FO_DT_BF16, fused.as_tile_cfg(raw))
     assert ok, why
     rk = rank_all(desc, hw=B200, detailed=True, **shape)
     assert rk[0]["score"] == score
