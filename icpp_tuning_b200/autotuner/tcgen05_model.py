@@ -62,10 +62,10 @@ CONSTANTS = {
     # of a tiled load's rate: measured 589 vs 836 TFLOP/s for BN=128 conv vs GEMM tiles
     "im2col_rate": 0.7,
     # direct conv: mainloop rate of a 128 x (rows x pitch) tile per taps-per-weight-stage
-    # (one MMA issue wait per stage; config5 224-position tiles measured 7.4 / 6.7 / 6.4
-    # us per tile for 1 / 2 / 3 taps per stage), and the factor when only one pixel slot
-    # fits (its reload is then not overlapped)
-    "direct_rate_kps": {1: 0.79, 2: 0.87, 3: 0.90},
+    # (one MMA issue wait per stage, issued by a warp-uniform loop; config5 224-position
+    # tiles measured 56.3 / 56.5 / 59.7 us for 1 tap x 6 stages, 2 x 3 and 3 x 2), and the
+    # factor when only one pixel slot fits (its reload is then not overlapped)
+    "direct_rate_kps": {1: 0.875, 2: 0.87, 3: 0.82},
     "direct_one_slot": 0.7,
     "mma_issue_cycles": 130,  # one thread issuing back-to-back MMAs with a wait per stage
     "fixed_s": 6.0e-6,  # launch + TMEM alloc + pipeline fill + last epilogue

@@ -181,79 +181,87 @@ __global__ void __launch_bounds__(kDirectThreads, 1)
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      // The issuing thread is the bottleneck of this loop (each tcgen05.mma takes ~60 issue
-      // cycles, a commit ~60, against 540 tensor cycles per tap), so every descriptor is
-      // stepped, not recomputed: the weights by one stage (16 KB) per tap, the rows by one
-      // position (128 B) per dx and by P - KW + 1 positions at the end of a filter row.
-      const uint32_t idesc = idesc_f16(p.ab_bf16, 0, BN, 128) | (1u << 15);  // A (weights) MN-major
-      const uint64_t a_desc0 = sdesc_sw128(sW, 64 * 128, 1024);
-      const uint64_t b_desc0 = sdesc_sw128_rows(sPix);
-      const uint32_t slot_units = static_cast<uint32_t>(slot_bytes) >> 4;
-      const uint32_t wrap_units = static_cast<uint32_t>(p.P - p.KW + 1) * 8;
-      int s = 0, ps = 0, acc = 0;
-      uint32_t ph = 0, pph = 0, acc_ph = 0;
-      uint64_t ad = a_desc0;
-      bool ok = true;
-      for (int u = cid; u < p.num_units && ok; u += ncl) {
-        if (!mbar_wait(bar_tempty + 8 * acc, acc_ph ^ 1, tmo, abort_flag)) {
+    // The whole warp runs this loop and lane 0 alone waits, issues and commits (elect.sync
+    // inside the MMA / commit instructions), so the loop's control flow and descriptor
+    // arithmetic stay warp-uniform.  The issuing lane is the bottleneck of this loop (each
+    // tcgen05.mma takes ~60 issue cycles, a commit ~60, against 448 tensor cycles per tap),
+    // so every descriptor is stepped, not recomputed: the weights by one stage (16 KB) per
+    // tap, the rows by one position (128 B) per dx and by P - KW + 1 positions at the end
+    // of a filter row.
+    auto wait = [&](uint32_t bar, uint32_t parity) {
+      int r = 1;
+      if (lane == 0) r = mbar_wait(bar, parity, tmo, abort_flag) ? 1 : 0;
+      return __shfl_sync(0xffffffffu, r, 0) != 0;
+    };
+    const uint32_t idesc = idesc_f16(p.ab_bf16, 0, BN, 128) | (1u << 15);  // A (weights) MN-major
+    const uint64_t a_desc0 = sdesc_sw128(sW, 64 * 128, 1024);
+    const uint64_t b_desc0 = sdesc_sw128_rows(sPix);
+    const uint32_t slot_units = static_cast<uint32_t>(slot_bytes) >> 4;
+    const uint32_t wrap_units = static_cast<uint32_t>(p.P - p.KW + 1) * 8;
+    int s = 0, ps = 0, acc = 0;
+    uint32_t ph = 0, pph = 0, acc_ph = 0;
+    uint64_t ad = a_desc0;
+    bool ok = true;
+    for (int u = cid; u < p.num_units && ok; u += ncl) {
+      if (!wait(bar_tempty + 8 * acc, acc_ph ^ 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d = tmem_base + acc * kDirectMaxBN;
+      uint32_t accum = 0;
+      for (int cb = 0; cb < p.c_blocks && ok; ++cb) {
+        if (!wait(bar_pfull + 8 * ps, pph)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t d = tmem_base + acc * kDirectMaxBN;
-        uint32_t accum = 0;
-        for (int cb = 0; cb < p.c_blocks && ok; ++cb) {
-          if (!mbar_wait(bar_pfull + 8 * ps, pph, tmo, abort_flag)) {
+        uint64_t bd = b_desc0 + static_cast<uint64_t>(ps * slot_units);
+        int dx = 0;
+        for (int t = 0; t < taps; t += KPS) {
+          const int nk = KPS == 1 ? 1 : min(KPS, taps - t);
+          if (!wait(bar_full + 8 * s, ph)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          uint64_t bd = b_desc0 + static_cast<uint64_t>(ps * slot_units);
-          int dx = 0;
-          for (int t = 0; t < taps; t += KPS) {
-            const int nk = KPS == 1 ? 1 : min(KPS, taps - t);
-            if (!mbar_wait(bar_full + 8 * s, ph, tmo, abort_flag)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
 #pragma unroll
-            for (int i = 0; i < KPS; ++i) {
-              if (KPS > 1 && i >= nk) break;
-              const uint64_t a = ad + static_cast<uint64_t>(i * (kDirectWStage >> 4));
-              tc_mma_f16(d, a, bd, idesc, accum);
-              tc_mma_f16(d, a + (2048 >> 4), bd + (32 >> 4), idesc, 1u);
-              tc_mma_f16(d, a + 2 * (2048 >> 4), bd + 2 * (32 >> 4), idesc, 1u);
-              tc_mma_f16(d, a + 3 * (2048 >> 4), bd + 3 * (32 >> 4), idesc, 1u);
-              accum = 1u;
-              if (++dx == p.KW) {
-                dx = 0;
-                bd += wrap_units;
-              } else {
-                bd += 8;
-              }
-            }
-            tc_commit(bar_empty + 8 * s);
-            if (++s == stages) {
-              s = 0;
-              ph ^= 1;
-              ad = a_desc0;
+          for (int i = 0; i < KPS; ++i) {
+            if (KPS > 1 && i >= nk) break;
+            const uint64_t a = ad + static_cast<uint64_t>(i * (kDirectWStage >> 4));
+            tc_mma_f16_elect(d, a, bd, idesc, accum);
+            tc_mma_f16_elect(d, a + (2048 >> 4), bd + (32 >> 4), idesc, 1u);
+            tc_mma_f16_elect(d, a + 2 * (2048 >> 4), bd + 2 * (32 >> 4), idesc, 1u);
+            tc_mma_f16_elect(d, a + 3 * (2048 >> 4), bd + 3 * (32 >> 4), idesc, 1u);
+            accum = 1u;
+            if (++dx == p.KW) {
+              dx = 0;
+              bd += wrap_units;
             } else {
-              ad += KPS * (kDirectWStage >> 4);
+              bd += 8;
             }
           }
-          tc_commit(bar_pempty + 8 * ps);
-          if (++ps == p.pslots) {
-            ps = 0;
-            pph ^= 1;
+          tc_commit_elect(bar_empty + 8 * s);
+          if (++s == stages) {
+            s = 0;
+            ph ^= 1;
+            ad = a_desc0;
+          } else {
+            ad += KPS * (kDirectWStage >> 4);
           }
         }
-        if (!ok) break;
-        tc_commit(bar_tfull + 8 * acc);
-        acc ^= 1;
-        if (acc == 0) acc_ph ^= 1;
+        tc_commit_elect(bar_pempty + 8 * ps);
+        if (++ps == p.pslots) {
+          ps = 0;
+          pph ^= 1;
+        }
       }
+      if (!ok) break;
+      tc_commit_elect(bar_tfull + 8 * acc);
+      acc ^= 1;
+      if (acc == 0) acc_ph ^= 1;
+    }
+    if (lane == 0) {
       if (!ok) {
         record_error(p, kStatusTimeout, 0x41);
         *abort_flag = 1;
