@@ -628,6 +628,7 @@ int fo_gemm(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
     if (pl.split > 1) {
       p.split_cnt = static_cast<int*>(d->workspace);
       p.split_ws = reinterpret_cast<float*>(static_cast<char*>(d->workspace) + split_counter_bytes(pl, pair ? 2 : 1));
+      p.tail_first = 1;
     }
     la.grid = pair ? 2 * pl.grid : pl.grid;
     la.smem = fo::smem_bytes_for(bn, cfg->stages, pair, p.kps);
@@ -940,6 +941,7 @@ int fo_conv2d(const FoConvDesc* d, const FoTileCfg* cfg, void* stream) {
     p.split_cnt = static_cast<int*>(d->workspace);
     p.split_ws = reinterpret_cast<float*>(static_cast<char*>(d->workspace) +
                                           split_counter_bytes(pl, 1));
+    p.tail_first = 1;
   }
   la.grid = pl.grid * (pair ? 2 : 1);
   p.kps = 1;  // conv kernels stage one K slice (block_k 128 is a GEMM-family option)

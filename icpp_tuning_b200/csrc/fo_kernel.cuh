@@ -90,6 +90,10 @@ struct KParams {
   // work units: units [0, dp_units) are whole tiles; the remaining tiles are split along K
   // into `split` parts of kb_per_part k-blocks, reduced through split_ws / split_cnt.
   int num_units, dp_units, split, kb_per_part;
+  // 1: the split parts run first (unit u < num_units - dp_units is split part u, whole
+  // tile w is unit w + num_units - dp_units), so their partial-sum exchange overlaps the
+  // whole tiles' mainloops instead of ending the grid.
+  int tail_first;
   // conv BatchNorm epilogues (inference form): per output channel f, with acc rounded to
   // the input dtype first, y = (acc - mean[f]) * rsqrt(var[f] + bn_eps) * gamma[f] + beta[f], var clamped at 0
   // when bn_mode == 2; then + add_src[pixel][f] when add_src is set; then ACT.
@@ -308,6 +312,10 @@ struct Unit {
 __device__ __forceinline__ Unit unit_of(const KParams& p, int u) {
   Unit r;
   int tile;
+  if (p.tail_first) {
+    const int parts = p.num_units - p.dp_units;
+    u = u < parts ? p.dp_units + u : u - parts;
+  }
   if (u < p.dp_units) {
     tile = u;
     r.kb0 = 0;
