@@ -229,10 +229,7 @@ __global__ void __launch_bounds__(kDirectThreads, 1)
           for (int i = 0; i < KPS; ++i) {
             if (KPS > 1 && i >= nk) break;
             const uint64_t a = ad + static_cast<uint64_t>(i * (kDirectWStage >> 4));
-            tc_mma_f16_elect(d, a, bd, idesc, accum);
-            tc_mma_f16_elect(d, a + (2048 >> 4), bd + (32 >> 4), idesc, 1u);
-            tc_mma_f16_elect(d, a + 2 * (2048 >> 4), bd + 2 * (32 >> 4), idesc, 1u);
-            tc_mma_f16_elect(d, a + 3 * (2048 >> 4), bd + 3 * (32 >> 4), idesc, 1u);
+            tc_mma_f16_x4_elect(d, a, bd, idesc, accum, 2048 >> 4, 32 >> 4);
             accum = 1u;
             if (++dx == p.KW) {
               dx = 0;

@@ -328,18 +328,27 @@ __device__ __forceinline__ void tc_commit(uint32_t bar) {
                    bar)
                : "memory");
 }
-// The same two operations issued by one lane of a converged warp: the whole warp runs
-// the issuing loop (so its control flow and descriptor arithmetic stay warp-uniform) and
-// elect.sync picks the lowest active lane -- lane 0 of a full warp, every time, so the
-// commits track that lane's own MMAs.
-__device__ __forceinline__ void tc_mma_f16_elect(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
-                                                 uint32_t idesc, uint32_t accumulate) {
+// MMA issue and commit by one lane of a converged warp: the whole warp runs the issuing
+// loop (so its control flow and descriptor arithmetic stay warp-uniform) and elect.sync
+// picks the lowest active lane -- lane 0 of a full warp, every time, so the commits
+// track that lane's own MMAs.
+// Four MMAs along K (one 64-wide K slice) issued under one elect.sync: A and B step by
+// a_step / b_step descriptor units per 16-wide K step.
+__device__ __forceinline__ void tc_mma_f16_x4_elect(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                                    uint32_t idesc, uint32_t accumulate, uint64_t a_step,
+                                                    uint64_t b_step) {
   asm volatile(
-      "{\n\t.reg .pred p, e;\n\t"
+      "{\n\t.reg .pred p, q, e;\n\t.reg .b64 a1, a2, a3, b1, b2, b3;\n\t"
       "elect.sync _|e, 0xffffffff;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+      "setp.eq.b32 q, %4, %4;\n\t"
+      "add.s64 a1, %1, %5;\n\tadd.s64 a2, a1, %5;\n\tadd.s64 a3, a2, %5;\n\t"
+      "add.s64 b1, %2, %6;\n\tadd.s64 b2, b1, %6;\n\tadd.s64 b3, b2, %6;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a1, b1, %3, q;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a2, b2, %3, q;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a3, b3, %3, q;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "l"(a_step), "l"(b_step));
 }
 __device__ __forceinline__ void tc_commit_elect(uint32_t bar) {
   asm volatile(
