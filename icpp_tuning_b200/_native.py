@@ -145,7 +145,7 @@ def launch_count() -> int:
 
 
 SPLIT_AUTO, SPLIT_WORKSPACE, SPLIT_CLUSTER = 0, 1, 2
-LN_AUTO, LN_TWO_KERNELS, LN_ONE_KERNEL = 0, 1, 2
+LN_AUTO, LN_TWO_KERNELS, LN_ONE_KERNEL, LN_HELD = 0, 1, 2, 3
 
 
 def tile_cfg(block_n: int = 256, stages: int = 4, group_m: int = 8, max_ctas: int = 0,

@@ -58,6 +58,10 @@ CONSTANTS = {
     # GEMM + bias kernel for 2 x 128 MiB)
     "ln_fused_bytes_per_s": 4.6e12,
     "ln_fused_tail_s": 7.4e-6,  # its normalisation after the last unit (2048 x 4096: +2.7 us)
+    # slices held in TMEM (<= 4 waves): the extra epilogue time as a share of a separate
+    # row pass's (measured 2-5% faster than the two-kernel path on 8192 x 768..1024 and
+    # 2048..4096 x 4096 shapes, whose row pass is 8-15% of the call)
+    "ln_held_factor": 0.6,
     # TMA im2col loads (one 128-pixel x 64-channel box per filter tap) run at this share
     # of a tiled load's rate: measured 589 vs 836 TFLOP/s for BN=128 conv vs GEMM tiles
     "im2col_rate": 0.7,
@@ -328,7 +332,11 @@ def _model(op: OpSpec, c: TuneConfig, hw: GPUSpec) -> dict:
     t_ln = 0.0
     if op.has_reduction_epilogue:
         ln_bytes = 2.0 * op.M * op.N * ml.output_element_bytes
-        if bn >= 128 and op.M * op.N >= (1 << 24):  # the C ABI runs these as one kernel
+        held = (bn >= 128 and c.group_size_m == 0 and tiles_n - 1 < ctas and waves <= 4 and op.K >= 2048
+                and op.M * op.N >= (1 << 22))
+        if held:  # the C ABI holds the slices in TMEM (fo_api.cu, automatic ln_mode)
+            t_ln = K["ln_held_factor"] * ln_bytes / K["ln_pass_bytes_per_s"]
+        elif bn >= 128 and op.M * op.N >= (1 << 24):  # the C ABI runs these as one kernel
             t_ln = ln_bytes / K["ln_fused_bytes_per_s"] + K["ln_fused_tail_s"]
         else:
             t_ln = ln_bytes / K["ln_pass_bytes_per_s"]

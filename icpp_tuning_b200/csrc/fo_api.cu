@@ -211,8 +211,9 @@ int check_cfg(int op, int out_dtype, const FoTileCfg* cfg, char* why, size_t why
   if (cfg->split_k < 0 || cfg->split_k > 16) return say("split_k must be 0 (automatic) .. 16, got %d", cfg->split_k);
   if (cfg->split_mode < 0 || cfg->split_mode > 2)
     return say("split_mode must be 0 (automatic), 1 (workspace) or 2 (cluster), got %d", cfg->split_mode);
-  if (cfg->ln_mode < 0 || cfg->ln_mode > 2)
-    return say("ln_mode must be 0 (automatic), 1 (two kernels) or 2 (one kernel), got %d", cfg->ln_mode);
+  if (cfg->ln_mode < 0 || cfg->ln_mode > 3)
+    return say("ln_mode must be 0 (automatic), 1 (two kernels), 2 (one kernel) or 3 (one kernel, slices held in "
+               "TMEM), got %d", cfg->ln_mode);
   // (the direct conv's shared memory depends on the image width: fo_conv2d checks it)
   const int smem = fo::smem_bytes_for(cfg->block_n, cfg->stages, cfg->block_m == 256, cfg->block_k / 64);
   if (cfg->swap_ab != 2 && smem > 232448) return say("shared memory %d B exceeds the 227 KB per-block limit", smem);
@@ -641,16 +642,32 @@ int fo_gemm(const FoGemmDesc* d, const FoTileCfg* cfg, void* stream) {
       if (cfg->ln_mode == 2 && !eligible)
         return fail(FO_EINVAL, "one-kernel LayerNorm needs block_n >= 128 and each row block's %d tiles within %d "
                     "waves of the tile raster (use group_m 0 or ln_mode 1)", p.tiles_n, fo::kLnMaxDefer);
+      // Held slices: a unit's epilogue waits for its row block's other tiles while it
+      // holds its accumulator, which is cycle-free when those tiles lie within fewer
+      // units of the raster than one wave has (span < units per wave).
+      const bool held_ok = bn >= 128 && span < pl.grid;
+      if (cfg->ln_mode == 3 && !held_ok)
+        return fail(FO_EINVAL, "one-kernel LayerNorm with held slices needs block_n >= 128 and each row block's tiles "
+                    "within %d units of the raster (span %d; use group_m 0, fewer column tiles or ln_mode 1)",
+                    pl.grid - 1, span);
       // Automatic: one kernel from 16M outputs up.  Below that the row pass is short and
       // the one kernel's normalisation tail (wait, read-back, store after the last unit)
       // measured 3-9 us slower (B200: 2048 x 4096 +2.7 us; 16384 x 4096 -30 us).
       const bool large = static_cast<int64_t>(p.M) * p.N >= (int64_t{1} << 24);
-      if (eligible && (cfg->ln_mode == 2 || large)) {
-        p.ln_fused = 1;
+      // Automatic, held slices: up to 4 waves of units, K >= 2048 and 4M outputs, where
+      // they measured fastest (B200, 256 x 256 pair tiles: 8192 x 1024 x 4096 71.6 us vs
+      // 74.8 two-kernel / 75.7 stored; 4096^3 123.4 vs 128.4 / 126.0).  With more waves a
+      // late tile delays its row block's partners, and the delays add up from wave to
+      // wave (16384 x 4096 x 4096: 422 vs 390 us stored).
+      const int waves = (pl.num_units + pl.grid - 1) / pl.grid;
+      const bool held_auto = held_ok && cfg->ln_mode == 0 && waves <= 4 && p.K >= 2048 &&
+                             static_cast<int64_t>(p.M) * p.N >= (int64_t{1} << 22);
+      if (cfg->ln_mode == 3 || held_auto || (eligible && (cfg->ln_mode == 2 || large))) {
+        p.ln_fused = cfg->ln_mode == 3 || held_auto ? 2 : 1;
         p.ln_span = span;
         la.coop = true;
         e = launch();
-        if (e != cudaSuccess && cfg->ln_mode == 2)
+        if (e != cudaSuccess && cfg->ln_mode >= 2)
           return fail(FO_ECUDA, "one-kernel LayerNorm launch failed: %s", cudaGetErrorString(e));
         if (e != cudaSuccess) {  // automatic: the two-kernel path instead
           cudaGetLastError();

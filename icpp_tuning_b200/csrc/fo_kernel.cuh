@@ -116,7 +116,11 @@ struct KParams {
   // epilogue warp publishes the (mean, M2) of its row slice to ln_st2[slice][row] and
   // counts itself into ln_cnt[row / 32]; the arrival that completes the 32 rows merges
   // their statistics into ln_fin; some units later the same warp reads its stored slice
-  // back and normalises it in place.  ln_cnt holds 2 x ln_groups int32 (arrivals, then finished normalisers),
+  // back and normalises it in place.  ln_fused = 2: the warp keeps its slice in the TMEM
+  // accumulator instead (nothing stored early), waits at the same unit for the merged
+  // statistics and normalises straight from TMEM before releasing the accumulator; this
+  // needs every row block's tiles within ln_span < (units per wave) of each other.
+  // ln_cnt holds 2 x ln_groups int32 (arrivals, then finished normalisers),
   // zero at launch and reset to zero by the last normaliser of each group.
   int ln_fused;
   int ln_span;    // largest unit distance between two tiles of one row block
@@ -950,6 +954,117 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
       --nh;
       return r;
     };
+    // ln_fused == 2: the slice of tile (tm_, tn_) is still in accumulator acc_ (this warp's
+    // rows and column half).  Waits for its 32 rows' merged (mean, rstd), then re-reads
+    // TMEM, adds the bias (aff_: lane l holds column 32 j + l of the half), normalises and
+    // stores each 64-column chunk once, and releases the accumulator.  Returns false when
+    // the wait ran out (the accumulator is released all the same).
+    auto ln_held = [&](int tm_, int tn_, int acc_, bool has_k_, const float2* aff_) -> bool {
+      const int r0 = tm_ * kTileM + static_cast<int>(rank) * kBM + quarter * 32;
+      bool good = true;
+      float mean = 0.f, rstd = 0.f;
+      auto release = [&]() {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (PAIR) {
+            mbar_arrive_cluster(mapa_shared(bar_tempty + 8 * acc_, 0));
+          } else {
+            mbar_arrive(bar_tempty + 8 * acc_);
+          }
+        }
+      };
+      if (r0 >= p.M) {
+        release();
+        return true;
+      }
+      const int grp = r0 >> 5;
+      const int target = 2 * p.tiles_n + 1;
+      int ready = 1;
+      if (lane == 0) {
+        const int* cp = p.ln_cnt + grp;
+        if (ld_acquire_gpu(cp) < target) {
+          const uint64_t t0 = global_timer_ns();
+          while (ld_acquire_gpu(cp) < target) {
+            if (*abort_flag || global_timer_ns() - t0 > tmo) {
+              ready = 0;
+              break;
+            }
+            __nanosleep(64);
+          }
+        }
+      }
+      good = __shfl_sync(0xffffffffu, ready, 0) != 0;
+      if (!good) {
+        release();
+        return false;
+      }
+      const int row = r0 + lane;  // lane i owns row r0 + i
+      const float2 fin = row < p.M ? __ldcg(p.ln_fin + row) : make_float2(0.f, 0.f);
+      mean = fin.x;
+      rstd = fin.y;
+      if (lane == 0 && atomicAdd(p.ln_cnt + p.ln_groups + grp, 1) == target - 2) {
+        // every normaliser of these rows has seen the arrivals: reset both counters
+        atomicExch(p.ln_cnt + grp, 0);
+        atomicExch(p.ln_cnt + p.ln_groups + grp, 0);
+      }
+#pragma unroll 1
+      for (int ci = 0; ci < kHalfChunks; ++ci) {
+        const int tc = hcol + ci * kCW;
+        const int cbase = tn_ * BN + tc;
+        float v[kCW];
+        {
+          uint32_t q0[32], q1[32];
+          tmem_ld_32x32b_x32(tmem_base + lane_off + acc_ * BN + tc, q0);
+          if constexpr (kCW == 64) tmem_ld_32x32b_x32(tmem_base + lane_off + acc_ * BN + tc + 32, q1);
+          tc_wait_ld_regs(q0);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = has_k_ ? __uint_as_float(q0[i]) : 0.f;
+          if constexpr (kCW == 64) {
+            tc_pin_regs(q1);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[32 + i] = has_k_ ? __uint_as_float(q1[i]) : 0.f;
+          }
+        }
+        if (ci == kHalfChunks - 1) release();
+        // lane l loads gamma / beta of column 32 h + l once; shuffles hand them out
+#pragma unroll
+        for (int h = 0; h < kCW / 32; ++h) {
+          const int col = cbase + h * 32 + lane;
+          const float gl = col < p.N ? load_vec(p.gamma, p.vec_dtype, col) : 0.f;
+          const float bl = col < p.N ? load_vec(p.beta, p.vec_dtype, col) : 0.f;
+          const float al = p.has_bias ? aff_[ci * (kCW / 32) + h].y : 0.f;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float x = v[h * 32 + i] + __shfl_sync(0xffffffffu, al, i);
+            v[h * 32 + i] = fmaf((x - mean) * rstd, __shfl_sync(0xffffffffu, gl, i), __shfl_sync(0xffffffffu, bl, i));
+          }
+        }
+        if (nstore >= 1) {
+          if (lane == 0) bulk_wait_read<0>();
+          __syncwarp();
+        }
+        const uint32_t rowp = buf0 + lane * 128;
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+          const uint32_t w0 = pack2<OUT_DT>(v[8 * jj + 0], v[8 * jj + 1]);
+          const uint32_t w1 = pack2<OUT_DT>(v[8 * jj + 2], v[8 * jj + 3]);
+          const uint32_t w2 = pack2<OUT_DT>(v[8 * jj + 4], v[8 * jj + 5]);
+          const uint32_t w3 = pack2<OUT_DT>(v[8 * jj + 6], v[8 * jj + 7]);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(rowp + ((jj ^ (lane & 7)) << 4)), "r"(w0),
+                       "r"(w1), "r"(w2), "r"(w3)
+                       : "memory");
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d_hint(&tmC, buf0, cbase, r0, l2_policy_evict_first());
+          bulk_commit();
+        }
+        ++nstore;
+      }
+      return true;
+    };
     for (int u = cid; u < p.num_units; u += ncl) {
       const Unit un = unit_of(p, u);
       const int tm = un.tm, tn = un.tn;
@@ -1345,7 +1460,7 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
             for (int i = 0; i < kCW; ++i) v[i] += part_value(q, tc - hcol + i);
           }
         }
-        if (ci == kHalfChunks - 1) {
+        if (ci == kHalfChunks - 1 && !(LN && p.ln_fused == 2)) {
           // The accumulator buffer is free once every lane's loads of it have completed.
           tc_fence_before();
           __syncwarp();
@@ -1431,7 +1546,9 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
           st_mean += (s1[0] + s1[1]) + (s1[2] + s1[3]);  // S1 until the slice ends
           st_m2 += (s2[0] + s2[1]) + (s2[2] + s2[3]);    // S2 until the slice ends
         }
-        if constexpr (kNarrow) {
+        if (LN && p.ln_fused == 2) {
+          // held in TMEM: stored once, normalised, by ln_held below
+        } else if constexpr (kNarrow) {
           // 16-bit BN 64: lane l stores row row0 + l of this 32-column half, 64
           // contiguous bytes, straight from registers.
           const int row = row0 + lane;
@@ -1539,18 +1656,26 @@ __global__ void __launch_bounds__(CONV ? 416 : 320, 1)
               if (lane == 0) red_add_release_gpu(p.ln_cnt + (row0 >> 5), 1);
             }
           }
-#pragma unroll
-          for (int i = 0; i < kLnQ; ++i) {
-            if (i == nh) {
-              h_tm[i] = tm;
-              h_tn[i] = tn;
-              h_sh[i] = shift;
+          if (p.ln_fused == 2) {
+            // the accumulator just flipped: this unit's slice is in buffer acc ^ 1
+            if (!ln_held(tm, tn, acc ^ 1, has_k, aff)) {
+              ok = false;
+              break;
             }
-          }
-          ++nh;
-          if (nh > ln_defer && !ln_pop(false)) {
-            ok = false;
-            break;
+          } else {
+#pragma unroll
+            for (int i = 0; i < kLnQ; ++i) {
+              if (i == nh) {
+                h_tm[i] = tm;
+                h_tn[i] = tn;
+                h_sh[i] = shift;
+              }
+            }
+            ++nh;
+            if (nh > ln_defer && !ln_pop(false)) {
+              ok = false;
+              break;
+            }
           }
         } else {
           // Per-tile row statistics; the row pass (launched next on the same stream)

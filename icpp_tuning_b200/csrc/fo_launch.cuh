@@ -83,8 +83,10 @@ cudaError_t launch_tc_k(const LaunchArgs& a) {
     }
     if (mc > 0 && static_cast<int>(cfg.gridDim.x) > 2 * mc) cfg.gridDim.x = 2 * mc;
     // the one-kernel LayerNorm's wait depth follows the number of pairs actually launched
-    if (LN && a.p.ln_fused && ln_defer_for(a.p.ln_span, static_cast<int>(cfg.gridDim.x) / 2) > kLnMaxDefer)
+    if (LN && a.p.ln_fused == 1 && ln_defer_for(a.p.ln_span, static_cast<int>(cfg.gridDim.x) / 2) > kLnMaxDefer)
       return cudaErrorCooperativeLaunchTooLarge;
+    if (LN && a.p.ln_fused == 2 && a.p.ln_span >= static_cast<int>(cfg.gridDim.x) / 2)
+      return cudaErrorCooperativeLaunchTooLarge;  // held slices need span < pairs launched
     if (a.coop) attr[1] = coop;  // a cooperative grid is not a programmatic dependent
     cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, kern, a.tmA, a.tmB, a.tmC, a.p);

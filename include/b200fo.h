@@ -94,6 +94,11 @@ typedef struct FoTileCfg {
                     /* 2 = one kernel: each epilogue warp normalises its own stored slice */
                     /*     once every slice of its rows has published its statistics     */
                     /*     (block_n >= 128; a cooperative launch, all CTAs resident)     */
+                    /* 3 = one kernel, slices held: each epilogue warp keeps its slice in */
+                    /*     the TMEM accumulator until its rows' statistics are merged,    */
+                    /*     then normalises and stores it once (block_n >= 128, every row  */
+                    /*     block's tiles within fewer raster units than one wave: group_m */
+                    /*     0 and tiles_n <= CTAs (pairs); cooperative launch)            */
 } FoTileCfg;
 
 /* One GEMM-family call.  A[M,K] row-major (row stride lda elements).  B per b_layout

@@ -89,6 +89,56 @@ def test_ln_one_kernel_rejections():
     assert_close(out, R.gemm_bias_layernorm(x, w, bias, gamma, beta, b_layout="nk", out_dtype=torch.bfloat16), TOL_LN)
 
 
+@pytest.mark.parametrize("bm,bn,bk,st", [(128, 128, 64, 6), (128, 256, 64, 4), (256, 256, 128, 3), (256, 128, 128, 4)])
+def test_ln_held(bm, bn, bk, st):
+    """ln_mode 3 (each epilogue warp keeps its slice in the TMEM accumulator until its
+    rows' statistics are merged, then normalises and stores it once) against the oracle
+    and the stored-slice one-kernel path, single CTAs and CTA pairs, ragged M and N; the
+    counters are left zeroed and a repeated call gives the same bits."""
+    M, Nn, K = 1500, 3000, 320
+    x, w, bias, gamma, beta = _inputs(16, M, Nn, K)
+    held = N.tile_cfg(bn, st, 0, block_m=bm, block_k=bk, ln_mode=N.LN_HELD)
+    n0 = N.launch_count()
+    out, ws = _ln_call(x, w, bias, gamma, beta, held)
+    assert N.launch_count() - n0 == 1
+    ref = R.gemm_bias_layernorm(x, w, bias, gamma, beta, b_layout="nk", out_dtype=torch.bfloat16)
+    assert_close(out, ref, TOL_LN)
+    assert int(ws[:_header_bytes(M)].count_nonzero()) == 0
+    again, _ = _ln_call(x, w, bias, gamma, beta, held, ws=ws)
+    assert torch.equal(again, out)
+    one, _ = _ln_call(x, w, bias, gamma, beta, N.tile_cfg(bn, st, 0, block_m=bm, block_k=bk, ln_mode=N.LN_ONE_KERNEL))
+    # the stored path rounds the centred slice to 16 bits once more: two output roundings apart
+    assert_close(out, one, TOL_LN)
+    status_clean()
+
+
+def test_ln_auto_takes_held_slices():
+    """Automatic mode holds the slices in TMEM for a problem of at most 4 waves with
+    K >= 2048 and >= 4M outputs: same bits as ln_mode 3, one launch, oracle on sampled rows."""
+    M, Nn, K = 4096, 1024, 2048
+    x, w, bias, gamma, beta = _inputs(18, M, Nn, K)
+    auto = N.tile_cfg(256, 3, 0, block_m=256, block_k=128)
+    n0 = N.launch_count()
+    out, _ = _ln_call(x, w, bias, gamma, beta, auto)
+    assert N.launch_count() - n0 == 1
+    held, _ = _ln_call(x, w, bias, gamma, beta, N.tile_cfg(256, 3, 0, block_m=256, block_k=128, ln_mode=N.LN_HELD))
+    assert torch.equal(out, held)
+    rows = torch.arange(0, M, 61)
+    ref = R.gemm_bias_layernorm(x[rows], w, bias, gamma, beta, b_layout="nk", out_dtype=torch.bfloat16)
+    assert_close(out[rows.cuda()], ref, TOL_LN)
+    status_clean()
+
+
+def test_ln_held_rejections():
+    """Held slices need block_n >= 128 and a raster whose row blocks span fewer units than
+    a wave (group_m 8 here spreads a row block over 8 x 23 units)."""
+    x, w, bias, gamma, beta = _inputs(17, 1500, 3000, 64)
+    with pytest.raises(N.FoError, match="held slices"):
+        _ln_call(x, w, bias, gamma, beta, N.tile_cfg(64, 8, 0, ln_mode=N.LN_HELD))
+    with pytest.raises(N.FoError, match="held slices"):
+        _ln_call(x, w, bias, gamma, beta, N.tile_cfg(128, 6, 8, ln_mode=N.LN_HELD))
+
+
 @pytest.mark.parametrize("M,Nn,bn", [(2000, 1000, 64), (1100, 2304, 256), (3000, 4096, 128), (100, 5000, 256),
                                      (1500, 6144, 128), (1, 768, 64)])
 def test_ln_row_pass_variants(M, Nn, bn):

@@ -182,12 +182,13 @@ def test_split_mode_field():
 
 
 def test_ln_mode_field_and_workspace():
-    """ln_mode: 0 automatic, 1 two kernels, 2 one kernel.  The LayerNorm workspace holds
+    """ln_mode: 0 automatic, 1 two kernels, 2 one kernel, 3 one kernel with the slices
+    held in TMEM.  The LayerNorm workspace holds
     the 32-row groups' arrival counters (two int32 each, 256-byte padded) and then one
     16-byte statistic per row per half-tile slice."""
-    for mode in (0, 1, 2):
+    for mode in (0, 1, 2, 3):
         assert N.config_legal(0, N.FO_DT_BF16, N.tile_cfg(128, 6, 8, ln_mode=mode))[0]
-    for bad in (-1, 3):
+    for bad in (-1, 4):
         ok, why = N.config_legal(0, N.FO_DT_BF16, N.tile_cfg(128, 6, 8, ln_mode=bad))
         assert not ok and "ln_mode" in why
     d = N.FoGemmDesc()
