@@ -112,6 +112,19 @@ def test_ln_held(bm, bn, bk, st):
     status_clean()
 
 
+def test_ln_held_fp16_ragged_rows():
+    """Held slices with fp16 output and M not a multiple of 32: the last row group's
+    partial warps still release their accumulators and the counters end at zero."""
+    M, Nn, K = 1000, 1536, 256
+    x, w, bias, gamma, beta = _inputs(19, M, Nn, K, dt=torch.float16)
+    cfg = N.tile_cfg(256, 3, 0, block_m=256, block_k=128, ln_mode=N.LN_HELD)
+    out, ws = _ln_call(x, w, bias, gamma, beta, cfg, odt=torch.float16)
+    ref = R.gemm_bias_layernorm(x, w, bias, gamma, beta, b_layout="nk", out_dtype=torch.float16)
+    assert_close(out, ref, TOL_LN)
+    assert int(ws[:_header_bytes(M)].count_nonzero()) == 0
+    status_clean()
+
+
 def test_ln_auto_takes_held_slices():
     """Automatic mode holds the slices in TMEM for a problem of at most 4 waves with
     K >= 2048 and >= 4M outputs: same bits as ln_mode 3, one launch, oracle on sampled rows."""
