@@ -90,9 +90,9 @@ struct KParams {
   // work units: units [0, dp_units) are whole tiles; the remaining tiles are split along K
   // into `split` parts of kb_per_part k-blocks, reduced through split_ws / split_cnt.
   int num_units, dp_units, split, kb_per_part;
-  // 1: the split parts run first (unit u < num_units - dp_units is split part u, whole
-  // tile w is unit w + num_units - dp_units), so their partial-sum exchange overlaps the
-  // whole tiles' mainloops instead of ending the grid.
+  // 1: the split tiles are the raster's first tiles and their parts run first (unit
+  // u < num_units - dp_units is split part u, whole tile w the unit after them), so their
+  // partial-sum exchange overlaps the whole tiles' mainloops instead of ending the grid.
   int tail_first;
   // conv BatchNorm epilogues (inference form): per output channel f, with acc rounded to
   // the input dtype first, y = (acc - mean[f]) * rsqrt(var[f] + bn_eps) * gamma[f] + beta[f], var clamped at 0
@@ -316,12 +316,21 @@ struct Unit {
 __device__ __forceinline__ Unit unit_of(const KParams& p, int u) {
   Unit r;
   int tile;
+  int whole0 = 0, split0 = p.dp_units;  // first tile of the whole / split tiles
   if (p.tail_first) {
+    // split tiles are the raster's first tiles and their parts the first units, so the
+    // schedule walks the raster from its start (L2 reuse as without a split)
     const int parts = p.num_units - p.dp_units;
-    u = u < parts ? p.dp_units + u : u - parts;
+    if (u < parts) {
+      u += p.dp_units;
+      split0 = 0;
+    } else {
+      u -= parts;
+      whole0 = parts / p.split;
+    }
   }
   if (u < p.dp_units) {
-    tile = u;
+    tile = whole0 + u;
     r.kb0 = 0;
     r.kb1 = p.k_blocks;
     r.st = -1;
@@ -330,7 +339,7 @@ __device__ __forceinline__ Unit unit_of(const KParams& p, int u) {
     const int v = u - p.dp_units;
     r.st = v / p.split;
     r.part = v - r.st * p.split;
-    tile = p.dp_units + r.st;
+    tile = split0 + r.st;
     if (p.csplit > 1) {
       // cluster split: the tile's stages (kps k-blocks each) spread evenly over the
       // parts, so no part is empty while parts <= stages
