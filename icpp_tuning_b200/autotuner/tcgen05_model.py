@@ -71,6 +71,11 @@ CONSTANTS = {
     # factor when only one pixel slot fits (its reload is then not overlapped)
     "direct_rate_kps": {1: 0.875, 2: 0.87, 3: 0.82},
     "direct_one_slot": 0.7,
+    # residual read of the conv + BN + add + ReLU epilogue, per SM, added to each tile's
+    # time (measured against the same kernels without it: the im2col kernel's lane-per-row
+    # loads ~17 GB/s, the direct conv's pixel-per-lane loads and transpose ~11 GB/s)
+    "residual_bytes_per_s_sm": 17e9,
+    "direct_residual_bytes_per_s_sm": 11e9,
     "mma_issue_cycles": 130,  # one thread issuing back-to-back MMAs with a wait per stage
     "fixed_s": 6.0e-6,  # launch + TMEM alloc + pipeline fill + last epilogue
     "pair_fixed_s": 1.0e-6,  # extra fixed cost of a CTA-pair launch (cluster start and exit)
@@ -234,6 +239,13 @@ def direct_plan(geo, block_n: int, sms: int, kps: int, stages: int):
     return None
 
 
+def _residual_s(op: OpSpec, outputs: int, rate: float) -> float:
+    """Time one tile spends reading its residual (a `residual_add` epilogue primitive)."""
+    if not any(p.name == "residual_add" for p in op.epilogue):
+        return 0.0
+    return outputs * op.mainloop.output_element_bytes / rate
+
+
 def _model_direct(op: OpSpec, c: TuneConfig, hw: GPUSpec) -> dict:
     """Direct conv (swap_ab 2): tiles of rpt padded rows x 128 channels, each input row
     loaded once per channel block and every filter tap a shifted view of it, so the
@@ -261,7 +273,7 @@ def _model_direct(op: OpSpec, c: TuneConfig, hw: GPUSpec) -> dict:
     n_mma = cin // 16 * kh * kw
     t_tile_mma = n_mma * max(bn / 2.0 / e_kps, K["mma_issue_cycles"]) / clk
     t_epi = 128 * bn * ml.output_element_bytes / K["epi_bytes_per_s_sm"]
-    t_tile = max(t_tile_mma, t_epi)
+    t_tile = max(t_tile_mma, t_epi) + _residual_s(op, min(128, oc) * bn, K["direct_residual_bytes_per_s_sm"])
     t_comp = waves * t_tile + t_epi + K["fixed_s"]
     traffic = (ml.input_elements * ml.input_element_bytes + ml.weight_elements * ml.weight_element_bytes
                + ml.output_elements * ml.output_element_bytes)
@@ -327,7 +339,7 @@ def _model(op: OpSpec, c: TuneConfig, hw: GPUSpec) -> dict:
     # -- epilogue: overlapped with the next tile's mainloop through two accumulators
     t_epi = bm * bn * ml.output_element_bytes / K["epi_bytes_per_s_sm"]
     e_epi = t_tile_mma / max(t_tile_mma, t_epi)
-    t_tile = max(t_tile_mma, t_epi)
+    t_tile = max(t_tile_mma, t_epi) + _residual_s(op, min(bm, rows) * min(bn, cols), K["residual_bytes_per_s_sm"])
     # -- LayerNorm: one normalisation pass (read + write) per 128-row block
     t_ln = 0.0
     if op.has_reduction_epilogue:

@@ -9,6 +9,7 @@ from __future__ import annotations
 
 import torch
 
+from ..autotuner.cost_model import FusionPrimitive
 from .conv2d import Conv2dDescriptor, calc_oh_ow
 from .conv2d_bn import bn_reference, build_bn_kernel
 
@@ -26,8 +27,13 @@ def get_ref_program(stride=1, padding=1, dilation=1, eps=EPS):
     return ref_program
 
 
+# The residual tile read next to the accumulator (2 bytes per output); the B200 cost
+# model charges its load time to each tile.
+RESIDUAL_ADD = FusionPrimitive("residual_add", 1.0, 2.0)
+
+
 class ConvBnAddReluDescriptor(Conv2dDescriptor):
-    primitives = ("batchnorm", "relu")
+    primitives = ("batchnorm", RESIDUAL_ADD, "relu")
 
     @property
     def name(self) -> str:

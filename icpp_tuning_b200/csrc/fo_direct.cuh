@@ -281,11 +281,6 @@ __global__ void __launch_bounds__(kDirectThreads, 1)
     bool ok = true;
     for (int u = cid; u < p.num_units; u += ncl) {
       const int tm = u % p.tiles_m, tn = u / p.tiles_m;
-      if (!mbar_wait(bar_tfull + 8 * acc, acc_ph, tmo, abort_flag)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
       const int f0 = tm * 128 + quarter * 32;
       const int f = f0 + lane;
       const float2 aff = channel_affine(p, f);
@@ -295,6 +290,42 @@ __global__ void __launch_bounds__(kDirectThreads, 1)
       // the tile's BN / 32 chunks: the first half of the warps takes chunks 0-3, the second
       // half the rest (none when BN <= 128: those warps only release the accumulator)
       const int mine = min(4, max(0, BN / 32 - half * 4));
+      // Residual of chunk c (32 positions of one padded row): lane = pixel ow0 + lane, its
+      // 32 channels as 4 x 16 B; zeros for padding positions and absent channels.  It does
+      // not depend on the accumulator, so the first chunk's is loaded before the wait and
+      // each next chunk's while the current one is processed.
+      auto load_res = [&](int c, uint4 (&q)[4]) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) q[j] = make_uint4(0u, 0u, 0u, 0u);
+        if constexpr (OUT_DT != DT_F32) {
+          const int pos0 = c * 32;
+          const int rr = pos0 / p.P;
+          const int oh = oh0 + rr;
+          const int ow = pos0 - rr * p.P + lane;
+          if (!has_add || oh >= p.OH || ow >= p.OW) return;
+          const unsigned short* src = reinterpret_cast<const unsigned short*>(p.add_src) +
+                                      ((static_cast<long long>(n) * p.OH + oh) * p.OW + ow) * p.ld_add + f0;
+          if (f0 + 32 <= p.N) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) q[j] = __ldg(reinterpret_cast<const uint4*>(src) + j);
+          } else {  // partial channel group
+            unsigned short tmp[32];
+#pragma unroll
+            for (int e = 0; e < 32; ++e) tmp[e] = f0 + e < p.N ? src[e] : static_cast<unsigned short>(0);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              q[j] = make_uint4(tmp[8 * j] | (tmp[8 * j + 1] << 16), tmp[8 * j + 2] | (tmp[8 * j + 3] << 16),
+                                tmp[8 * j + 4] | (tmp[8 * j + 5] << 16), tmp[8 * j + 6] | (tmp[8 * j + 7] << 16));
+          }
+        }
+      };
+      uint4 qn[4] = {};
+      if (has_add && mine > 0) load_res(half * 4, qn);
+      if (!mbar_wait(bar_tfull + 8 * acc, acc_ph, tmo, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
       if (mine == 0) {
         tc_fence_before();
         __syncwarp();
@@ -303,6 +334,10 @@ __global__ void __launch_bounds__(kDirectThreads, 1)
 #pragma unroll 1
       for (int ci = 0; ci < mine; ++ci) {
         const int c = half * 4 + ci;
+        uint4 q[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) q[j] = qn[j];
+        if (has_add && ci + 1 < mine) load_res(c + 1, qn);
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem_base + lane_off + acc * kDirectMaxBN + c * 32, r);
         tc_wait_ld_regs(r);
@@ -333,27 +368,8 @@ __global__ void __launch_bounds__(kDirectThreads, 1)
         }
         if constexpr (OUT_DT != DT_F32) {
           if (has_add) {
-            // residual: lane = pixel ow0 + lane, 32 channels (4 x 16 B); transposed
-            // through the staging block it will be stored from
-            const int ow = ow0 + lane;
-            uint4 q[4] = {};
-            if (ow < p.OW && f0 + 32 <= p.N) {
-              const uint4* src = reinterpret_cast<const uint4*>(
-                  reinterpret_cast<const unsigned short*>(p.add_src) +
-                  ((static_cast<long long>(n) * p.OH + oh) * p.OW + ow) * p.ld_add + f0);
-#pragma unroll
-              for (int j = 0; j < 4; ++j) q[j] = __ldg(src + j);
-            } else if (ow < p.OW) {  // partial channel group
-              const unsigned short* src = reinterpret_cast<const unsigned short*>(p.add_src) +
-                                          ((static_cast<long long>(n) * p.OH + oh) * p.OW + ow) * p.ld_add + f0;
-              unsigned short tmp[32];
-#pragma unroll
-              for (int e = 0; e < 32; ++e) tmp[e] = f0 + e < p.N ? src[e] : static_cast<unsigned short>(0);
-#pragma unroll
-              for (int j = 0; j < 4; ++j)
-                q[j] = make_uint4(tmp[8 * j] | (tmp[8 * j + 1] << 16), tmp[8 * j + 2] | (tmp[8 * j + 3] << 16),
-                                  tmp[8 * j + 4] | (tmp[8 * j + 5] << 16), tmp[8 * j + 6] | (tmp[8 * j + 7] << 16));
-            }
+            // residual (loaded ahead, q): transposed through the staging block it will be
+            // stored from
 #pragma unroll
             for (int j = 0; j < 4; ++j)
               asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(buf + lane * kRowB + j * 16), "r"(q[j].x),
